@@ -1,0 +1,283 @@
+"""ctypes binding of libghostweight_b200.so (the sm_100a C ABI).
+
+Every function here takes torch CUDA tensors, passes raw device pointers,
+sizes and torch's current stream to the C ABI declared in
+``include/ghostweight_b200.h`` and turns a non-zero status into an exception.
+There is no fallback: if the library is missing or the GPU is not an sm_100
+part, calls raise.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_NAME = "libghostweight_b200.so"
+LIB_PATH = Path(__file__).resolve().with_name(LIB_NAME)
+
+# gw_dtype / gw_epilogue / gw_status values (include/ghostweight_b200.h).
+DTYPE_CODES = {torch.float16: 0, torch.bfloat16: 1, torch.float32: 2}
+EPILOGUES = {None: 0, "none": 0, "gelu": 1, "gelu_erf": 1, "gelu_tanh": 2}
+GW_OK = 0
+GW_ERR_SHAPE = 1
+GW_ERR_DTYPE = 2
+GW_ERR_ALIGN = 3
+GW_ERR_NULL = 4
+GW_ERR_WORKSPACE = 5
+GW_ERR_CUDA = 6
+GW_ERR_DEVICE = 7
+GW_ERR_UNSUPPORTED = 8
+DEVICE_ERR_WAIT_TIMEOUT = 1
+DEVICE_ERR_BAD_INDEX = 2
+
+# Exported symbols and their ctypes signatures.
+_vp, _i, _i64, _sz, _d = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t, ctypes.c_double
+SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "gw_status_string": (ctypes.c_char_p, [_i]),
+    "gw_last_cuda_error": (ctypes.c_char_p, []),
+    "gw_version": (ctypes.c_char_p, []),
+    "gw_device_supported": (_i, [_i]),
+    "gw_get_device_error": (_i, [_i, ctypes.POINTER(ctypes.c_uint)]),
+    "gw_mask_workspace_bytes": (_sz, [_i64]),
+    "gw_mask_compact": (_i, [_vp, _i, _i64, _i64, _i64, _d, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "gw_gather_columns": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _vp]),
+    "gw_gather_rows": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _vp]),
+    "gw_gather_rows_t": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _vp]),
+    "gw_gather_gemm": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _i,
+                            _vp, _i64, _vp]),
+    "gw_packed_gemm": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i, _vp, _i64, _vp]),
+    "gw_validate_indices": (_i, [_vp, _i64, _i64, _vp, _vp]),
+}
+
+_lib: ctypes.CDLL | None = None
+_lib_lock = threading.Lock()
+
+
+class GhostweightError(RuntimeError):
+    """A C-ABI call of libghostweight_b200.so returned a non-zero status."""
+
+    def __init__(self, status: int, what: str, detail: str = ""):
+        self.status = status
+        msg = f"{what}: {status_string(status)} (status {status})"
+        if detail:
+            msg += f" [{detail}]"
+        super().__init__(msg)
+
+
+def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
+    """Load (once) and return the native library; raises if it is absent."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    with _lib_lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = Path(path) if path is not None else LIB_PATH
+        if not p.exists():
+            raise RuntimeError(
+                f"{p.name} is not built: run `python -m ghostweight_triton_b200.csrc.build` "
+                "(nvcc for sm_100a); there is no non-native fallback"
+            )
+        lib = ctypes.CDLL(str(p))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def status_string(status: int) -> str:
+    try:
+        return load().gw_status_string(int(status)).decode()
+    except Exception:  # library itself unavailable
+        return "unknown"
+
+
+def _check(status: int, what: str) -> None:
+    if status != GW_OK:
+        detail = load().gw_last_cuda_error().decode() if status == GW_ERR_CUDA else ""
+        raise GhostweightError(status, what, detail)
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return DTYPE_CODES[dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {dtype}; expected float16, bfloat16 or float32") from None
+
+
+def epilogue_code(activation: str | None) -> int:
+    try:
+        return EPILOGUES[activation]
+    except KeyError:
+        raise ValueError(f"unsupported activation {activation!r}; expected None, 'gelu' or 'gelu_tanh'") from None
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _rowmajor(*ts: torch.Tensor) -> None:
+    """Matrices cross the ABI as (pointer, leading dimension): unit column stride required."""
+    for t in ts:
+        assert t.ndim == 2 and (t.stride(1) == 1 or t.shape[1] <= 1), (
+            f"expected a row-major matrix, got shape {tuple(t.shape)} strides {t.stride()}")
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+class _on_device:
+    """Make `device` current for the duration of a C call (cheap when already current)."""
+
+    __slots__ = ("idx", "prev")
+
+    def __init__(self, device: torch.device):
+        self.idx = device.index if device.index is not None else torch.cuda.current_device()
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if cur != self.idx:
+            self.prev = cur
+            torch.cuda.set_device(self.idx)
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+
+
+# ---------------------------------------------------------------------------
+# Mask workspace: zero-initialised once, returned to zero by every call.
+# One buffer per (device, stream) so concurrent streams never share one.
+# ---------------------------------------------------------------------------
+_ws_cache: dict[tuple[int, int], torch.Tensor] = {}
+_ws_lock = threading.Lock()
+
+
+def mask_workspace(device: torch.device, cols: int) -> torch.Tensor:
+    need = int(load().gw_mask_workspace_bytes(int(cols)))
+    key = (device.index if device.index is not None else torch.cuda.current_device(), _stream(device))
+    with _ws_lock:
+        ws = _ws_cache.get(key)
+        if ws is None or ws.numel() < need:
+            ws = torch.zeros(max(need, 4096), dtype=torch.uint8, device=device)
+            _ws_cache[key] = ws
+    return ws
+
+
+# ---------------------------------------------------------------------------
+# Thin wrappers (tensors in, tensors out; no allocation except where noted)
+# ---------------------------------------------------------------------------
+def mask_compact(x: torch.Tensor, threshold: float, mask: torch.Tensor | None = None,
+                 alive_idx: torch.Tensor | None = None, count: torch.Tensor | None = None) -> None:
+    """K1 over a row-major [rows, cols] CUDA matrix (x.stride(1) == 1)."""
+    assert x.ndim == 2 and (x.stride(1) == 1 or x.shape[1] <= 1)
+    rows, cols = x.shape
+    ws = mask_workspace(x.device, cols)
+    with _on_device(x.device):
+        st = load().gw_mask_compact(
+            _ptr(x), dtype_code(x.dtype), rows, cols, max(x.stride(0), cols), float(threshold),
+            _ptr(mask), _ptr(alive_idx), _ptr(count), _ptr(ws), ws.numel(), _stream(x.device))
+    _check(st, "gw_mask_compact")
+
+
+def gather_columns(src: torch.Tensor, idx: torch.Tensor, dst: torch.Tensor, pad_to: int | None = None) -> None:
+    """dst[r, j] = src[r, idx[j]]; zero columns [len(idx), pad_to)."""
+    _rowmajor(src, dst)
+    assert idx.dtype == torch.int64
+    rows, cols = src.shape
+    n = idx.numel()
+    pad = n if pad_to is None else int(pad_to)
+    with _on_device(src.device):
+        st = load().gw_gather_columns(
+            _ptr(src), dtype_code(src.dtype), rows, cols, max(src.stride(0), cols), _ptr(idx), n,
+            _ptr(dst), max(dst.stride(0), pad), pad, _stream(src.device))
+    _check(st, "gw_gather_columns")
+
+
+def gather_rows(src: torch.Tensor, idx: torch.Tensor, dst: torch.Tensor) -> None:
+    """dst[j, :] = src[idx[j], :]."""
+    _rowmajor(src, dst)
+    assert idx.dtype == torch.int64
+    rows, cols = src.shape
+    n = idx.numel()
+    with _on_device(src.device):
+        st = load().gw_gather_rows(
+            _ptr(src), dtype_code(src.dtype), rows, cols, max(src.stride(0), cols), _ptr(idx), n,
+            _ptr(dst), max(dst.stride(0), cols), _stream(src.device))
+    _check(st, "gw_gather_rows")
+
+
+def gather_rows_t(src: torch.Tensor, idx: torch.Tensor, dst: torch.Tensor, pad_to: int | None = None) -> None:
+    """dst[n, j] = src[idx[j], n]; zero columns [len(idx), pad_to)."""
+    _rowmajor(src, dst)
+    assert idx.dtype == torch.int64
+    rows, cols = src.shape
+    n = idx.numel()
+    pad = n if pad_to is None else int(pad_to)
+    with _on_device(src.device):
+        st = load().gw_gather_rows_t(
+            _ptr(src), dtype_code(src.dtype), rows, cols, max(src.stride(0), cols), _ptr(idx), n,
+            _ptr(dst), max(dst.stride(0), pad), pad, _stream(src.device))
+    _check(st, "gw_gather_rows_t")
+
+
+def gather_gemm(x: torch.Tensor, w_packed: torch.Tensor, idx: torch.Tensor, y: torch.Tensor,
+                bias: torch.Tensor | None = None, activation: str | None = None) -> None:
+    """y = act(x[:, idx] @ w_packed[:, :len(idx)]^T + bias) on the current stream."""
+    _rowmajor(x, w_packed, y)
+    assert idx.dtype == torch.int64 and idx.is_contiguous()
+    M, K = x.shape
+    N = w_packed.shape[0]
+    n = idx.numel()
+    with _on_device(x.device):
+        st = load().gw_gather_gemm(
+            _ptr(x), dtype_code(x.dtype), M, K, max(x.stride(0), K), _ptr(w_packed), N,
+            max(w_packed.stride(0), n), _ptr(idx), n, _ptr(bias), epilogue_code(activation),
+            _ptr(y), max(y.stride(0), N), _stream(x.device))
+    _check(st, "gw_gather_gemm")
+
+
+def packed_gemm(a: torch.Tensor, w_packed: torch.Tensor, y: torch.Tensor,
+                bias: torch.Tensor | None = None, activation: str | None = None) -> None:
+    """y = act(a @ w_packed[:, :K]^T + bias) with both operands loaded by TMA."""
+    _rowmajor(a, w_packed, y)
+    M, K = a.shape
+    N = w_packed.shape[0]
+    with _on_device(a.device):
+        st = load().gw_packed_gemm(
+            _ptr(a), dtype_code(a.dtype), M, K, max(a.stride(0), K), _ptr(w_packed), N,
+            max(w_packed.stride(0), K), _ptr(bias), epilogue_code(activation), _ptr(y),
+            max(y.stride(0), N), _stream(a.device))
+    _check(st, "gw_packed_gemm")
+
+
+def validate_indices(idx: torch.Tensor, K: int) -> int:
+    """Number of entries of idx outside [0, K) (synchronises)."""
+    bad = torch.empty(1, dtype=torch.int32, device=idx.device)
+    with _on_device(idx.device):
+        st = load().gw_validate_indices(_ptr(idx), idx.numel(), int(K), _ptr(bad), _stream(idx.device))
+    _check(st, "gw_validate_indices")
+    return int(bad.item())
+
+
+def device_error(reset: bool = True, device: torch.device | None = None) -> int:
+    """Device error word bits (DEVICE_ERR_*) of `device` (synchronises)."""
+    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    out = ctypes.c_uint(0)
+    with _on_device(dev):
+        st = load().gw_get_device_error(1 if reset else 0, ctypes.byref(out))
+    _check(st, "gw_get_device_error")
+    return int(out.value)
+
+
+def device_supported(device: int = 0) -> bool:
+    return bool(load().gw_device_supported(int(device)))

@@ -1,0 +1,295 @@
+// C-ABI layer: argument validation, per-device set-up and kernel dispatch.
+// Declarations (with the reference interface each entry point replaces) are in
+// include/ghostweight_b200.h.
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "gw_common.cuh"
+#include "gw_internal.h"
+
+// Module-wide device error word (GW_DEVICE_ERR_* bits). Kernels receive its
+// device address, fetched once per device with cudaGetSymbolAddress.
+__device__ unsigned int g_gw_device_error = 0;
+
+namespace gw {
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_mu;
+DeviceInfo g_info[kMaxDevices];
+bool g_ready[kMaxDevices] = {};
+}  // namespace
+
+thread_local char g_cuda_msg[256] = "no error";
+
+const DeviceInfo* device_info(int device) {
+  if (device < 0 || device >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (g_ready[device]) return &g_info[device];
+  DeviceInfo d;
+  if (cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
+    return nullptr;
+  if (cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess)
+    return nullptr;
+  if (cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, device) != cudaSuccess)
+    return nullptr;
+  if (d.cc_major == 10) {
+    void* p = nullptr;
+    // `device` is the current device here (callers pass cudaGetDevice()).
+    if (cudaGetSymbolAddress(&p, g_gw_device_error) != cudaSuccess) return nullptr;
+    d.err_word = static_cast<unsigned int*>(p);
+  }
+  g_info[device] = d;
+  g_ready[device] = true;
+  return &g_info[device];
+}
+
+void* tensor_map_encoder() {
+  static void* fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = f;
+  });
+  return fn;
+}
+
+}  // namespace gw
+
+namespace {
+
+int cuda_fail(cudaError_t e) {
+  std::snprintf(gw::g_cuda_msg, sizeof(gw::g_cuda_msg), "%s: %s", cudaGetErrorName(e),
+                cudaGetErrorString(e));
+  return GW_ERR_CUDA;
+}
+
+// Current device info; fails with GW_ERR_DEVICE off sm_100.
+int current_device(const gw::DeviceInfo** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e);
+  const gw::DeviceInfo* d = gw::device_info(dev);
+  if (!d) return cuda_fail(cudaGetLastError());
+  if (d->cc_major != 10 || !d->err_word) return GW_ERR_DEVICE;
+  *out = d;
+  return GW_OK;
+}
+
+bool valid_dtype(int dt) { return dt == GW_DTYPE_F16 || dt == GW_DTYPE_BF16 || dt == GW_DTYPE_F32; }
+bool valid_epi(int e) { return e == GW_EPI_NONE || e == GW_EPI_GELU_ERF || e == GW_EPI_GELU_TANH; }
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+// A [rows, cols] matrix with leading dimension ld is well-formed.
+bool matrix_ok(int64_t rows, int64_t cols, int64_t ld) {
+  return rows >= 0 && cols >= 0 && ld >= 0 && (rows <= 1 || ld >= cols);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* gw_status_string(int status) {
+  switch (status) {
+    case GW_OK: return "ok";
+    case GW_ERR_SHAPE: return "invalid shape or leading dimension";
+    case GW_ERR_DTYPE: return "unsupported dtype";
+    case GW_ERR_ALIGN: return "pointer or leading dimension not aligned as required";
+    case GW_ERR_NULL: return "required pointer is NULL";
+    case GW_ERR_WORKSPACE: return "workspace missing or too small";
+    case GW_ERR_CUDA: return "CUDA error";
+    case GW_ERR_DEVICE: return "current device is not an sm_100 (B200) GPU";
+    case GW_ERR_UNSUPPORTED: return "unsupported configuration";
+    default: return "unknown status";
+  }
+}
+
+const char* gw_last_cuda_error(void) { return gw::g_cuda_msg; }
+
+const char* gw_version(void) { return "0.1.0"; }
+
+int gw_device_supported(int device) {
+  int major = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return major == 10 ? 1 : 0;
+}
+
+int gw_get_device_error(int reset, unsigned int* out) {
+  if (!out) return GW_ERR_NULL;
+  const gw::DeviceInfo* d = nullptr;
+  int st = current_device(&d);
+  if (st != GW_OK) return st;
+  cudaError_t e = cudaMemcpyFromSymbol(out, g_gw_device_error, sizeof(unsigned int));
+  if (e != cudaSuccess) return cuda_fail(e);
+  if (reset) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(g_gw_device_error, &zero, sizeof(unsigned int));
+    if (e != cudaSuccess) return cuda_fail(e);
+  }
+  return GW_OK;
+}
+
+size_t gw_mask_workspace_bytes(int64_t cols) {
+  return gw::mask_workspace_bytes(cols < 0 ? 0 : cols);
+}
+
+int gw_mask_compact(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld,
+                    double threshold, int32_t* mask, int64_t* alive_idx, int32_t* alive_count,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  if (!valid_dtype(dtype)) return GW_ERR_DTYPE;
+  if (!matrix_ok(rows, cols, ld) || cols > 0x7FFFFFFFll) return GW_ERR_SHAPE;
+  const gw::DeviceInfo* d = nullptr;
+  int st = current_device(&d);
+  if (st != GW_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cols == 0) {
+    if (alive_count) {
+      cudaError_t e = cudaMemsetAsync(alive_count, 0, sizeof(int32_t), s);
+      if (e != cudaSuccess) return cuda_fail(e);
+    }
+    return GW_OK;
+  }
+  if (rows > 0 && !x) return GW_ERR_NULL;
+  if (!workspace) return GW_ERR_NULL;
+  if (workspace_bytes < gw::mask_workspace_bytes(cols)) return GW_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return GW_ERR_ALIGN;
+  // The reference passes the threshold as an fp32 kernel scalar (mask.py:100).
+  const float thr = static_cast<float>(threshold);
+  cudaError_t e = gw::launch_mask_compact(x, dtype, rows, cols, ld, thr, mask, alive_idx,
+                                          alive_count, workspace, d->sm_count, s);
+  return e == cudaSuccess ? GW_OK : cuda_fail(e);
+}
+
+int gw_gather_columns(const void* src, int dtype, int64_t rows, int64_t cols, int64_t ld_src,
+                      const int64_t* idx, int64_t n_idx, void* dst, int64_t ld_dst,
+                      int64_t pad_to, void* stream) {
+  if (!valid_dtype(dtype)) return GW_ERR_DTYPE;
+  if (!matrix_ok(rows, cols, ld_src) || n_idx < 0 || pad_to < n_idx ||
+      !matrix_ok(rows, pad_to, ld_dst))
+    return GW_ERR_SHAPE;
+  const gw::DeviceInfo* d = nullptr;
+  int st = current_device(&d);
+  if (st != GW_OK) return st;
+  if (rows == 0 || pad_to == 0) return GW_OK;
+  if (!dst || (n_idx > 0 && (!src || !idx))) return GW_ERR_NULL;
+  cudaError_t e = gw::launch_gather_columns(src, dtype, rows, ld_src, cols, idx, n_idx, dst,
+                                            ld_dst, pad_to, d->err_word, d->sm_count,
+                                            static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? GW_OK : cuda_fail(e);
+}
+
+int gw_gather_rows(const void* src, int dtype, int64_t rows, int64_t cols, int64_t ld_src,
+                   const int64_t* idx, int64_t n_idx, void* dst, int64_t ld_dst, void* stream) {
+  if (!valid_dtype(dtype)) return GW_ERR_DTYPE;
+  if (!matrix_ok(rows, cols, ld_src) || n_idx < 0 || !matrix_ok(n_idx, cols, ld_dst))
+    return GW_ERR_SHAPE;
+  const gw::DeviceInfo* d = nullptr;
+  int st = current_device(&d);
+  if (st != GW_OK) return st;
+  if (n_idx == 0 || cols == 0) return GW_OK;
+  if (!src || !idx || !dst) return GW_ERR_NULL;
+  cudaError_t e = gw::launch_gather_rows(src, dtype, rows, cols, ld_src, idx, n_idx, dst, ld_dst,
+                                         d->err_word, d->sm_count,
+                                         static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? GW_OK : cuda_fail(e);
+}
+
+int gw_gather_rows_t(const void* src, int dtype, int64_t rows, int64_t cols, int64_t ld_src,
+                     const int64_t* idx, int64_t n_idx, void* dst, int64_t ld_dst,
+                     int64_t pad_to, void* stream) {
+  if (!valid_dtype(dtype)) return GW_ERR_DTYPE;
+  if (!matrix_ok(rows, cols, ld_src) || n_idx < 0 || pad_to < n_idx ||
+      !matrix_ok(cols, pad_to, ld_dst))
+    return GW_ERR_SHAPE;
+  const gw::DeviceInfo* d = nullptr;
+  int st = current_device(&d);
+  if (st != GW_OK) return st;
+  if (cols == 0 || pad_to == 0) return GW_OK;
+  if (!dst || (n_idx > 0 && (!src || !idx))) return GW_ERR_NULL;
+  cudaError_t e = gw::launch_gather_rows_t(src, dtype, rows, cols, ld_src, idx, n_idx, dst,
+                                           ld_dst, pad_to, d->err_word,
+                                           static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? GW_OK : cuda_fail(e);
+}
+
+int gw_gather_gemm(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
+                   const void* w_packed, int64_t N, int64_t ldw, const int64_t* idx,
+                   int64_t n_alive, const void* bias, int epilogue, void* y, int64_t ldy,
+                   void* stream) {
+  if (!valid_dtype(dtype)) return GW_ERR_DTYPE;
+  if (!valid_epi(epilogue)) return GW_ERR_UNSUPPORTED;
+  if (!matrix_ok(M, K, ldx) || n_alive < 0 || !matrix_ok(N, n_alive, ldw) ||
+      !matrix_ok(M, N, ldy))
+    return GW_ERR_SHAPE;
+  const gw::DeviceInfo* d = nullptr;
+  int st = current_device(&d);
+  if (st != GW_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (M == 0 || N == 0) return GW_OK;
+  if (!y) return GW_ERR_NULL;
+  cudaError_t e;
+  if (n_alive == 0) {
+    e = gw::launch_fill_bias(y, dtype, M, N, ldy, bias, epilogue, s);
+    return e == cudaSuccess ? GW_OK : cuda_fail(e);
+  }
+  if (!x || !w_packed || !idx) return GW_ERR_NULL;
+  if (dtype == GW_DTYPE_F32) {
+    e = gw::launch_gemm_f32(static_cast<const float*>(x), M, K, ldx,
+                            static_cast<const float*>(w_packed), N, ldw, idx, n_alive,
+                            static_cast<const float*>(bias), epilogue, static_cast<float*>(y),
+                            ldy, d->err_word, s);
+  } else {
+    if (!aligned16(w_packed) || (ldw % 8) != 0) return GW_ERR_ALIGN;
+    if (n_alive > 0x7FFFFFFFll - 64) return GW_ERR_SHAPE;
+    e = gw::launch_gemm_tc(true, x, dtype, M, K, ldx, w_packed, N, ldw, idx, n_alive, bias,
+                           epilogue, y, ldy, d->err_word, d->sm_count, s);
+  }
+  return e == cudaSuccess ? GW_OK : cuda_fail(e);
+}
+
+int gw_packed_gemm(const void* a, int dtype, int64_t M, int64_t K, int64_t lda,
+                   const void* w_packed, int64_t N, int64_t ldw, const void* bias, int epilogue,
+                   void* y, int64_t ldy, void* stream) {
+  if (dtype != GW_DTYPE_F16 && dtype != GW_DTYPE_BF16) return GW_ERR_DTYPE;
+  if (!valid_epi(epilogue)) return GW_ERR_UNSUPPORTED;
+  if (!matrix_ok(M, K, lda) || !matrix_ok(N, K, ldw) || !matrix_ok(M, N, ldy))
+    return GW_ERR_SHAPE;
+  const gw::DeviceInfo* d = nullptr;
+  int st = current_device(&d);
+  if (st != GW_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (M == 0 || N == 0) return GW_OK;
+  if (!y) return GW_ERR_NULL;
+  cudaError_t e;
+  if (K == 0) {
+    e = gw::launch_fill_bias(y, dtype, M, N, ldy, bias, epilogue, s);
+    return e == cudaSuccess ? GW_OK : cuda_fail(e);
+  }
+  if (!a || !w_packed) return GW_ERR_NULL;
+  if (!aligned16(a) || !aligned16(w_packed) || (lda % 8) != 0 || (ldw % 8) != 0)
+    return GW_ERR_ALIGN;
+  e = gw::launch_gemm_tc(false, a, dtype, M, K, lda, w_packed, N, ldw, nullptr, K, bias,
+                         epilogue, y, ldy, d->err_word, d->sm_count, s);
+  return e == cudaSuccess ? GW_OK : cuda_fail(e);
+}
+
+int gw_validate_indices(const int64_t* idx, int64_t n, int64_t K, int32_t* bad_count,
+                        void* stream) {
+  if (n < 0 || K < 0) return GW_ERR_SHAPE;
+  if (!bad_count || (n > 0 && !idx)) return GW_ERR_NULL;
+  const gw::DeviceInfo* d = nullptr;
+  int st = current_device(&d);
+  if (st != GW_OK) return st;
+  cudaError_t e = gw::launch_validate_indices(idx, n, K, bad_count,
+                                              static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? GW_OK : cuda_fail(e);
+}
+
+}  // extern "C"

@@ -1,0 +1,239 @@
+// Shared device helpers for the ghostweight B200 kernels (sm_100a only).
+//
+// Everything here is hand-written inline PTX for the Blackwell async machinery:
+// mbarriers, TMA tile loads, and the tcgen05 (5th-gen tensor core + TMEM) ops.
+// Each wait on an mbarrier is bounded: after GW_WAIT_LIMIT_NS of wall time the
+// wait gives up, raises a bit in the module error word and tells the caller to
+// abandon its loop, so a logic error can never wedge the GPU.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+
+#include "../../include/ghostweight_b200.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "ghostweight_b200 kernels are written for sm_100a (B200) only"
+#endif
+
+namespace gw {
+
+// Wall-clock limit for any single mbarrier wait (2 s). A correct kernel never
+// comes close: the longest legitimate wait is one output tile's main loop.
+constexpr unsigned long long GW_WAIT_LIMIT_NS = 2000000000ull;
+
+// Bits of the module-wide device error word (read back by gw_get_device_error).
+enum : unsigned int {
+  GW_DERR_WAIT_TIMEOUT = 1u << 0,   // an mbarrier wait ran out of time
+  GW_DERR_BAD_INDEX    = 1u << 1,   // an alive index was outside [0, K)
+};
+
+// The error word lives in gw_api.cu; kernels in other translation units get
+// its device address as a parameter (no relocatable device code).
+__device__ __forceinline__ void raise_error(unsigned int* err, unsigned int bits) {
+  if (err) atomicOr(err, bits);
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long global_timer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ----------------------------------------------------------------------------
+// mbarrier
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+               :: "r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity. Returns false when the
+// CTA-wide abort flag is (or becomes) set, or the wall-clock limit is hit; in
+// the latter case the abort flag and the module error word are raised.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
+                                          volatile int* abort_flag,
+                                          unsigned int* err,
+                                          unsigned long long limit_ns = GW_WAIT_LIMIT_NS) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0u) {
+      if (abort_flag && *abort_flag) return false;
+      if (global_timer_ns() - t0 > limit_ns) {
+        if (abort_flag) *abort_flag = 1;
+        raise_error(err, GW_DERR_WAIT_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------
+// TMA (non-multicast tile loads only)
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
+  asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
+
+// 2-D tile load global -> shared, completion signalled on `bar` as tx bytes.
+// x is the innermost (contiguous) coordinate in elements; callers keep
+// x * sizeof(elem) a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int32_t x, int32_t y,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];"
+      :: "r"(dst), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ----------------------------------------------------------------------------
+// tcgen05 / TMEM
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+               :: "r"(dst_smem), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
+               :: "r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (fp16 or bf16 in, fp32 accumulate).
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive once on `bar` when every previously issued tcgen05 op of this thread completes.
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               :: "r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tc_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Each lane reads 32 consecutive 32-bit TMEM columns of its own lane (row).
+__device__ __forceinline__ void tc_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor for a K-major operand tile stored in the
+// 128-byte-swizzled canonical layout: rows of 128 B (64 16-bit elements),
+// 16-byte chunk c of row r stored at chunk position c ^ (r % 8), groups of 8
+// rows 1024 B apart. Tile base must be 1024-byte aligned.
+__device__ __forceinline__ uint64_t smem_desc_kmajor_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);      // start address
+  d |= static_cast<uint64_t>(1u) << 16;                     // leading byte offset (unused for SW128 K-major)
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;             // stride byte offset: 8 rows * 128 B
+  d |= static_cast<uint64_t>(1u) << 46;                     // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(2u) << 61;                     // layout: 128-byte swizzle
+  return d;
+}
+
+// Instruction descriptor, kind::f16, fp32 accumulate, A and B both K-major.
+// ab_format: 0 = fp16, 1 = bf16 (A and B always share one type).
+__host__ __device__ constexpr uint32_t idesc_f16(uint32_t ab_format, uint32_t m, uint32_t n) {
+  return (1u << 4)                 // D format: f32
+       | (ab_format << 7)          // A format
+       | (ab_format << 10)         // B format
+       | ((n >> 3) << 17)          // N / 8
+       | ((m >> 4) << 24);         // M / 16
+}
+
+// ----------------------------------------------------------------------------
+// Scalar conversions
+// ----------------------------------------------------------------------------
+template <int DT> struct Elem;
+template <> struct Elem<GW_DTYPE_F16> {
+  using raw = uint16_t;
+  static __device__ __forceinline__ float to_f(raw v) { return __half2float(__ushort_as_half(v)); }
+  static __device__ __forceinline__ raw from_f(float f) { return __half_as_ushort(__float2half_rn(f)); }
+};
+template <> struct Elem<GW_DTYPE_BF16> {
+  using raw = uint16_t;
+  static __device__ __forceinline__ float to_f(raw v) { return __uint_as_float(static_cast<uint32_t>(v) << 16); }
+  static __device__ __forceinline__ raw from_f(float f) { return __bfloat16_as_ushort(__float2bfloat16_rn(f)); }
+};
+template <> struct Elem<GW_DTYPE_F32> {
+  using raw = uint32_t;
+  static __device__ __forceinline__ float to_f(raw v) { return __uint_as_float(v); }
+  static __device__ __forceinline__ raw from_f(float f) { return __float_as_uint(f); }
+};
+
+// Output activation applied in GEMM epilogues, from the GELU definitions
+// (Hendrycks & Gimpel): exact erf form and the tanh approximation. erff / tanhf
+// are CUDA's own functions.
+__device__ __forceinline__ float apply_epilogue(float v, int epi) {
+  if (epi == GW_EPI_GELU_ERF) {
+    return 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
+  } else if (epi == GW_EPI_GELU_TANH) {
+    const float u = 0.79788456080286535588f * (v + 0.044715f * v * v * v);
+    return 0.5f * v * (1.0f + tanhf(u));
+  }
+  return v;
+}
+
+}  // namespace gw

@@ -1,0 +1,419 @@
+// K3: fused gather-GEMM on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+//   y[m, n] = act( sum_j x[m, idx[j]] * w[n, j] + bias[n] )      fp16 / bf16 in, fp32 accumulate
+//
+// This is the B200 replacement of ghostweight_triton/kernels/matmul.py:27-82
+// (which gathers A columns and W rows with pointer loads inside a 64x64x32
+// tl.dot loop) plus the bias add of module.py:116-117. Design:
+//
+//   * persistent kernel, one 448-thread CTA per SM, 128 x BN output tiles
+//     (BN = 256 or 128), K' consumed in 64-wide k-blocks (128 B of fp16/bf16,
+//     one 128-byte swizzle atom), 4-stage shared-memory ring;
+//   * warp 0      : TMA producer for the packed weight tile w[n0:n0+BN, k:k+64]
+//                   (and for A too when A is an already compacted matrix);
+//   * warp 1      : TMEM allocator and the single-thread tcgen05.mma issuer
+//                   (128 x BN x 16 per instruction, 4 per k-block), commits
+//                   free smem stages and publish finished accumulators;
+//   * warps 2..9  : gather producers -- two groups of four warps take
+//                   alternate k-blocks; a warp loads 32 rows x 64 alive columns
+//                   of x straight from global memory (lane <-> alive column, so
+//                   a request covers 32 consecutive alive indices of one row),
+//                   waits for the stage to be free, and writes the values into
+//                   the 128B-swizzled K-major layout tcgen05 reads;
+//   * warps 10..13: epilogue -- tcgen05.ld of the fp32 accumulator (one TMEM
+//                   lane per output row), bias, optional GELU, one rounding to
+//                   the output type, 16-byte stores;
+//   * the accumulator is double-buffered in TMEM (2 x BN columns), so the
+//     epilogue of tile t overlaps the main loop of tile t+1.
+// No TMA multicast is used anywhere (the kernel also runs in multi-GPU jobs).
+// Every mbarrier wait is bounded (gw_common.cuh); on a timeout all roles leave
+// their loops, in-flight TMA loads and MMAs are drained, TMEM is freed and the
+// device error word records the event.
+#include <algorithm>
+
+#include <cuda.h>
+
+#include "gw_common.cuh"
+#include "gw_internal.h"
+
+namespace gw {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kStages = 4;
+constexpr int kThreads = 448;
+constexpr int kWarpTma = 0;
+constexpr int kWarpMma = 1;
+constexpr int kWarpGather0 = 2;
+constexpr int kGatherWarps = 8;      // two groups of four
+constexpr int kWarpEpi0 = 10;        // four epilogue warps
+
+template <int BN>
+struct TcCfg {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kBarBytes = 256;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarBytes;
+};
+
+struct TcParams {
+  const uint16_t* x;
+  int64_t ldx;
+  int64_t M;
+  int64_t K;
+  const int64_t* idx;
+  int64_t n_alive;
+  int64_t N;
+  const uint16_t* bias;
+  int epi;
+  int y_vec_ok;
+  uint16_t* y;
+  int64_t ldy;
+  int num_kb;
+  int m_tiles;
+  int n_tiles;
+  int num_tiles;
+  unsigned int* err;
+};
+
+template <int BN, int DT, bool GATHER>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
+               const __grid_constant__ CUtensorMap tmap_a, const TcParams p) {
+  using C = TcCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment (of the shared-window address) for the swizzled tiles.
+  const uint32_t raw_s = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_s & 1023u)) & 1023u);
+  const uint32_t sbase = smem_u32(smem);
+
+  uint8_t* bar_region = smem + kStages * C::kStageBytes;
+  const uint32_t bar0 = smem_u32(bar_region);
+  // barriers: full_a[S] full_b[S] empty[S] tfull[2] tempty[2] drain
+  auto full_a = [&](int s) { return bar0 + 8u * s; };
+  auto full_b = [&](int s) { return bar0 + 8u * (kStages + s); };
+  auto empty = [&](int s) { return bar0 + 8u * (2 * kStages + s); };
+  auto tfull = [&](int b) { return bar0 + 8u * (3 * kStages + b); };
+  auto tempty = [&](int b) { return bar0 + 8u * (3 * kStages + 2 + b); };
+  const uint32_t drain_bar = bar0 + 8u * (3 * kStages + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_region + 192);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_region + 196);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full_a(s), kGatherWarps / 2);
+      mbar_init(full_b(s), 1);
+      mbar_init(empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull(b), 1);
+      mbar_init(tempty(b), 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    mbar_init_fence();
+  }
+  if (warp == kWarpTma && lane == 0) {
+    tma_prefetch_desc(&tmap_b);
+    if (!GATHER) tma_prefetch_desc(&tmap_a);
+  }
+  if (warp == kWarpMma) {
+    tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == kWarpTma) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        const int m_blk = tile % p.m_tiles;
+        const int n_blk = tile / p.m_tiles;
+        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1u;
+          if (!mbar_wait(empty(s), ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
+          const uint32_t a_s = sbase + s * C::kStageBytes;
+          const uint32_t b_s = a_s + C::kABytes;
+          if (GATHER) {
+            mbar_arrive_expect_tx(full_b(s), C::kBBytes);
+            tma_load_2d(b_s, &tmap_b, kb * kBK, n_blk * BN, full_b(s));
+          } else {
+            mbar_arrive_expect_tx(full_b(s), C::kBBytes + C::kABytes);
+            tma_load_2d(b_s, &tmap_b, kb * kBK, n_blk * BN, full_b(s));
+            tma_load_2d(a_s, &tmap_a, kb * kBK, m_blk * kBM, full_b(s));
+          }
+        }
+      }
+      if (!ok) {
+        // Drain loads still in flight before the CTA exits (bounded, 100 ms).
+        const uint32_t first = it > static_cast<uint32_t>(kStages) ? it - kStages : 0u;
+        for (uint32_t i = first; i < it; ++i)
+          mbar_wait(full_b(i % kStages), (i / kStages) & 1u, nullptr, p.err, 100000000ull);
+      }
+    }
+  } else if (warp == kWarpMma) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(DT == GW_DTYPE_BF16 ? 1u : 0u, kBM, BN);
+      uint32_t it = 0, lt = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++lt) {
+        const uint32_t b = lt & 1u;
+        const uint32_t aph = (lt >> 1) & 1u;
+        if (!mbar_wait(tempty(b), aph ^ 1u, abort_flag, p.err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + b * BN;
+        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1u;
+          if (!mbar_wait(full_b(s), ph, abort_flag, p.err)) { ok = false; break; }
+          if (GATHER && !mbar_wait(full_a(s), ph, abort_flag, p.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_s = sbase + s * C::kStageBytes;
+          const uint64_t a_desc = smem_desc_kmajor_sw128(a_s);
+          const uint64_t b_desc = smem_desc_kmajor_sw128(a_s + C::kABytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            // +32 bytes per 16-element k step inside the swizzle atom (>> 4 in the descriptor).
+            tc_mma_f16(d_tmem, a_desc + 2u * k, b_desc + 2u * k, idesc,
+                       (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(empty(s));
+        }
+        if (!ok) break;
+        tc_commit(tfull(b));
+      }
+      // All MMAs of this thread complete before TMEM can be released.
+      tc_commit(drain_bar);
+      mbar_wait(drain_bar, 0u, nullptr, p.err, 100000000ull);
+    }
+    __syncwarp();
+  } else if (warp < kWarpEpi0) {
+    // ------------------------------------------------------------ gather producers
+    if (GATHER) {
+      const int gw_idx = warp - kWarpGather0;
+      const uint32_t grp = static_cast<uint32_t>(gw_idx >> 2);
+      const int wrow = (gw_idx & 3) * 32;
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        const int m_blk = tile % p.m_tiles;
+        const int64_t row0 = static_cast<int64_t>(m_blk) * kBM + wrow;
+        const int64_t rem = p.M - row0;
+        const int rows_here = rem <= 0 ? 0 : (rem >= 32 ? 32 : static_cast<int>(rem));
+        const uint16_t* xw = p.x + (rows_here > 0 ? row0 * p.ldx : 0);
+        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+          if ((it & 1u) != grp) continue;
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1u;
+          const int64_t k0 = static_cast<int64_t>(kb) * kBK + lane;
+          int64_t c0 = -1, c1 = -1;
+          bool bad = false;
+          if (k0 < p.n_alive) {
+            c0 = __ldg(p.idx + k0);
+            if (c0 < 0 || c0 >= p.K) { bad = true; c0 = -1; }
+          }
+          if (k0 + 32 < p.n_alive) {
+            c1 = __ldg(p.idx + k0 + 32);
+            if (c1 < 0 || c1 >= p.K) { bad = true; c1 = -1; }
+          }
+          if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) raise_error(p.err, GW_DERR_BAD_INDEX);
+          uint16_t v0[32], v1[32];
+#pragma unroll
+          for (int r = 0; r < 32; ++r) {
+            const bool rv = r < rows_here;
+            v0[r] = (rv && c0 >= 0) ? __ldg(xw + r * p.ldx + c0) : static_cast<uint16_t>(0);
+            v1[r] = (rv && c1 >= 0) ? __ldg(xw + r * p.ldx + c1) : static_cast<uint16_t>(0);
+          }
+          if (!mbar_wait(empty(s), ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
+          uint8_t* a_tile = smem + s * C::kStageBytes;
+          const int ch0 = lane >> 3;
+          const int byte_in_chunk = (lane & 7) << 1;
+#pragma unroll
+          for (int r = 0; r < 32; ++r) {
+            const int row = wrow + r;
+            const int sw = row & 7;
+            uint8_t* rowp = a_tile + row * 128 + byte_in_chunk;
+            *reinterpret_cast<uint16_t*>(rowp + ((ch0 ^ sw) << 4)) = v0[r];
+            *reinterpret_cast<uint16_t*>(rowp + (((ch0 + 4) ^ sw) << 4)) = v1[r];
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(full_a(s));
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;                       // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    uint32_t lt = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++lt) {
+      const int m_blk = tile % p.m_tiles;
+      const int n_blk = tile / p.m_tiles;
+      const uint32_t b = lt & 1u;
+      const uint32_t aph = (lt >> 1) & 1u;
+      if (!mbar_wait(tfull(b), aph, abort_flag, p.err)) break;
+      tc_fence_after();
+      const int64_t row = static_cast<int64_t>(m_blk) * kBM + row_in_tile;
+      const bool row_ok = row < p.M;
+      uint16_t* yrow = p.y + (row_ok ? row * p.ldy : 0);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t acc[32];
+        tc_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * BN + c * 32, acc);
+        tc_wait_ld();
+        const int64_t n_base = static_cast<int64_t>(n_blk) * BN + c * 32;
+        float f[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(acc[j]);
+        if (p.bias) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n_base + j < p.N) f[j] += Elem<DT>::to_f(__ldg(p.bias + n_base + j));
+        }
+        if (p.epi != GW_EPI_NONE) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[j] = apply_epilogue(f[j], p.epi);
+        }
+        if (row_ok) {
+          if (p.y_vec_ok && n_base + 32 <= p.N) {
+            uint32_t packed[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              packed[j] = static_cast<uint32_t>(Elem<DT>::from_f(f[2 * j])) |
+                          (static_cast<uint32_t>(Elem<DT>::from_f(f[2 * j + 1])) << 16);
+            uint4* dst = reinterpret_cast<uint4*>(yrow + n_base);
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n_base + j < p.N) yrow[n_base + j] = Elem<DT>::from_f(f[j]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty(b));
+    }
+  }
+
+  __syncthreads();
+  if (warp == kWarpMma) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// 2-D K-major tile map over a [rows, cols] 16-bit matrix with row stride ld,
+// box = box_cols x box_rows, 128-byte swizzle, zero fill outside the matrix.
+bool make_tmap_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
+                  int box_cols, int box_rows) {
+  auto encode = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
+  if (!encode) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2u};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims,
+                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN, int DT, bool GATHER>
+cudaError_t launch_tc(const CUtensorMap& tb, const CUtensorMap& ta, const TcParams& p,
+                      int sm_count, cudaStream_t stream) {
+  using C = TcCfg<BN>;
+  auto kern = gemm_tc_kernel<BN, DT, GATHER>;
+  // Opt in to the large dynamic shared-memory carve-out (idempotent, cheap).
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       C::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  const int grid = std::min(p.num_tiles, sm_count > 0 ? sm_count : 148);
+  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(tb, ta, p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_gemm_tc(bool a_gather, const void* x, int dtype, int64_t M, int64_t K,
+                           int64_t ldx, const void* w, int64_t N, int64_t ldw,
+                           const int64_t* idx, int64_t n_alive, const void* bias, int epilogue,
+                           void* y, int64_t ldy, unsigned int* err, int sm_count,
+                           cudaStream_t stream) {
+  // BN = 256 unless 128-wide tiles give noticeably more CTAs to spread over the SMs.
+  const int64_t m_tiles = (M + kBM - 1) / kBM;
+  const int64_t sms = sm_count > 0 ? sm_count : 148;
+  const int64_t t256 = m_tiles * ((N + 255) / 256);
+  const bool use128 = (N <= 128) || (t256 < sms && m_tiles * ((N + 127) / 128) > t256);
+  const int BN = use128 ? 128 : 256;
+  const int64_t n_tiles = (N + BN - 1) / BN;
+  const int64_t num_tiles = m_tiles * n_tiles;
+  if (num_tiles > 0x7FFFFFFFll || m_tiles > 0x7FFFFFFFll) return cudaErrorInvalidValue;
+
+  TcParams p{};
+  p.x = static_cast<const uint16_t*>(x);
+  p.ldx = ldx;
+  p.M = M;
+  p.K = K;
+  p.idx = idx;
+  p.n_alive = n_alive;
+  p.N = N;
+  p.bias = static_cast<const uint16_t*>(bias);
+  p.epi = epilogue;
+  p.y = static_cast<uint16_t*>(y);
+  p.ldy = ldy;
+  p.y_vec_ok = ((reinterpret_cast<uintptr_t>(y) & 15u) == 0 && (ldy % 8) == 0) ? 1 : 0;
+  p.num_kb = static_cast<int>((n_alive + kBK - 1) / kBK);
+  p.m_tiles = static_cast<int>(m_tiles);
+  p.n_tiles = static_cast<int>(n_tiles);
+  p.num_tiles = static_cast<int>(num_tiles);
+  p.err = err;
+
+  CUtensorMap tb, ta;
+  if (!make_tmap_2d(&tb, w, N, n_alive, ldw, kBK, BN)) return cudaErrorInvalidValue;
+  if (a_gather) {
+    ta = tb;   // unused by the gather variant
+  } else {
+    if (!make_tmap_2d(&ta, x, M, n_alive, ldx, kBK, kBM)) return cudaErrorInvalidValue;
+  }
+
+#define GW_TC_CASE(BNV, DTV)                                                      \
+  return a_gather ? launch_tc<BNV, DTV, true>(tb, ta, p, static_cast<int>(sms), stream) \
+                  : launch_tc<BNV, DTV, false>(tb, ta, p, static_cast<int>(sms), stream)
+  if (BN == 256) {
+    if (dtype == GW_DTYPE_BF16) { GW_TC_CASE(256, GW_DTYPE_BF16); }
+    GW_TC_CASE(256, GW_DTYPE_F16);
+  } else {
+    if (dtype == GW_DTYPE_BF16) { GW_TC_CASE(128, GW_DTYPE_BF16); }
+    GW_TC_CASE(128, GW_DTYPE_F16);
+  }
+#undef GW_TC_CASE
+}
+
+}  // namespace gw

@@ -1,0 +1,62 @@
+// Host-side launchers shared between the kernel translation units and the
+// C-ABI layer (gw_api.cu). Not part of the public ABI.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace gw {
+
+// Per-device facts cached by gw_api.cu.
+struct DeviceInfo {
+  int sm_count = 0;
+  int cc_major = 0;
+  int cc_minor = 0;
+  unsigned int* err_word = nullptr;   // device address of the module error word
+};
+const DeviceInfo* device_info(int device);   // nullptr on failure
+
+// gw_mask.cu
+size_t mask_workspace_bytes(int64_t cols);
+cudaError_t launch_mask_compact(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld,
+                                float thr, int32_t* mask, int64_t* idx, int32_t* count,
+                                void* workspace, int sm_count, cudaStream_t stream);
+
+// gw_gather.cu
+cudaError_t launch_gather_columns(const void* src, int dtype, int64_t rows, int64_t ld_src,
+                                  int64_t cols_src, const int64_t* idx, int64_t n_idx, void* dst,
+                                  int64_t ld_dst, int64_t pad_to, unsigned int* err,
+                                  int sm_count, cudaStream_t stream);
+cudaError_t launch_gather_rows(const void* src, int dtype, int64_t rows_src, int64_t cols,
+                               int64_t ld_src, const int64_t* idx, int64_t n_idx, void* dst,
+                               int64_t ld_dst, unsigned int* err, int sm_count,
+                               cudaStream_t stream);
+cudaError_t launch_gather_rows_t(const void* src, int dtype, int64_t rows_src, int64_t cols,
+                                 int64_t ld_src, const int64_t* idx, int64_t n_idx, void* dst,
+                                 int64_t ld_dst, int64_t pad_to, unsigned int* err,
+                                 cudaStream_t stream);
+cudaError_t launch_fill_bias(void* y, int dtype, int64_t M, int64_t N, int64_t ldy,
+                             const void* bias, int epilogue, cudaStream_t stream);
+cudaError_t launch_validate_indices(const int64_t* idx, int64_t n, int64_t K, int32_t* bad,
+                                    cudaStream_t stream);
+
+// gw_gemm_tc.cu: tcgen05 gather-GEMM / packed GEMM (fp16, bf16).
+// a_gather: true  -> A is gathered from x via idx (producer warps)
+//           false -> A is a dense [M, n_alive] matrix loaded by TMA (idx unused)
+cudaError_t launch_gemm_tc(bool a_gather, const void* x, int dtype, int64_t M, int64_t K,
+                           int64_t ldx, const void* w, int64_t N, int64_t ldw,
+                           const int64_t* idx, int64_t n_alive, const void* bias, int epilogue,
+                           void* y, int64_t ldy, unsigned int* err, int sm_count,
+                           cudaStream_t stream);
+
+// gw_gemm_simt.cu: exact-fp32 gather-GEMM.
+cudaError_t launch_gemm_f32(const float* x, int64_t M, int64_t K, int64_t ldx, const float* w,
+                            int64_t N, int64_t ldw, const int64_t* idx, int64_t n_alive,
+                            const float* bias, int epilogue, float* y, int64_t ldy,
+                            unsigned int* err, cudaStream_t stream);
+
+// Driver entry point for cuTensorMapEncodeTiled (resolved once, no libcuda link).
+void* tensor_map_encoder();
+
+}  // namespace gw

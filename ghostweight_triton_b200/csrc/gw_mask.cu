@@ -1,0 +1,274 @@
+// K1: dead-column mask fused with stream compaction (one launch).
+//
+// Semantics follow the reference Triton kernel ghostweight_triton/kernels/
+// mask.py:21-59 bit for bit: per column the running max starts at 0.0 (mask.py:46),
+// NaN entries never win the max (tl.maximum ignores NaN), values are compared in
+// fp32 after conversion (mask.py:53) and a column is alive iff max > fp32(threshold)
+// (mask.py:58). Since max starts at 0, that is exactly
+//     alive[k] = (0 > thr) || any_r( fp32(|x[r,k]|) > thr )
+// (a NaN compares false), which needs one bit per column instead of a float, so
+// the cross-CTA combine is an OR of 32-bit words.
+//
+// Layout/parallelism (HBM-bound, row-major [rows, cols] input):
+//   * a warp covers 32 consecutive 16-byte vectors of one row (512 contiguous
+//     bytes, fully coalesced); 8 warps of a CTA walk different rows; each CTA
+//     owns a 32-vector column strip and a contiguous chunk of rows;
+//   * 4 rows are loaded per iteration per thread (streaming, no L1 allocation);
+//   * a warp whose columns are all alive stops reading (warp-uniform exit);
+//   * per-CTA alive bits are OR-ed into a 32-bit word array in the workspace;
+//   * the last CTA to finish (ticket counter) performs the compaction: a
+//     block-wide prefix sum of popcounts emits mask[], the ascending alive
+//     index list (the torch.nonzero of module.py:104) and the count, and resets
+//     the workspace to zero for the next call.
+#include "gw_common.cuh"
+#include "gw_internal.h"
+
+namespace gw {
+
+namespace {
+
+constexpr int kMaskThreads = 256;
+constexpr int kMaskWarps = kMaskThreads / 32;
+constexpr int kMaskUnroll = 4;
+
+// Workspace: [0] ticket counter, [4..16) padding, then ceil(cols/32) flag words.
+constexpr size_t kFlagsOffset = 16;
+
+__device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+
+// Alive bits (bit e for element e) of one 16-byte vector.
+template <int DT>
+__device__ __forceinline__ uint32_t vec_bits(const uint4 v, float thr) {
+  uint32_t b = 0;
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  if constexpr (DT == GW_DTYPE_F32) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) b |= (fabsf(__uint_as_float(w[e])) > thr ? 1u : 0u) << e;
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float lo = Elem<DT>::to_f(static_cast<uint16_t>(w[e] & 0xFFFFu));
+      const float hi = Elem<DT>::to_f(static_cast<uint16_t>(w[e] >> 16));
+      b |= (fabsf(lo) > thr ? 1u : 0u) << (2 * e);
+      b |= (fabsf(hi) > thr ? 1u : 0u) << (2 * e + 1);
+    }
+  }
+  return b;
+}
+
+// VEC = true: each thread owns one 16-byte vector (8 x 16-bit or 4 x fp32
+// columns); requires 16-byte aligned base, ld and cols multiples of the vector.
+// VEC = false: each thread owns one column (scalar loads).
+template <int DT, bool VEC>
+__global__ void __launch_bounds__(kMaskThreads)
+mask_compact_kernel(const void* __restrict__ x, int64_t rows, int64_t cols, int64_t ld,
+                    float thr, int64_t rows_per_cta, uint32_t* __restrict__ ws,
+                    int32_t* __restrict__ mask, int64_t* __restrict__ idx,
+                    int32_t* __restrict__ count) {
+  using raw = typename Elem<DT>::raw;
+  constexpr int VPT = VEC ? static_cast<int>(16 / sizeof(raw)) : 1;   // columns per thread
+  constexpr uint32_t kFull = (VPT == 32) ? 0xFFFFFFFFu : ((1u << VPT) - 1u);
+
+  uint32_t* ticket = ws;
+  uint32_t* flags = ws + kFlagsOffset / sizeof(uint32_t);
+
+  __shared__ uint32_t s_bits[kMaskWarps][32];
+  __shared__ int s_last;
+  __shared__ int64_t s_scan[kMaskWarps];
+
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const bool all_alive = (0.0f > thr);   // max starts at 0: every column alive
+
+  const int64_t nvec = VEC ? cols / VPT : cols;
+  const int64_t v = static_cast<int64_t>(blockIdx.x) * 32 + lane;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.y) * rows_per_cta;
+  const int64_t r1 = min(rows, r0 + rows_per_cta);
+
+  uint32_t bits = 0;
+  const bool have = (v < nvec);
+  if (!all_alive) {
+    const raw* col = static_cast<const raw*>(x) + (have ? v * VPT : 0);
+    int64_t r = r0 + warp;
+    // Main loop: 4 independent rows in flight per thread.
+    for (; r + (kMaskUnroll - 1) * kMaskWarps < r1; r += kMaskUnroll * kMaskWarps) {
+      if (__all_sync(0xFFFFFFFFu, !have || bits == kFull)) break;
+      if (have) {
+        if constexpr (VEC) {
+          uint4 q[kMaskUnroll];
+#pragma unroll
+          for (int u = 0; u < kMaskUnroll; ++u) q[u] = ld_stream_v4(col + (r + u * kMaskWarps) * ld);
+#pragma unroll
+          for (int u = 0; u < kMaskUnroll; ++u) bits |= vec_bits<DT>(q[u], thr);
+        } else {
+          raw q[kMaskUnroll];
+#pragma unroll
+          for (int u = 0; u < kMaskUnroll; ++u) q[u] = __ldg(col + (r + u * kMaskWarps) * ld);
+#pragma unroll
+          for (int u = 0; u < kMaskUnroll; ++u) bits |= (fabsf(Elem<DT>::to_f(q[u])) > thr) ? 1u : 0u;
+        }
+      }
+    }
+    for (; r < r1; r += kMaskWarps) {
+      if (have) {
+        if constexpr (VEC) {
+          bits |= vec_bits<DT>(ld_stream_v4(col + r * ld), thr);
+        } else {
+          bits |= (fabsf(Elem<DT>::to_f(__ldg(col + r * ld))) > thr) ? 1u : 0u;
+        }
+      }
+    }
+  }
+  s_bits[warp][lane] = bits;
+  __syncthreads();
+
+  if (warp == 0) {
+    uint32_t b = 0;
+#pragma unroll
+    for (int w = 0; w < kMaskWarps; ++w) b |= s_bits[w][lane];
+    // Pack lane bits into 32-column words: G lanes share one word.
+    constexpr int G = 32 / VPT;
+    uint32_t word = b << ((lane % G) * VPT);
+#pragma unroll
+    for (int off = G / 2; off > 0; off >>= 1) word |= __shfl_xor_sync(0xFFFFFFFFu, word, off);
+    if ((lane % G) == 0 && word != 0u) {
+      const int64_t w_idx = (static_cast<int64_t>(blockIdx.x) * 32 * VPT + lane * VPT) / 32;
+      atomicOr(flags + w_idx, word);
+    }
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence();
+      const uint32_t total = gridDim.x * gridDim.y;
+      const uint32_t prev = atomicAdd(ticket, 1u);
+      s_last = (prev == total - 1u) ? 1 : 0;
+    }
+  }
+  __syncthreads();
+  if (!s_last) return;
+
+  // ---- Last CTA: stream compaction over the alive words --------------------
+  __threadfence();
+  const int64_t nwords = (cols + 31) / 32;
+  int64_t base = 0;
+  const bool mask_vec = (reinterpret_cast<uintptr_t>(mask) & 15u) == 0;
+  for (int64_t w0 = 0; w0 < nwords; w0 += kMaskThreads) {
+    const int64_t w = w0 + threadIdx.x;
+    uint32_t word = 0;
+    int nvalid = 0;
+    if (w < nwords) {
+      word = atomicExch(flags + w, 0u);
+      if (all_alive) word = 0xFFFFFFFFu;
+      const int64_t rem = cols - w * 32;
+      nvalid = rem < 32 ? static_cast<int>(rem) : 32;
+      if (nvalid < 32) word &= (1u << nvalid) - 1u;
+    }
+    // Block-wide exclusive scan of popcounts.
+    const int c = __popc(word);
+    int incl = c;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int t = __shfl_up_sync(0xFFFFFFFFu, incl, off);
+      if (lane >= off) incl += t;
+    }
+    if (lane == 31) s_scan[warp] = incl;
+    __syncthreads();
+    int64_t warp_base = 0, block_total = 0;
+#pragma unroll
+    for (int i = 0; i < kMaskWarps; ++i) {
+      if (i < warp) warp_base += s_scan[i];
+      block_total += s_scan[i];
+    }
+    int64_t pos = base + warp_base + (incl - c);
+    if (w < nwords) {
+      if (mask) {
+        int32_t* mrow = mask + w * 32;
+        if (mask_vec && nvalid == 32) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            int4 m4;
+            m4.x = (word >> (4 * q + 0)) & 1u;
+            m4.y = (word >> (4 * q + 1)) & 1u;
+            m4.z = (word >> (4 * q + 2)) & 1u;
+            m4.w = (word >> (4 * q + 3)) & 1u;
+            reinterpret_cast<int4*>(mrow)[q] = m4;
+          }
+        } else {
+          for (int e = 0; e < nvalid; ++e) mrow[e] = (word >> e) & 1u;
+        }
+      }
+      if (idx) {
+        uint32_t rest = word;
+        while (rest) {
+          const int e = __ffs(rest) - 1;
+          idx[pos++] = w * 32 + e;
+          rest &= rest - 1u;
+        }
+      }
+    }
+    base += block_total;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    if (count) *count = static_cast<int32_t>(base);
+    *ticket = 0u;
+  }
+}
+
+}  // namespace
+
+size_t mask_workspace_bytes(int64_t cols) {
+  const size_t words = static_cast<size_t>((cols + 31) / 32);
+  const size_t bytes = kFlagsOffset + words * sizeof(uint32_t);
+  return (bytes + 255) & ~static_cast<size_t>(255);
+}
+
+cudaError_t launch_mask_compact(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld,
+                                float thr, int32_t* mask, int64_t* idx, int32_t* count,
+                                void* workspace, int sm_count, cudaStream_t stream) {
+  const int esize = (dtype == GW_DTYPE_F32) ? 4 : 2;
+  const int vpt = 16 / esize;
+  const bool vec = ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) && (ld % vpt == 0) &&
+                   (cols % vpt == 0);
+  const int64_t nvec = vec ? cols / vpt : cols;
+  const int64_t col_tiles = (nvec + 31) / 32;
+  // Enough CTAs for ~8 resident per SM; at least 32 rows per CTA.
+  const int64_t target = static_cast<int64_t>(sm_count > 0 ? sm_count : 148) * 8;
+  int64_t row_tiles = (target + col_tiles - 1) / col_tiles;
+  const int64_t max_row_tiles = (rows + 31) / 32;
+  if (row_tiles > max_row_tiles) row_tiles = max_row_tiles;
+  if (row_tiles < 1) row_tiles = 1;
+  if (row_tiles > 65535) row_tiles = 65535;
+  int64_t rows_per_cta = (rows + row_tiles - 1) / row_tiles;
+  if (rows_per_cta > 0) row_tiles = (rows + rows_per_cta - 1) / rows_per_cta;
+  if (row_tiles < 1) row_tiles = 1;
+  if (col_tiles > 0x7FFFFFFFll) return cudaErrorInvalidValue;
+
+  dim3 grid(static_cast<unsigned>(col_tiles), static_cast<unsigned>(row_tiles));
+  uint32_t* ws = static_cast<uint32_t*>(workspace);
+#define GW_MASK_LAUNCH(DT, V)                                                               \
+  mask_compact_kernel<DT, V><<<grid, kMaskThreads, 0, stream>>>(x, rows, cols, ld, thr,     \
+                                                                 rows_per_cta, ws, mask, idx, \
+                                                                 count)
+  switch (dtype) {
+    case GW_DTYPE_F16:
+      if (vec) GW_MASK_LAUNCH(GW_DTYPE_F16, true); else GW_MASK_LAUNCH(GW_DTYPE_F16, false);
+      break;
+    case GW_DTYPE_BF16:
+      if (vec) GW_MASK_LAUNCH(GW_DTYPE_BF16, true); else GW_MASK_LAUNCH(GW_DTYPE_BF16, false);
+      break;
+    case GW_DTYPE_F32:
+      if (vec) GW_MASK_LAUNCH(GW_DTYPE_F32, true); else GW_MASK_LAUNCH(GW_DTYPE_F32, false);
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
+#undef GW_MASK_LAUNCH
+  return cudaGetLastError();
+}
+
+}  // namespace gw

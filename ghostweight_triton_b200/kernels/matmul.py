@@ -1,0 +1,100 @@
+"""Fused gather-GEMM on B200.
+
+``ghostweight_matmul`` mirrors ghostweight_triton/kernels/matmul.py:85-142:
+C[M, N] = A[:, alive] @ W[alive, :] with fp32 accumulation, cast to A's dtype;
+unsorted or repeated indices are fine and an empty index list gives zeros.
+On B200 the weight rows are first packed into the K'-major operand (one
+transposing gather) and the product runs on the tcgen05 kernel K3
+(csrc/gw_gemm_tc.cu), whose producer warps gather the alive activation columns
+straight into shared memory. fp32 inputs use the exact-fp32 kernel, matching
+the reference's TF32-off choice for fp32 (matmul.py:127-130).
+
+``ghost_linear`` is the module-level entry: activations [M, K] times an
+already packed weight, with bias and optional GELU fused into the epilogue.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ghostweight_triton_b200 import _native
+from ghostweight_triton_b200.kernels.gather import pack_weight
+
+
+def ghostweight_matmul(
+    activations: torch.Tensor,
+    weights: torch.Tensor,
+    alive_indices: torch.Tensor,
+    BLOCK_M: int = 64,
+    BLOCK_N: int = 64,
+    BLOCK_K: int = 32,
+    *,
+    bias: torch.Tensor | None = None,
+    activation: str | None = None,
+) -> torch.Tensor:
+    """Sparse matmul that skips dead neurons.
+
+    Parameters
+    ----------
+    activations   : [M, K]
+    weights       : [K, N]
+    alive_indices : [K_alive], any integer dtype (converted to int64)
+    BLOCK_M, BLOCK_N, BLOCK_K : accepted for signature compatibility; ignored.
+    bias          : optional [N], added in the fp32 epilogue (extension).
+    activation    : None, "gelu" or "gelu_tanh", applied after the bias (extension).
+
+    Returns
+    -------
+    torch.Tensor [M, N], dtype of ``activations``, contiguous.
+    """
+    assert activations.ndim == 2 and weights.ndim == 2
+    assert activations.is_cuda and weights.is_cuda
+    M, K = activations.shape
+    K_w, N = weights.shape
+    assert K == K_w, f"K mismatch: A K={K}, W K={K_w}"
+
+    activations = activations.contiguous()
+    weights = weights.contiguous()
+    alive_indices = alive_indices.contiguous().to(device=activations.device, dtype=torch.int64)
+    C = torch.empty((M, N), dtype=activations.dtype, device=activations.device)
+    if M == 0 or N == 0:
+        return C
+    w_packed = pack_weight(weights.t(), alive_indices, dtype=activations.dtype)
+    if bias is not None:
+        bias = bias.contiguous().to(dtype=activations.dtype)
+    _native.gather_gemm(activations, w_packed, alive_indices, C, bias=bias, activation=activation)
+    return C
+
+
+def ghost_linear(
+    x: torch.Tensor,
+    w_packed: torch.Tensor,
+    alive_indices: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    activation: str | None = None,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """y = act(x[:, alive] @ w_packed^T + bias) for x [M, K], w_packed [N, K_alive]."""
+    assert x.ndim == 2 and x.is_cuda
+    x = x.contiguous()
+    M = x.shape[0]
+    N = w_packed.shape[0]
+    y = out if out is not None else torch.empty((M, N), dtype=x.dtype, device=x.device)
+    if M and N:
+        _native.gather_gemm(x, w_packed, alive_indices, y, bias=bias, activation=activation)
+    return y
+
+
+def packed_linear(
+    a: torch.Tensor,
+    w_packed: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    activation: str | None = None,
+) -> torch.Tensor:
+    """y = act(a @ w_packed^T + bias) for an already compacted a [M, K_alive] (TMA operands)."""
+    assert a.ndim == 2 and a.is_cuda
+    a = a.contiguous()
+    y = torch.empty((a.shape[0], w_packed.shape[0]), dtype=a.dtype, device=a.device)
+    if y.numel():
+        _native.packed_gemm(a, w_packed, y, bias=bias, activation=activation)
+    return y

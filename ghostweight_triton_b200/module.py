@@ -1,0 +1,252 @@
+"""GhostLinear: drop-in nn.Linear with dead-neuron (dead-column) sparsity on B200.
+
+Mirrors ghostweight_triton/module.py:12-157 (same constructor, from_linear,
+forward semantics, freeze/unfreeze, current_sparsity, mask_frozen, repr).
+What changes underneath:
+
+* no per-call ``weight.t().contiguous()`` (module.py:97): the alive columns of
+  ``weight`` [N, K] are packed once into the K'-major operand W' and cached
+  (frozen mode) or packed per call from the alive list (dynamic mode, reading
+  only N*K' elements instead of transposing all N*K);
+* dynamic mode runs the fused mask+compaction kernel K1 instead of
+  dead_neuron_mask + torch.nonzero + cast (module.py:103-104); reading the
+  alive count is the one host synchronisation, as nonzero's is in the reference;
+* the bias add (module.py:116-117) is fused into the GEMM epilogue.
+
+Additions beyond the reference surface: ``freeze_weight_mask()`` freezes the
+mask from the per-input-column |W| reduction (the weight-side dead-column
+mask), ``from_conv1d`` wraps a transformers Conv1D, ``activation`` fuses a GELU
+into the epilogue, and the frozen index list survives state_dict round trips.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from ghostweight_triton_b200.kernels.gather import pack_weight
+from ghostweight_triton_b200.kernels.mask import dead_neuron_mask_compact, alive_indices as _alive
+from ghostweight_triton_b200.kernels.matmul import ghost_linear
+
+_ACTIVATIONS = (None, "gelu", "gelu_tanh")
+
+
+class GhostLinear(nn.Module):
+    """Drop-in nn.Linear replacement with training-free inference sparsity.
+
+    At inference time:
+      1. Detects dead input neurons (|activation| <= threshold across the batch).
+      2. If the dead fraction >= min_sparsity_to_activate: tcgen05 gather-GEMM
+         over the alive columns only.
+      3. Otherwise: dense F.linear (cuBLAS), as the reference does (module.py:111-112).
+
+    Masking modes:
+      Dynamic (default): recomputed every forward pass from the input.
+      Frozen: computed once by freeze_mask(calibration) or freeze_weight_mask().
+
+    Parameters
+    ----------
+    in_features, out_features, bias, device, dtype : as nn.Linear
+    threshold : float
+        Dead-neuron detection threshold (strict: alive iff max |x| > threshold).
+    min_sparsity_to_activate : float
+        Minimum dead fraction before the sparse path is used.
+    activation : None | "gelu" | "gelu_tanh"
+        Optional activation fused after the bias (extension; default None).
+    """
+
+    def __init__(
+        self,
+        in_features: int,
+        out_features: int,
+        bias: bool = True,
+        threshold: float = 1e-6,
+        min_sparsity_to_activate: float = 0.1,
+        device=None,
+        dtype=None,
+        activation: str | None = None,
+    ):
+        super().__init__()
+        if activation not in _ACTIVATIONS:
+            raise ValueError(f"activation must be one of {_ACTIVATIONS}, got {activation!r}")
+        self.in_features = in_features
+        self.out_features = out_features
+        self.threshold = threshold
+        self.min_sparsity_to_activate = min_sparsity_to_activate
+        self.activation = activation
+
+        factory = {"device": device, "dtype": dtype}
+        self.weight = nn.Parameter(torch.empty(out_features, in_features, **factory))
+        if bias:
+            self.bias = nn.Parameter(torch.empty(out_features, **factory))
+        else:
+            self.register_parameter("bias", None)
+
+        self.register_buffer("_frozen_indices", None)
+        self._mask_frozen: bool = False
+        self._last_sparsity: float = 0.0
+        # (key, packed weight) for the frozen index list; rebuilt when the
+        # weight, its dtype/device or the index list changes.
+        self._packed: tuple[tuple, torch.Tensor] | None = None
+
+    # ------------------------------------------------------------------ construction
+    @classmethod
+    def from_linear(
+        cls,
+        linear: nn.Linear,
+        threshold: float = 1e-6,
+        min_sparsity_to_activate: float = 0.1,
+    ) -> "GhostLinear":
+        """Wrap an existing nn.Linear; weight and bias Parameters are shared, not copied."""
+        ghost = cls(
+            in_features=linear.in_features,
+            out_features=linear.out_features,
+            bias=linear.bias is not None,
+            threshold=threshold,
+            min_sparsity_to_activate=min_sparsity_to_activate,
+            device=linear.weight.device,
+            dtype=linear.weight.dtype,
+        )
+        ghost.weight = linear.weight
+        if linear.bias is not None:
+            ghost.bias = linear.bias
+        return ghost
+
+    @classmethod
+    def from_conv1d(
+        cls,
+        conv: nn.Module,
+        threshold: float = 1e-6,
+        min_sparsity_to_activate: float = 0.1,
+    ) -> "GhostLinear":
+        """Wrap a transformers Conv1D (weight [in, out], y = x @ W + b).
+
+        The GhostLinear weight is a transposed VIEW of the Conv1D weight (same
+        storage, shape [out, in]); packing reads it with the transposing gather.
+        """
+        w = conv.weight
+        in_f, out_f = w.shape
+        ghost = cls(
+            in_features=in_f,
+            out_features=out_f,
+            bias=conv.bias is not None,
+            threshold=threshold,
+            min_sparsity_to_activate=min_sparsity_to_activate,
+            device=w.device,
+            dtype=w.dtype,
+        )
+        ghost.weight = nn.Parameter(w.data.t(), requires_grad=w.requires_grad)
+        if conv.bias is not None:
+            ghost.bias = conv.bias
+        return ghost
+
+    # ------------------------------------------------------------------ forward
+    def _weight_packed(self, alive: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+        w = self.weight
+        key = (w.data_ptr(), w._version, tuple(w.stride()), dtype, w.device,
+               alive.data_ptr(), alive.numel(), alive._version)
+        if self._packed is not None and self._packed[0] == key:
+            return self._packed[1]
+        packed = pack_weight(w.detach(), alive, dtype=dtype)
+        self._packed = (key, packed)
+        return packed
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        """x : [..., in_features] -> [..., out_features] (arbitrary batch dims)."""
+        orig_shape = x.shape
+        x_2d = x.reshape(-1, self.in_features)
+        assert x_2d.is_cuda, "GhostLinear runs on CUDA (sm_100) only"
+
+        frozen = self._mask_frozen and self._frozen_indices is not None
+        if frozen:
+            alive = self._frozen_indices
+            k_alive = alive.shape[0]
+        else:
+            _, buf, count = dead_neuron_mask_compact(x_2d, self.threshold, want_mask=False)
+            k_alive = int(count.item())
+            alive = buf[:k_alive]
+
+        sparsity = 1.0 - k_alive / self.in_features
+        self._last_sparsity = float(sparsity)
+
+        bias = self.bias
+        if bias is not None and bias.dtype != x_2d.dtype:
+            bias = bias.to(x_2d.dtype)
+        if sparsity < self.min_sparsity_to_activate or k_alive == 0:
+            out = F.linear(x_2d, self.weight.to(x_2d.dtype), bias)
+            if self.activation is not None:
+                out = F.gelu(out, approximate="tanh" if self.activation == "gelu_tanh" else "none")
+        else:
+            if frozen:
+                w_packed = self._weight_packed(alive, x_2d.dtype)
+            else:
+                w_packed = pack_weight(self.weight.detach(), alive, dtype=x_2d.dtype)
+            out = ghost_linear(x_2d, w_packed, alive, bias=bias, activation=self.activation)
+        return out.reshape(*orig_shape[:-1], self.out_features)
+
+    # ------------------------------------------------------------------ masks
+    def freeze_mask(self, calibration_input: torch.Tensor) -> None:
+        """Freeze the dead-neuron mask from calibration activations; later calls reuse it."""
+        with torch.no_grad():
+            x_2d = calibration_input.reshape(-1, self.in_features)
+            self._set_frozen(_alive(x_2d, self.threshold))
+
+    def freeze_weight_mask(self) -> None:
+        """Freeze the mask from the weight: input column k is dead iff max_n |W[n, k]| <= threshold.
+
+        A dead weight column contributes exactly zero, so the output equals the
+        dense layer's for every input.
+        """
+        with torch.no_grad():
+            w = self.weight.detach()
+            self._set_frozen(_alive(w if w.stride(1) == 1 else w.contiguous(), self.threshold))
+
+    def _set_frozen(self, idx: torch.Tensor) -> None:
+        self._frozen_indices = idx.to(torch.int64)
+        self._mask_frozen = True
+        self._packed = None
+        k_alive = int(self._frozen_indices.numel())
+        self._last_sparsity = float(1.0 - k_alive / self.in_features)
+
+    def unfreeze_mask(self) -> None:
+        """Switch back to dynamic per-forward masking."""
+        self._mask_frozen = False
+        self._frozen_indices = None
+        self._packed = None
+
+    @property
+    def current_sparsity(self) -> float:
+        """Sparsity of the frozen mask, or of the most recent forward pass."""
+        return self._last_sparsity
+
+    @property
+    def mask_frozen(self) -> bool:
+        return self._mask_frozen
+
+    # ------------------------------------------------------------------ checkpointing
+    def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict,
+                              missing_keys, unexpected_keys, error_msgs):
+        key = prefix + "_frozen_indices"
+        if key in state_dict and self._frozen_indices is None:
+            idx = state_dict.pop(key)
+            super()._load_from_state_dict(state_dict, prefix, local_metadata, strict,
+                                          missing_keys, unexpected_keys, error_msgs)
+            state_dict[key] = idx
+            self._set_frozen(idx.to(self.weight.device))
+            return
+        super()._load_from_state_dict(state_dict, prefix, local_metadata, strict,
+                                      missing_keys, unexpected_keys, error_msgs)
+        if self._frozen_indices is not None:
+            self._mask_frozen = True
+            self._packed = None
+            self._last_sparsity = float(1.0 - self._frozen_indices.numel() / self.in_features)
+
+    def extra_repr(self) -> str:
+        return (
+            f"in={self.in_features}, out={self.out_features}, "
+            f"bias={self.bias is not None}, "
+            f"threshold={self.threshold}, "
+            f"frozen={self._mask_frozen}, "
+            f"sparsity={self._last_sparsity:.1%}"
+        )

@@ -1,0 +1,189 @@
+/*
+ * ghostweight_b200.h -- C ABI of the B200 (sm_100a) column-sparse linear hot path.
+ *
+ * The library (ghostweight_triton_b200/libghostweight_b200.so) replaces the
+ * Triton kernels of ghostweight-triton (ghostweight_triton/kernels/*.py) with
+ * hand-written CUDA for sm_100a. Every entry point:
+ *   - takes caller-allocated DEVICE pointers, plain sizes and leading
+ *     dimensions (in elements), and a cudaStream_t passed as void*;
+ *   - never allocates device memory and never synchronises the stream;
+ *   - returns a gw_status (0 = success) after validating shapes, dtypes,
+ *     alignment and the launch; no torch types cross this boundary.
+ * Matrices are row-major: element (r, c) of a matrix with leading dimension
+ * ld lives at base[r * ld + c].
+ *
+ * Index lists ("alive indices") are int64, as the reference passes them
+ * (ghostweight_triton/kernels/matmul.py:120, gather.py:128). An index outside
+ * [0, K) is read as a zero column (never dereferenced) and raises
+ * GW_DEVICE_ERR_BAD_INDEX in the device error word.
+ */
+#ifndef GHOSTWEIGHT_B200_H
+#define GHOSTWEIGHT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define GW_API __attribute__((visibility("default")))
+#else
+#define GW_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types. The reference accepts fp16 and fp32 (tests/conftest.py:101); bf16 is added. */
+typedef enum {
+  GW_DTYPE_F16 = 0,
+  GW_DTYPE_BF16 = 1,
+  GW_DTYPE_F32 = 2
+} gw_dtype;
+
+/* Fused GEMM epilogue activation (applied after the bias add). */
+typedef enum {
+  GW_EPI_NONE = 0,
+  GW_EPI_GELU_ERF = 1,  /* torch.nn.GELU() / F.gelu(approximate="none") */
+  GW_EPI_GELU_TANH = 2  /* F.gelu(approximate="tanh"), GPT-2's gelu_new */
+} gw_epilogue;
+
+typedef enum {
+  GW_OK = 0,
+  GW_ERR_SHAPE = 1,       /* negative / inconsistent sizes or leading dimensions */
+  GW_ERR_DTYPE = 2,       /* unsupported dtype for this entry point */
+  GW_ERR_ALIGN = 3,       /* pointer or leading dimension misaligned for the kernel */
+  GW_ERR_NULL = 4,        /* required pointer is NULL */
+  GW_ERR_WORKSPACE = 5,   /* workspace missing or too small */
+  GW_ERR_CUDA = 6,        /* a CUDA runtime call or launch failed */
+  GW_ERR_DEVICE = 7,      /* current device is not sm_100 (B200) */
+  GW_ERR_UNSUPPORTED = 8  /* valid request this build does not implement */
+} gw_status;
+
+/* Bits of the device error word (gw_get_device_error). */
+#define GW_DEVICE_ERR_WAIT_TIMEOUT 1u
+#define GW_DEVICE_ERR_BAD_INDEX 2u
+
+/* Human-readable text for a gw_status value. */
+GW_API const char* gw_status_string(int status);
+
+/* Text of the last CUDA error seen by this library on the calling thread. */
+GW_API const char* gw_last_cuda_error(void);
+
+/* Library version, e.g. "0.1.0". */
+GW_API const char* gw_version(void);
+
+/* 1 if `device` is an sm_100 part this library can launch on, else 0. */
+GW_API int gw_device_supported(int device);
+
+/*
+ * Reads (and, if reset != 0, clears) the device error word of the current
+ * device. Synchronises the device. *out receives GW_DEVICE_ERR_* bits.
+ */
+GW_API int gw_get_device_error(int reset, unsigned int* out);
+
+/*
+ * Dead-column mask fused with stream compaction.
+ *
+ * Replaces ghostweight_triton/kernels/mask.py:62-104 (dead_neuron_mask,
+ * kernel mask.py:21-59) together with the torch.nonzero compaction that
+ * follows it at ghostweight_triton/module.py:104 and module.py:129-131.
+ *
+ * For an [rows, cols] matrix x:
+ *   colmax[k]  = max(0, max_r fp32(|x[r, k]|)), NaN entries ignored
+ *   mask[k]    = colmax[k] > fp32(threshold) ? 1 : 0           (int32, [cols])
+ *   alive_idx  = ascending k with mask[k] == 1                 (int64, [cols] capacity)
+ *   *alive_count = number of alive columns                      (int32, device)
+ * Applied to an activation [M, K] it is the reference's activation mask; applied
+ * to nn.Linear.weight [N, K] it is the per-input-column |W| mask.
+ * mask, alive_idx and alive_count may each be NULL if not wanted.
+ *
+ * workspace: at least gw_mask_workspace_bytes(cols) bytes of device memory that
+ * must be all-zero before the first call; every call leaves it all-zero again.
+ * Calls sharing one workspace must be ordered on one stream.
+ */
+GW_API size_t gw_mask_workspace_bytes(int64_t cols);
+GW_API int gw_mask_compact(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld,
+                           double threshold, int32_t* mask, int64_t* alive_idx,
+                           int32_t* alive_count, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
+/*
+ * Column gather: dst[r, j] = src[r, idx[j]] for j < n_idx, and dst[r, j] = 0
+ * for n_idx <= j < pad_to (pad_to <= ld_dst; pass pad_to = n_idx for no padding).
+ *
+ * Replaces the activation side of gather_compact, ghostweight_triton/kernels/
+ * gather.py:19-55 (_gather_columns_kernel) and :139-146. With src =
+ * nn.Linear.weight [N, K] it is the one-time weight compaction that packs
+ * W[:, alive] into the K'-major operand layout of gw_gather_gemm.
+ */
+GW_API int gw_gather_columns(const void* src, int dtype, int64_t rows, int64_t cols,
+                             int64_t ld_src, const int64_t* idx, int64_t n_idx, void* dst,
+                             int64_t ld_dst, int64_t pad_to, void* stream);
+
+/*
+ * Row gather: dst[j, :] = src[idx[j], :] for j < n_idx.
+ *
+ * Replaces the weight side of gather_compact, ghostweight_triton/kernels/
+ * gather.py:58-94 (_gather_rows_kernel) and :149-156.
+ */
+GW_API int gw_gather_rows(const void* src, int dtype, int64_t rows, int64_t cols, int64_t ld_src,
+                          const int64_t* idx, int64_t n_idx, void* dst, int64_t ld_dst,
+                          void* stream);
+
+/*
+ * Transposing row gather: dst[n, j] = src[idx[j], n] for n < cols, j < n_idx;
+ * dst[n, j] = 0 for n_idx <= j < pad_to.
+ *
+ * Packs a reference-orientation weight W [K, N] (the `weights` argument of
+ * ghostweight_triton/kernels/matmul.py:85-92, i.e. linear.weight.t() from
+ * module.py:97, or a transformers Conv1D weight) into the [N, K'] K'-major
+ * operand of gw_gather_gemm. It replaces the W-row gather done inside the
+ * reference's matmul loop (matmul.py:66-72).
+ */
+GW_API int gw_gather_rows_t(const void* src, int dtype, int64_t rows, int64_t cols,
+                            int64_t ld_src, const int64_t* idx, int64_t n_idx, void* dst,
+                            int64_t ld_dst, int64_t pad_to, void* stream);
+
+/*
+ * Fused gather-GEMM:
+ *   y[m, n] = act( sum_{j < n_alive} x[m, idx[j]] * w_packed[n, j] + bias[n] )
+ * x: [M, K] (ldx), w_packed: [N, >= n_alive] K'-major (ldw), bias: [N] or NULL,
+ * y: [M, N] (ldy). fp32 accumulation; output rounded once to the input dtype.
+ * idx may be in any order and contain repeats. n_alive == 0 gives act(bias)
+ * (zeros without bias).
+ *
+ * Replaces ghostweight_triton/kernels/matmul.py:85-142 (ghostweight_matmul,
+ * kernel matmul.py:27-82) plus the separate bias add at module.py:116-117.
+ * fp16/bf16 run on tcgen05 tensor cores (requires ldw % 8 == 0 and a 16-byte
+ * aligned w_packed); fp32 runs an exact-fp32 FFMA kernel (no TF32), as the
+ * reference disables TF32 for fp32 (matmul.py:127-130).
+ */
+GW_API int gw_gather_gemm(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
+                          const void* w_packed, int64_t N, int64_t ldw, const int64_t* idx,
+                          int64_t n_alive, const void* bias, int epilogue, void* y, int64_t ldy,
+                          void* stream);
+
+/*
+ * Dense GEMM over an already-compacted activation (the two-step path of
+ * gather.py:1-14: gather_compact followed by a matmul):
+ *   y[m, n] = act( sum_{j < K} a[m, j] * w_packed[n, j] + bias[n] )
+ * fp16/bf16 only; both operands arrive by TMA (requires 16-byte aligned bases
+ * and lda, ldw multiples of 8).
+ */
+GW_API int gw_packed_gemm(const void* a, int dtype, int64_t M, int64_t K, int64_t lda,
+                          const void* w_packed, int64_t N, int64_t ldw, const void* bias,
+                          int epilogue, void* y, int64_t ldy, void* stream);
+
+/*
+ * Counts indices outside [0, K) into *bad_count (int32, device, overwritten).
+ * Debug helper for callers that want the reference's implicit "indices are
+ * valid" contract checked (kernels/matmul.py:120 performs no check).
+ */
+GW_API int gw_validate_indices(const int64_t* idx, int64_t n, int64_t K, int32_t* bad_count,
+                               void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* GHOSTWEIGHT_B200_H */

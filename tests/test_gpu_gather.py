@@ -1,0 +1,122 @@
+"""GPU parity of K2 (gathers, weight packing) through the C ABI: bit-exact.
+
+Golden fixtures hold the reference's own gather outputs (gather.py:19-94);
+packing is checked against the oracle in both weight orientations.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from ghostweight_triton_b200 import _native
+from ghostweight_triton_b200.kernels import gather_compact
+from ghostweight_triton_b200.kernels.gather import pack_weight, pack_weight_kn
+from oracle import gw_oracle as O
+from tests.golden import gw_golden as G
+from tests.golden.gw_inputs import rand_matrix, dead_columns, alive_from_dead
+
+pytestmark = pytest.mark.gpu
+
+
+def to_dev(a: np.ndarray) -> torch.Tensor:
+    if a.dtype == np.uint16:
+        return torch.from_numpy(a.view(np.int16)).view(torch.bfloat16).cuda()
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def to_np(t: torch.Tensor) -> np.ndarray:
+    if t.dtype == torch.bfloat16:
+        return t.cpu().view(torch.int16).numpy().view(np.uint16)
+    return t.cpu().numpy()
+
+
+@pytest.mark.parametrize("name", G.names("gather"))
+def test_golden_gather(name):
+    meta, inp, exp = G.load(name)
+    A_c, W_c = gather_compact(to_dev(inp["A"]), to_dev(inp["W"]), to_dev(exp["idx"]))
+    G.check_exact(to_np(A_c), exp, "A_c")
+    G.check_exact(to_np(W_c), exp, "W_c")
+    assert A_c.is_contiguous() and W_c.is_contiguous()
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16", "f32"])
+@pytest.mark.parametrize("N,K,sp", [(1, 64, 0.5), (10, 128, 0.0), (136, 320, 0.5),
+                                    (3072, 768, 0.5), (512, 4096, 0.9), (77, 1000, 0.33)])
+def test_pack_weight_both_orientations(dt, N, K, sp):
+    w = rand_matrix((N, K), N + K, dt)
+    idx = alive_from_dead(K, dead_columns(K, sp, N + K))
+    ld = max(-(-len(idx) // 64) * 64, 64)
+    ref = O.pack_weight(w, idx, pad_to=ld)
+    wd = to_dev(w)
+    idd = torch.from_numpy(idx).cuda()
+    p1 = pack_weight(wd, idd)                                   # [N, K] row-major: column gather
+    p2 = pack_weight_kn(wd.t().contiguous(), idd)               # [K, N]: transposing gather
+    for p in (p1, p2):
+        assert p.shape == (N, len(idx)) and p.stride() == (ld, 1)
+        full = to_np(p.as_strided((N, ld), (ld, 1)))
+        assert np.array_equal(full.view(np.uint8), ref.view(np.uint8))
+
+
+def test_unsorted_repeated_and_reversed_indices():
+    A = rand_matrix((9, 300), 1, "f16")
+    W = rand_matrix((300, 70), 2, "f16")
+    for idx in (np.arange(299, -1, -1), np.array([5, 5, 0, 299, 17, 5]),
+                np.random.default_rng(4).permutation(300)[:123]):
+        A_c, W_c = gather_compact(to_dev(A), to_dev(W), torch.from_numpy(idx).cuda())
+        assert np.array_equal(to_np(A_c), O.gather_columns(A, idx))
+        assert np.array_equal(to_np(W_c), O.gather_rows(W, idx))
+
+
+def test_int32_indices_accepted():
+    A = torch.randn(4, 64, device="cuda")
+    W = torch.randn(64, 8, device="cuda")
+    idx = torch.arange(0, 64, 3, device="cuda", dtype=torch.int32)
+    A_c, W_c = gather_compact(A, W, idx)
+    assert torch.equal(A_c, A[:, idx.long()]) and torch.equal(W_c, W[idx.long()])
+
+
+def test_out_of_range_index_reads_zero_and_flags():
+    _native.device_error(reset=True)
+    A = torch.randn(4, 16, device="cuda")
+    W = torch.randn(16, 8, device="cuda")
+    idx = torch.tensor([0, 99, 3], device="cuda")
+    A_c, W_c = gather_compact(A, W, idx)
+    assert torch.equal(A_c[:, 1], torch.zeros(4, device="cuda"))
+    assert torch.equal(W_c[1], torch.zeros(8, device="cuda"))
+    assert torch.equal(A_c[:, 2], A[:, 3])
+    assert _native.device_error(reset=True) & _native.DEVICE_ERR_BAD_INDEX
+    assert _native.validate_indices(idx, 16) == 1
+
+
+class TestReferenceSuite:
+    """ghostweight_triton tests/test_gather.py:66-216, on B200."""
+
+    @pytest.mark.parametrize("M,K,N,sparsity", [(1, 128, 256, 0.0), (1, 128, 256, 0.5),
+                                                (16, 768, 3072, 0.3), (128, 768, 3072, 0.7),
+                                                (128, 3072, 768, 0.5)])
+    def test_output_shapes(self, device, M, K, N, sparsity):
+        A = torch.randn(M, K, dtype=torch.float16, device=device)
+        W = torch.randn(K, N, dtype=torch.float16, device=device)
+        idx = torch.from_numpy(alive_from_dead(K, dead_columns(K, sparsity, 7))).to(device)
+        A_c, W_c = gather_compact(A, W, idx)
+        assert A_c.shape == (M, idx.numel()) and W_c.shape == (idx.numel(), N)
+
+    def test_identity_and_single(self, device):
+        A = torch.randn(4, 32, device=device)
+        W = torch.randn(32, 16, device=device)
+        A_c, W_c = gather_compact(A, W, torch.arange(32, device=device))
+        assert torch.equal(A_c, A) and torch.equal(W_c, W)
+        A = torch.arange(16, dtype=torch.float32, device=device).unsqueeze(0)
+        W = torch.eye(16, 8, device=device)
+        A_c, W_c = gather_compact(A, W, torch.tensor([5], device=device))
+        assert A_c[0, 0].item() == 5.0 and torch.equal(W_c[0], W[5])
+
+    @pytest.mark.parametrize("dtype", [torch.float16, torch.float32, torch.bfloat16])
+    def test_dtype_device_contiguity(self, device, dtype):
+        A = torch.randn(4, 64, dtype=dtype, device=device)
+        W = torch.randn(64, 32, dtype=dtype, device=device)
+        A_c, W_c = gather_compact(A, W, torch.arange(32, device=device))
+        assert A_c.dtype == dtype and W_c.dtype == dtype
+        assert A_c.is_cuda and W_c.is_cuda and A_c.is_contiguous() and W_c.is_contiguous()

@@ -1,0 +1,247 @@
+"""GPU parity of K3 (tcgen05 gather-GEMM, exact-fp32 gather-GEMM) through the C ABI.
+
+Tolerances are the reference's own (tests/test_matmul.py:68-72): fp16/bf16
+atol = rtol = 1e-2, fp32 atol = rtol = 1e-4. Golden fixtures hold the
+reference's ghostweight_matmul outputs; the oracle covers bf16, bias and the
+GELU epilogues; full-size cases are checked against the dense fp32 product
+(dead columns are zero, so the sparse and dense products agree).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from ghostweight_triton_b200 import _native
+from ghostweight_triton_b200.kernels import ghostweight_matmul
+from ghostweight_triton_b200.kernels.gather import pack_weight
+from ghostweight_triton_b200.kernels.matmul import ghost_linear, packed_linear
+from oracle import gw_oracle as O
+from tests.conftest import tols
+from tests.golden import gw_golden as G
+from tests.golden.gw_inputs import rand_matrix, dead_columns, alive_from_dead, zero_columns
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"f16": (1e-2, 1e-2), "bf16": (1e-2, 1e-2), "f32": (1e-4, 1e-4)}
+DT = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}
+
+
+def to_dev(a: np.ndarray) -> torch.Tensor:
+    if a.dtype == np.uint16:
+        return torch.from_numpy(a.view(np.int16)).view(torch.bfloat16).cuda()
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def to_np(t: torch.Tensor) -> np.ndarray:
+    if t.dtype == torch.bfloat16:
+        return t.cpu().view(torch.int16).numpy().view(np.uint16)
+    return t.cpu().numpy()
+
+
+def as_f32(a: np.ndarray, dt: str) -> np.ndarray:
+    return O.to_f32(a, dt)
+
+
+def assert_close(got: np.ndarray, ref: np.ndarray, dt: str, what: str = ""):
+    atol, rtol = TOL[dt]
+    g, r = as_f32(got, dt).astype(np.float64), as_f32(ref, dt).astype(np.float64)
+    bad = ~(np.abs(g - r) <= atol + rtol * np.abs(r))
+    assert not bad.any(), f"{what}: {bad.sum()}/{bad.size} off, max err {np.abs(g - r).max():.3g}"
+
+
+# ----------------------------------------------------------------- golden (reference outputs)
+@pytest.mark.parametrize("name", G.names("matmul"))
+def test_golden_matmul(name):
+    meta, inp, exp = G.load(name)
+    C = ghostweight_matmul(to_dev(inp["A"]), to_dev(inp["W"]), to_dev(exp["idx"]))
+    atol, rtol = TOL[meta["dtype"]]
+    G.check_close(to_np(C), exp, "C", atol, rtol)
+
+
+# ----------------------------------------------------------------- oracle sweep (linear form)
+@pytest.mark.parametrize("dt", ["f16", "bf16", "f32"])
+@pytest.mark.parametrize("M,K,N,sp,pattern", [
+    (1, 128, 256, 0.5, "random"), (7, 64, 10, 0.0, "random"), (128, 768, 3072, 0.5, "random"),
+    (200, 320, 136, 0.5, "random"), (129, 1000, 520, 0.9, "random"), (300, 4096, 384, 0.75, "block"),
+    (1024, 2048, 1024, 0.5, "random"), (16, 4096, 4096, 0.5, "random"), (77, 130, 33, 0.1, "random"),
+])
+@pytest.mark.parametrize("bias,act", [(False, None), (True, None), (True, "gelu"), (True, "gelu_tanh")])
+def test_ghost_linear_vs_oracle(dt, M, K, N, sp, pattern, bias, act):
+    seed = M + 3 * K + 7 * N
+    x = rand_matrix((M, K), seed, dt, 0.5)
+    w = rand_matrix((N, K), seed + 1, dt, 1.0 / np.sqrt(K))
+    b = rand_matrix((N,), seed + 2, dt, 0.5) if bias else None
+    idx = alive_from_dead(K, dead_columns(K, sp, seed, pattern, 64))
+    ref = O.ghost_linear(x, w, idx, b, act, dtype=dt)
+    xd, wd, idd = to_dev(x), to_dev(w), torch.from_numpy(idx).cuda()
+    y = ghost_linear(xd, pack_weight(wd, idd), idd, bias=to_dev(b) if bias else None, activation=act)
+    assert y.dtype == DT[dt] and y.shape == (M, N)
+    assert_close(to_np(y), ref, dt, f"{dt} {M}x{K}x{N} s={sp} bias={bias} act={act}")
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_packed_gemm_tma_operands(dt):
+    M, K, N = 333, 512, 264
+    a = rand_matrix((M, K), 1, dt)
+    w = rand_matrix((N, K), 2, dt, 1 / np.sqrt(K))
+    b = rand_matrix((N,), 3, dt)
+    ref = O.ghost_linear(a, w, np.arange(K), b, "gelu", dtype=dt)
+    wd = pack_weight(to_dev(w), torch.arange(K, device="cuda"))
+    y = packed_linear(to_dev(a), wd, bias=to_dev(b), activation="gelu")
+    assert_close(to_np(y), ref, dt, "packed")
+
+
+def test_empty_alive_gives_bias_or_zeros():
+    x = torch.randn(5, 64, device="cuda", dtype=torch.float16)
+    w = torch.randn(64, 24, device="cuda", dtype=torch.float16)
+    C = ghostweight_matmul(x, w, torch.empty(0, dtype=torch.int64, device="cuda"))
+    assert C.shape == (5, 24) and torch.count_nonzero(C).item() == 0
+    b = torch.randn(24, device="cuda", dtype=torch.float16)
+    C = ghostweight_matmul(x, w, torch.empty(0, dtype=torch.int64, device="cuda"), bias=b)
+    assert torch.equal(C, b.expand(5, 24))
+
+
+def test_misaligned_output_leading_dimension():
+    """ldy not a multiple of 8 forces the scalar epilogue store path."""
+    x = torch.randn(70, 256, device="cuda", dtype=torch.float16)
+    w = torch.randn(100, 256, device="cuda", dtype=torch.float16) / 16
+    idx = torch.arange(0, 256, 2, device="cuda")
+    big = torch.zeros(70, 101, device="cuda", dtype=torch.float16)
+    y = big[:, :100]
+    _native.gather_gemm(x, pack_weight(w, idx), idx, y)
+    ref = (x.float()[:, idx] @ w.float()[:, idx].t()).half()
+    torch.testing.assert_close(y, ref, **tols(torch.float16))
+    assert torch.count_nonzero(big[:, 100]).item() == 0
+
+
+def test_repeated_indices_and_out_of_range():
+    _native.device_error(reset=True)
+    x = torch.randn(20, 64, device="cuda", dtype=torch.float16)
+    w = torch.randn(64, 48, device="cuda", dtype=torch.float16) / 8
+    idx = torch.tensor([3, 3, 7, 63, 0, 3], device="cuda")
+    C = ghostweight_matmul(x, w, idx)
+    ref = (x.float()[:, idx] @ w.float()[idx, :]).half()
+    torch.testing.assert_close(C, ref, **tols(torch.float16))
+    assert _native.device_error(reset=True) == 0
+    bad = torch.tensor([3, 64, 7], device="cuda")
+    C = ghostweight_matmul(x, w, bad)       # index 64 is out of range: contributes zero
+    keep = torch.tensor([3, 7], device="cuda")
+    torch.testing.assert_close(C, (x.float()[:, keep] @ w.float()[keep, :]).half(), **tols(torch.float16))
+    assert _native.device_error(reset=True) & _native.DEVICE_ERR_BAD_INDEX
+
+
+def test_no_wait_timeouts_after_suite():
+    assert _native.device_error(reset=False) & _native.DEVICE_ERR_WAIT_TIMEOUT == 0
+
+
+# ----------------------------------------------------------------- reference-suite cases
+class TestReferenceSuite:
+    """ghostweight_triton tests/test_matmul.py:105-207, on B200."""
+
+    @staticmethod
+    def _inputs(M, K, N, dtype, device, sparsity, seed=99):
+        torch.manual_seed(seed)
+        A = torch.randn(M, K, dtype=dtype, device=device) * 0.1
+        W = torch.randn(K, N, dtype=dtype, device=device) * 0.1
+        dead = set(torch.randperm(K)[: int(K * sparsity)].tolist())
+        idx = torch.tensor(sorted(k for k in range(K) if k not in dead), dtype=torch.int64, device=device)
+        return A, W, idx
+
+    @staticmethod
+    def _ref(A, W, idx):
+        return (A.float()[:, idx] @ W.float()[idx, :]).to(A.dtype)
+
+    @pytest.mark.parametrize("M,K,N", [(1, 128, 256), (1, 768, 3072), (16, 768, 3072),
+                                       (128, 768, 3072), (128, 3072, 768)])
+    def test_output_shape(self, device, M, K, N):
+        A, W, idx = self._inputs(M, K, N, torch.float16, device, 0.5)
+        C = ghostweight_matmul(A, W, idx)
+        assert C.shape == (M, N) and C.is_cuda and C.is_contiguous()
+
+    @pytest.mark.parametrize("dtype", [torch.float16, torch.float32, torch.bfloat16])
+    @pytest.mark.parametrize("M,K,N,sparsity", [(1, 128, 256, 0.0), (1, 768, 3072, 0.5),
+                                                (16, 768, 3072, 0.3), (128, 768, 3072, 0.7),
+                                                (128, 3072, 768, 0.5), (16, 256, 128, 0.9)])
+    def test_matches_reference(self, device, dtype, M, K, N, sparsity):
+        A, W, idx = self._inputs(M, K, N, dtype, device, sparsity)
+        C = ghostweight_matmul(A, W, idx)
+        assert C.dtype == dtype
+        torch.testing.assert_close(C, self._ref(A, W, idx), **tols(dtype))
+
+    def test_dense_equals_matmul(self, device):
+        torch.manual_seed(1)
+        A = torch.randn(32, 128, device=device) * 0.1
+        W = torch.randn(128, 64, device=device) * 0.1
+        C = ghostweight_matmul(A, W, torch.arange(128, device=device))
+        torch.backends.cuda.matmul.allow_tf32 = False
+        torch.testing.assert_close(C, A @ W, atol=1e-4, rtol=1e-4)
+
+    def test_k_alive_one(self, device):
+        torch.manual_seed(2)
+        A = torch.randn(4, 128, device=device)
+        W = torch.randn(128, 16, device=device)
+        C = ghostweight_matmul(A, W, torch.tensor([7], device=device))
+        torch.testing.assert_close(C, A[:, [7]] * W[[7], :], atol=1e-4, rtol=1e-4)
+
+    def test_unsorted(self, device):
+        torch.manual_seed(3)
+        A = torch.randn(8, 64, device=device) * 0.1
+        W = torch.randn(64, 32, device=device) * 0.1
+        idx = torch.randperm(64, device=device)[:32]
+        torch.testing.assert_close(ghostweight_matmul(A, W, idx), self._ref(A, W, idx),
+                                   atol=1e-4, rtol=1e-4)
+
+    def test_block_kwargs_accepted(self, device):
+        A, W, idx = self._inputs(64, 128, 64, torch.float32, device, 0.5)
+        ref = self._ref(A, W, idx)
+        for bm, bn, bk in [(32, 32, 16), (64, 64, 32), (128, 64, 32)]:
+            torch.testing.assert_close(ghostweight_matmul(A, W, idx, BLOCK_M=bm, BLOCK_N=bn, BLOCK_K=bk),
+                                       ref, atol=1e-4, rtol=1e-4)
+
+    @pytest.mark.parametrize("M,K,N", [(1, 768, 3072), (128, 768, 3072), (128, 3072, 768), (1, 768, 2304)])
+    def test_gpt2_shapes_finite(self, device, M, K, N):
+        A, W, idx = self._inputs(M, K, N, torch.float16, device, 0.5)
+        C = ghostweight_matmul(A, W, idx)
+        assert torch.isfinite(C).all()
+
+
+# ----------------------------------------------------------------- full-size properties
+@pytest.mark.parametrize("M", [4096, 1024, 128, 16])
+@pytest.mark.parametrize("sp,pattern", [(0.0, "random"), (0.5, "random"), (0.9, "random"),
+                                        (0.75, "block")])
+def test_gemm_sweep_size_vs_dense_fp32(M, sp, pattern):
+    """M x 4096 x 4096 fp16: sparse result equals the dense fp32 product of the zeroed weight."""
+    K = N = 4096
+    g = torch.Generator(device="cuda").manual_seed(M)
+    x = torch.randn(M, K, device="cuda", dtype=torch.float16, generator=g)
+    w = (torch.randn(N, K, device="cuda", generator=g) / K ** 0.5).half()
+    dead = torch.from_numpy(dead_columns(K, sp, M, pattern, 64)).cuda()
+    w[:, dead] = 0
+    from ghostweight_triton_b200.kernels.mask import alive_indices
+
+    idx = alive_indices(w, 0.0)
+    assert idx.numel() == K - dead.numel()
+    y = ghost_linear(x, pack_weight(w, idx), idx)
+    ref = F.linear(x.float(), w.float()).half()
+    torch.testing.assert_close(y, ref, **tols(torch.float16))
+
+
+def test_sharded_mlp_size_bf16_rows():
+    """X [8192, 8192] bf16, W [28672, 8192] with 70% dead 128-blocks: spot-check rows vs fp32."""
+    M, K, N = 8192, 8192, 28672
+    g = torch.Generator(device="cuda").manual_seed(11)
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16, generator=g)
+    w = (torch.randn(N, K, device="cuda", generator=g) / K ** 0.5).bfloat16()
+    dead = torch.from_numpy(dead_columns(K, 0.7, 11, "block", 128)).cuda()
+    w[:, dead] = 0
+    from ghostweight_triton_b200.kernels.mask import alive_indices
+
+    idx = alive_indices(w, 0.0)
+    assert idx.numel() == 2560
+    y = ghost_linear(x, pack_weight(w, idx), idx)
+    rows = torch.arange(0, M, 257, device="cuda")
+    ref = (x[rows].float() @ w.float().t()).bfloat16()
+    torch.testing.assert_close(y[rows], ref, **tols(torch.bfloat16))
