@@ -1,0 +1,558 @@
+"""Benchmark of the column-sparse linear hot path on B200.
+
+Headline workload (one "step"): one fused gather-GEMM of the standalone sweep's
+reference point, y = x[:, alive] @ W'^T with x [4096, 4096] fp16, W [4096, 4096]
+fp16 ~ N(0, 1/sqrt(K)) with 50 % of its input columns (seeded uniform choice)
+zeroed, K' = 2048 alive columns found by the mask kernel and packed once.
+Metric: useful TFLOP/s = 2*M*N*K' / time (dense-equivalent 2*M*N*K also shown).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload gemm|mlp-sharded] [--no-sweep] [--no-cpu-baseline]
+
+* Inputs are resident in HBM: 4 independent layers (x, W', y) rotate so every
+  step reads cold data (4 x 80 MB > 126 MB L2).
+* Device time by CUDA events on the launching stream, barrier + synchronize on
+  both sides, max over ranks. N > 1 (torchrun): every rank runs its own batch
+  through its own copy of the layer ("scaling": "weak"); no collective on the
+  data path. --workload mlp-sharded runs the sharded MLP projection instead:
+  x [8192, 8192] bf16, W [28672, 8192] with 70 % dead 128-column blocks,
+  output features split across ranks, NCCL all-gather of y ("strong").
+* e2e: the same step through GhostLinear (frozen weight mask) with x copied
+  from pinned host memory and y copied back inside the timed region.
+* --impl reference: the reference's CPU path for this computation
+  (A.float()[:, idx] @ W.float()[idx, :], tests/test_matmul.py:30-42 of
+  ghostweight-triton), restated by the oracle in numpy on all host cores, on
+  a bounded row sample per step; rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+HEADLINE = dict(M=4096, N=4096, K=4096, sparsity=0.5, pattern="random", dtype="fp16")
+MLP = dict(M=8192, N=28672, K=8192, sparsity=0.7, pattern="block128", dtype="bf16")
+METRIC = "useful TFLOP/s of the fused gather-GEMM (2*M*N*K')"
+N_SETS = 4
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+# ---------------------------------------------------------------------------- helpers
+def load_peaks() -> tuple[dict, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()), "measured"
+        except Exception:
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def dead_columns(K: int, sparsity: float, seed: int, pattern: str) -> np.ndarray:
+    rng = np.random.default_rng(seed + 7919)
+    if pattern == "random":
+        return np.sort(rng.permutation(K)[: int(K * sparsity)])
+    block = int(pattern.replace("block", ""))
+    nb = K // block
+    blocks = np.sort(rng.permutation(nb)[: int(nb * sparsity)])
+    return (blocks[:, None] * block + np.arange(block)[None, :]).reshape(-1)
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clock and throttle reasons while the GPU is busy."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.rows: list[list[str]] = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu_index), "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return self
+
+        def reader():
+            for line in self.proc.stdout:
+                self.rows.append([c.strip() for c in line.split(",")])
+
+        self.thread = threading.Thread(target=reader, daemon=True)
+        self.thread.start()
+        return self
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=5)
+        sm, smax, power, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            try:
+                sm.append(float(r[1])); smax.append(float(r[2])); power.append(float(r[3]))
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "power_w_max": max(power) if power else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def physical_gpu_index(local: int) -> int:
+    cvd = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    parts = [p.strip() for p in cvd.split(",") if p.strip()]
+    if local < len(parts) and parts[local].isdigit():
+        return int(parts[local])
+    return local
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        if args.impl == "ours":
+            torch.cuda.set_device(local)
+        dist.init_process_group("nccl" if args.impl == "ours" else "gloo",
+                                timeout=datetime.timedelta(seconds=300))
+    elif args.impl == "ours":
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def timed(fn, steps: int, world: int, stream=None) -> float:
+    """Seconds for `steps` calls of fn(i), CUDA events on the launching stream, max over ranks."""
+    barrier(world)
+    torch.cuda.synchronize()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for i in range(steps):
+        fn(i)
+    e.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(s.elapsed_time(e) / 1e3, world)
+
+
+def event_time(fn, iters: int = 10, warmup: int = 3) -> float:
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(iters):
+        fn(i)
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / 1e3 / iters
+
+
+# ---------------------------------------------------------------------------- CPU reference path
+def cpu_reference_sample(M: int, N: int, K: int, sparsity: float, pattern: str, rows: int,
+                         budget_s: float, max_reps: int, seed: int = 0) -> dict:
+    """Time the oracle (numpy, all cores) on `rows` rows of the workload."""
+    from oracle import gw_oracle as O
+
+    try:
+        from threadpoolctl import threadpool_limits
+    except Exception:  # pragma: no cover
+        threadpool_limits = None
+    cores = os.cpu_count() or 1
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((rows, K), dtype=np.float32).astype(np.float16)
+    w_kn = (rng.standard_normal((K, N), dtype=np.float32) / np.sqrt(K)).astype(np.float16)
+    dead = dead_columns(K, sparsity, seed, pattern)
+    w_kn[dead, :] = 0
+    x[:, dead] = 0
+    idx = np.setdiff1d(np.arange(K), dead)
+    ctx = threadpool_limits(limits=cores) if threadpool_limits else None
+    try:
+        O.ghostweight_matmul(x, w_kn, idx)          # warm
+        times = []
+        t_end = time.perf_counter() + budget_s
+        while len(times) < max_reps and (not times or time.perf_counter() < t_end):
+            t0 = time.perf_counter()
+            O.ghostweight_matmul(x, w_kn, idx)
+            times.append(time.perf_counter() - t0)
+    finally:
+        if ctx is not None:
+            ctx.__exit__(None, None, None)
+    t = statistics.median(times)
+    flops = 2.0 * rows * N * len(idx)
+    return {"value": flops / t / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "seconds_per_sample": t, "reps": len(times),
+            "sample": f"{rows} of {M} rows of x through oracle.ghostweight_matmul "
+                      f"(fp32 gather + numpy sgemm over K'={len(idx)}, N={N}), median of {len(times)}"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    cfg = HEADLINE
+    rows = 256
+    steps_total = args.warmup + args.steps
+    # Bound the whole run to a few minutes: at most ~150 s of CPU work.
+    per_step_budget = max(0.05, 150.0 / max(1, steps_total))
+    res = cpu_reference_sample(cfg["M"], cfg["N"], cfg["K"], cfg["sparsity"], cfg["pattern"], rows,
+                               budget_s=per_step_budget * steps_total, max_reps=steps_total)
+    kp = cfg["K"] - int(cfg["K"] * cfg["sparsity"])
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(res["value"], 6), "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": res["reps"], "warmup": 1,
+        "ms_per_step": round(res["seconds_per_sample"] * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16 in, fp32 compute (CPU)",
+        "data": "synthetic (seeded N(0,1) activations, N(0,1/sqrt(K)) weight, dead columns zeroed)",
+        "config": {"workload": "gather-GEMM M=N=K=4096, 50% random dead input columns",
+                   "M": cfg["M"], "N": cfg["N"], "K": cfg["K"], "K_alive": kp,
+                   "sample_rows": rows},
+        "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": round(res["value"], 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------- ours: headline GEMM
+def build_layer(M, N, K, sparsity, pattern, dtype, seed, device):
+    from ghostweight_triton_b200.kernels.gather import pack_weight
+    from ghostweight_triton_b200.kernels.mask import alive_indices
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    w = (torch.randn(N, K, device=device, generator=g) / K ** 0.5).to(dtype)
+    x = torch.randn(M, K, device=device, generator=g).to(dtype)
+    dead = torch.from_numpy(dead_columns(K, sparsity, seed, pattern)).to(device)
+    w[:, dead] = 0
+    x[:, dead] = 0
+    idx = alive_indices(w, 0.0)
+    wp = pack_weight(w, idx)
+    y = torch.empty(M, N, device=device, dtype=dtype)
+    return dict(x=x, w=w, idx=idx, wp=wp, y=y)
+
+
+def kernel_metrics(device, peaks) -> dict:
+    """Mask (K1) and weight-packing (K2) achieved bandwidth on the headline weight."""
+    from ghostweight_triton_b200 import _native
+    from ghostweight_triton_b200.kernels.gather import pack_weight
+
+    out = {}
+    for name, (N, K, dt) in {"headline_weight_4096x4096_fp16": (4096, 4096, torch.float16),
+                             "mlp_weight_28672x8192_bf16": (28672, 8192, torch.bfloat16)}.items():
+        w = torch.randn(N, K, device=device).to(dt)
+        dead = torch.from_numpy(dead_columns(K, 0.5, 1, "random")).to(device)
+        w[:, dead] = 0
+        mask = torch.empty(K, dtype=torch.int32, device=device)
+        buf = torch.empty(K, dtype=torch.int64, device=device)
+        cnt = torch.empty(1, dtype=torch.int32, device=device)
+        t_mask = event_time(lambda i: _native.mask_compact(w, 0.0, mask, buf, cnt))
+        kp = int(cnt.item())
+        idx = buf[:kp]
+        t_pack = event_time(lambda i: pack_weight(w, idx))
+        esz = w.element_size()
+        mask_bytes = N * K * esz + K * 4 + kp * 8
+        pack_bytes = 2 * N * kp * esz
+        out[name] = {"mask_us": round(t_mask * 1e6, 2),
+                     "mask_GBps": round(mask_bytes / t_mask / 1e9, 1),
+                     "mask_frac_hbm": round(mask_bytes / t_mask / 1e9 / peaks["hbm_gbs"], 3),
+                     "pack_us": round(t_pack * 1e6, 2),
+                     "pack_GBps": round(pack_bytes / t_pack / 1e9, 1),
+                     "pack_frac_hbm": round(pack_bytes / t_pack / 1e9 / peaks["hbm_gbs"], 3),
+                     "K_alive": kp}
+        del w
+    torch.cuda.empty_cache()
+    return out
+
+
+def sweep(device, peaks) -> list[dict]:
+    """M in {4096, 1024, 128, 16} x sparsity x {random, block64}: ours vs dense cuBLAS."""
+    import torch.nn.functional as F
+
+    from ghostweight_triton_b200.kernels.matmul import ghost_linear
+
+    rows = []
+    K = N = 4096
+    for M in (4096, 1024, 128, 16):
+        for pattern in ("random", "block64"):
+            for sp in (0.0, 0.25, 0.5, 0.75, 0.9):
+                L = build_layer(M, N, K, sp, pattern, torch.float16, 100 + M, device)
+                kp = L["idx"].numel()
+                t = event_time(lambda i: ghost_linear(L["x"], L["wp"], L["idx"], out=L["y"]), iters=20)
+                td = event_time(lambda i: F.linear(L["x"], L["w"]), iters=20)
+                useful = 2.0 * M * N * kp
+                rows.append({"M": M, "pattern": pattern, "sparsity": sp, "K_alive": kp,
+                             "us": round(t * 1e6, 2), "useful_tflops": round(useful / t / 1e12, 1),
+                             "dense_equiv_tflops": round(2.0 * M * N * K / t / 1e12, 1),
+                             "frac_tensor_peak": round(useful / t / 1e12 / peaks["bf16_tflops"], 3),
+                             "cublas_dense_us": round(td * 1e6, 2),
+                             "speedup_vs_dense": round(td / t, 3), "ideal": round(K / kp, 3)})
+                del L
+    torch.cuda.empty_cache()
+    return rows
+
+
+def traffic_from_profiles() -> float | None:
+    p = REPO / "profiles" / "traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get("gather_gemm_headline_bytes_per_launch")
+        except Exception:
+            return None
+    return None
+
+
+def run_ours(args, world, rank, local):
+    from ghostweight_triton_b200 import GhostLinear
+
+    device = torch.device("cuda", torch.cuda.current_device())
+    peaks, peak_src = load_peaks()
+    cfg = HEADLINE
+    M, N, K = cfg["M"], cfg["N"], cfg["K"]
+    layers = [build_layer(M, N, K, cfg["sparsity"], cfg["pattern"], torch.float16,
+                          seed=1000 * rank + s, device=device) for s in range(N_SETS)]
+    kp = layers[0]["idx"].numel()
+    useful = 2.0 * M * N * kp
+
+    from ghostweight_triton_b200 import _native
+
+    # Product path: the two-launch pregather strategy (x[:, alive] -> scratch, then
+    # the TMA-fed tcgen05 GEMM); one scratch buffer serves every step in turn.
+    ws = torch.empty(_native.gather_gemm_workspace_bytes(M, kp, torch.float16), dtype=torch.uint8,
+                     device=device)
+    ldp = (kp + 63) // 64 * 64
+    xg = ws[: M * ldp * 2].view(torch.float16).view(M, ldp)[:, :kp]
+
+    def step(i):
+        L = layers[i % N_SETS]
+        _native.gather_gemm(L["x"], L["wp"], L["idx"], L["y"], strategy="pregather", workspace=ws)
+
+    def gemm_only(i):
+        L = layers[i % N_SETS]
+        _native.packed_gemm(xg, L["wp"], L["y"])
+
+    def gather_only(i):
+        L = layers[i % N_SETS]
+        _native.gather_columns(L["x"], L["idx"], xg)
+
+    # Warm-up, then a clock-sampled soak of ~1 s so the sampler sees the load,
+    # then exactly `steps` timed steps (the sampler keeps running through them).
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(physical_gpu_index(local)).start() if rank == 0 else None
+    t_soak = time.perf_counter()
+    n_soak = 0
+    while time.perf_counter() - t_soak < 1.0:
+        for i in range(200):
+            step(i)
+        n_soak += 200
+        torch.cuda.synchronize()
+    t = timed(step, args.steps, world)
+    clocks = sampler.stop() if sampler else None
+
+    per_step = t / args.steps
+    value = world * useful / per_step / 1e12
+    # Dominant kernel alone (tcgen05 GEMM on the gathered operand) and the gather alone.
+    t_gemm = timed(gemm_only, args.steps, world) / args.steps
+    t_gather = timed(gather_only, args.steps, world) / args.steps
+    achieved = useful / t_gemm / 1e12
+    gather_bytes = M * K * 2 + M * kp * 2 + kp * 8       # full rows read (50% random touches every sector) + x' written
+
+    # e2e through the public API: GhostLinear (frozen weight mask), pinned host x in, y out.
+    e2e = None
+    if not args.no_e2e:
+        gl = GhostLinear(K, N, bias=False, device=device, dtype=torch.float16)
+        with torch.no_grad():
+            gl.weight.copy_(layers[0]["w"])
+        gl.freeze_weight_mask()
+        hx = [L["x"].cpu().pin_memory() for L in layers]
+        hy = torch.empty(M, N, dtype=torch.float16).pin_memory()
+
+        def e2e_step(i):
+            xd = hx[i % N_SETS].to(device, non_blocking=True)
+            with torch.no_grad():
+                yd = gl(xd)
+            hy.copy_(yd, non_blocking=True)
+
+        for i in range(max(3, args.warmup)):
+            e2e_step(i)
+        e_steps = max(1, min(args.steps, 200))
+        te = timed(e2e_step, e_steps, world)
+        e2e = {"value": round(world * useful / (te / e_steps) / 1e12, 3), "unit": "TFLOP/s",
+               "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2,
+               "steps": e_steps, "ms_per_step": round(te / e_steps * 1e3, 4),
+               "path": "GhostLinear.forward (frozen weight mask) with pinned-host x -> device -> pinned-host y"}
+
+    extra = {}
+    cpu = None
+    if rank == 0 and world == 1:
+        if not args.no_sweep:
+            extra["sweep"] = sweep(device, peaks)
+            extra["kernels"] = kernel_metrics(device, peaks)
+        if not args.no_cpu_baseline:
+            r = cpu_reference_sample(M, N, K, cfg["sparsity"], cfg["pattern"], rows=256,
+                                     budget_s=15.0, max_reps=50)
+            cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            cpu["value"] = round(cpu["value"], 6)
+
+    if rank == 0:
+        peak = float(peaks["bf16_tflops"])
+        traffic = traffic_from_profiles()
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step * 1e3, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+            "data": "synthetic: x ~ N(0,1), W ~ N(0,1/sqrt(K)), 50% input columns zeroed (seeded uniform); random init",
+            "config": {"workload": "gather-GEMM M=N=K=4096 fp16, 50% random dead input columns (K'=2048)",
+                       "M": M, "N": N, "K": K, "K_alive": kp, "global_batch_rows": world * M,
+                       "parallelism": f"independent batches per GPU x{world}",
+                       "l2": f"{N_SETS} rotating layer sets (x, W', y) = {N_SETS * 80} MB > 126 MB L2",
+                       "soak_steps_before_timing": n_soak},
+            "dense_equiv_tflops": round(world * 2.0 * M * N * K / per_step / 1e12, 3),
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
+                         "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                         "peak_source": f"{peak_src} bf16_tflops (fp16 taken equal)",
+                         "traffic": traffic,
+                         "kernel": "gemm_tc_kernel<256, f16, TMA A> (csrc/gw_gemm_tc.cu), timed alone"},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "clocks": clocks,
+            "gpu_launches": 2 * args.steps,
+            "step_kernels": {"gather_us": round(t_gather * 1e6, 2),
+                             "gather_GBps": round(gather_bytes / t_gather / 1e9, 1),
+                             "gather_frac_hbm": round(gather_bytes / t_gather / 1e9 / float(peaks["hbm_gbs"]), 3),
+                             "gemm_us": round(t_gemm * 1e6, 2),
+                             "gemm_useful_tflops": round(achieved, 2),
+                             "step_us": round(per_step * 1e6, 2)},
+            "strategy": "pregather (gather launch + TMA tcgen05 GEMM launch)",
+        }
+        line.update(extra)
+        print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------- ours: sharded MLP
+def run_mlp_sharded(args, world, rank, local):
+    from ghostweight_triton_b200.sharded import ColumnParallelGhostLinear
+
+    device = torch.device("cuda", torch.cuda.current_device())
+    peaks, peak_src = load_peaks()
+    cfg = MLP
+    M, N, K = cfg["M"], cfg["N"], cfg["K"]
+    g = torch.Generator(device=device).manual_seed(5)
+    x = torch.randn(M, K, device=device, generator=g).to(torch.bfloat16)
+    layer = ColumnParallelGhostLinear.from_full_weight_seed(
+        N, K, seed=5, dead=dead_columns(K, cfg["sparsity"], 5, cfg["pattern"]),
+        dtype=torch.bfloat16, device=device)
+    kp = layer.k_alive
+    useful = 2.0 * M * N * kp
+
+    def step_gemm(i):
+        layer.local_forward(x)
+
+    def step_full(i):
+        layer(x)
+
+    for i in range(args.warmup):
+        step_full(i)
+    t_gemm = timed(step_gemm, args.steps, world)
+    t_full = timed(step_full, args.steps, world)
+    if rank == 0:
+        per = t_full / args.steps
+        line = {
+            "metric": METRIC, "value": round(useful / per / 1e12, 3), "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(per * 1e3, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic, seeded",
+            "config": {"workload": "sharded MLP projection x[8192,8192] W[28672,8192] bf16, 70% dead 128-col blocks",
+                       "K_alive": kp, "parallelism": f"column-parallel N over {world} GPUs + NCCL all-gather"},
+            "gemm_only_tflops": round(useful / (t_gemm / args.steps) / 1e12, 3),
+            "gemm_only_ms": round(t_gemm / args.steps * 1e3, 4),
+            "roofline": {"bound": "tensor", "achieved": round(useful / world / (t_gemm / args.steps) / 1e12, 2),
+                         "peak": float(peaks["bf16_tflops"]), "unit": "TFLOP/s",
+                         "frac": round(useful / world / (t_gemm / args.steps) / 1e12 / float(peaks["bf16_tflops"]), 4),
+                         "peak_source": peak_src, "traffic": None},
+            "gpu_launches": args.steps,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["gemm", "mlp-sharded"], default="gemm")
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    world, rank, local = dist_setup(args)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        elif args.workload == "gemm":
+            run_ours(args, world, rank, local)
+        else:
+            run_mlp_sharded(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -31,6 +31,7 @@ GW_ERR_WORKSPACE = 5
 GW_ERR_CUDA = 6
 GW_ERR_DEVICE = 7
 GW_ERR_UNSUPPORTED = 8
+GEMM_STRATEGIES = {"auto": 0, "fused": 1, "pregather": 2}
 DEVICE_ERR_WAIT_TIMEOUT = 1
 DEVICE_ERR_BAD_INDEX = 2
 
@@ -47,8 +48,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gw_gather_columns": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _vp]),
     "gw_gather_rows": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _vp]),
     "gw_gather_rows_t": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _vp]),
+    "gw_gather_gemm_workspace_bytes": (_sz, [_i64, _i64, _i]),
     "gw_gather_gemm": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _i,
-                            _vp, _i64, _vp]),
+                            _vp, _i64, _i, _vp, _sz, _vp]),
     "gw_packed_gemm": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i, _vp, _i64, _vp]),
     "gw_validate_indices": (_i, [_vp, _i64, _i64, _vp, _vp]),
 }
@@ -230,19 +232,30 @@ def gather_rows_t(src: torch.Tensor, idx: torch.Tensor, dst: torch.Tensor, pad_t
     _check(st, "gw_gather_rows_t")
 
 
+def gather_gemm_workspace_bytes(M: int, n_alive: int, dtype: torch.dtype) -> int:
+    return int(load().gw_gather_gemm_workspace_bytes(int(M), int(n_alive), dtype_code(dtype)))
+
+
 def gather_gemm(x: torch.Tensor, w_packed: torch.Tensor, idx: torch.Tensor, y: torch.Tensor,
-                bias: torch.Tensor | None = None, activation: str | None = None) -> None:
-    """y = act(x[:, idx] @ w_packed[:, :len(idx)]^T + bias) on the current stream."""
+                bias: torch.Tensor | None = None, activation: str | None = None,
+                strategy: str = "auto", workspace: torch.Tensor | None = None) -> None:
+    """y = act(x[:, idx] @ w_packed[:, :len(idx)]^T + bias) on the current stream.
+
+    strategy "auto" uses the two-launch pregather path when `workspace` is large
+    enough, else the single fused kernel; "fused" / "pregather" force one.
+    """
     _rowmajor(x, w_packed, y)
     assert idx.dtype == torch.int64 and idx.is_contiguous()
     M, K = x.shape
     N = w_packed.shape[0]
     n = idx.numel()
+    ws_ptr, ws_bytes = (None, 0) if workspace is None else (workspace.data_ptr(), workspace.numel() * workspace.element_size())
     with _on_device(x.device):
         st = load().gw_gather_gemm(
             _ptr(x), dtype_code(x.dtype), M, K, max(x.stride(0), K), _ptr(w_packed), N,
             max(w_packed.stride(0), n), _ptr(idx), n, _ptr(bias), epilogue_code(activation),
-            _ptr(y), max(y.stride(0), N), _stream(x.device))
+            _ptr(y), max(y.stride(0), N), GEMM_STRATEGIES[strategy], ws_ptr, ws_bytes,
+            _stream(x.device))
     _check(st, "gw_gather_gemm")
 
 

@@ -219,12 +219,20 @@ int gw_gather_rows_t(const void* src, int dtype, int64_t rows, int64_t cols, int
   return e == cudaSuccess ? GW_OK : cuda_fail(e);
 }
 
+size_t gw_gather_gemm_workspace_bytes(int64_t M, int64_t n_alive, int dtype) {
+  if (M <= 0 || n_alive <= 0 || dtype == GW_DTYPE_F32) return 0;
+  const int64_t ld = (n_alive + 63) / 64 * 64;   // gathered rows start 128-byte aligned
+  return static_cast<size_t>((M * ld * 2 + 255) / 256 * 256);
+}
+
 int gw_gather_gemm(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
                    const void* w_packed, int64_t N, int64_t ldw, const int64_t* idx,
                    int64_t n_alive, const void* bias, int epilogue, void* y, int64_t ldy,
-                   void* stream) {
+                   int strategy, void* workspace, size_t workspace_bytes, void* stream) {
   if (!valid_dtype(dtype)) return GW_ERR_DTYPE;
   if (!valid_epi(epilogue)) return GW_ERR_UNSUPPORTED;
+  if (strategy != GW_GEMM_AUTO && strategy != GW_GEMM_FUSED && strategy != GW_GEMM_PREGATHER)
+    return GW_ERR_UNSUPPORTED;
   if (!matrix_ok(M, K, ldx) || n_alive < 0 || !matrix_ok(N, n_alive, ldw) ||
       !matrix_ok(M, N, ldy))
     return GW_ERR_SHAPE;
@@ -245,9 +253,24 @@ int gw_gather_gemm(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
                             static_cast<const float*>(w_packed), N, ldw, idx, n_alive,
                             static_cast<const float*>(bias), epilogue, static_cast<float*>(y),
                             ldy, d->err_word, s);
+    return e == cudaSuccess ? GW_OK : cuda_fail(e);
+  }
+  if (!aligned16(w_packed) || (ldw % 8) != 0) return GW_ERR_ALIGN;
+  if (n_alive > 0x7FFFFFFFll - 64) return GW_ERR_SHAPE;
+  const size_t need = gw_gather_gemm_workspace_bytes(M, n_alive, dtype);
+  const bool ws_ok = workspace != nullptr && workspace_bytes >= need;
+  bool pregather = (strategy == GW_GEMM_PREGATHER) || (strategy == GW_GEMM_AUTO && ws_ok);
+  if (pregather) {
+    if (!workspace) return GW_ERR_NULL;
+    if (!ws_ok) return GW_ERR_WORKSPACE;
+    if (!aligned16(workspace)) return GW_ERR_ALIGN;
+    const int64_t ldp = (n_alive + 63) / 64 * 64;
+    e = gw::launch_gather_columns(x, dtype, M, ldx, K, idx, n_alive, workspace, ldp, n_alive,
+                                  d->err_word, d->sm_count, s);
+    if (e != cudaSuccess) return cuda_fail(e);
+    e = gw::launch_gemm_tc(false, workspace, dtype, M, n_alive, ldp, w_packed, N, ldw, nullptr,
+                           n_alive, bias, epilogue, y, ldy, d->err_word, d->sm_count, s);
   } else {
-    if (!aligned16(w_packed) || (ldw % 8) != 0) return GW_ERR_ALIGN;
-    if (n_alive > 0x7FFFFFFFll - 64) return GW_ERR_SHAPE;
     e = gw::launch_gemm_tc(true, x, dtype, M, K, ldx, w_packed, N, ldw, idx, n_alive, bias,
                            epilogue, y, ldy, d->err_word, d->sm_count, s);
   }

@@ -5,9 +5,12 @@ C[M, N] = A[:, alive] @ W[alive, :] with fp32 accumulation, cast to A's dtype;
 unsorted or repeated indices are fine and an empty index list gives zeros.
 On B200 the weight rows are first packed into the K'-major operand (one
 transposing gather) and the product runs on the tcgen05 kernel K3
-(csrc/gw_gemm_tc.cu), whose producer warps gather the alive activation columns
-straight into shared memory. fp32 inputs use the exact-fp32 kernel, matching
-the reference's TF32-off choice for fp32 (matmul.py:127-130).
+(csrc/gw_gemm_tc.cu). Two strategies feed its A operand: "pregather" gathers
+the alive activation columns into a dense scratch matrix and streams both
+operands by TMA (two launches; the default when a workspace is affordable),
+"fused" has producer warps gather them straight into shared memory (one
+launch, no scratch). fp32 inputs use the exact-fp32 kernel, matching the
+reference's TF32-off choice for fp32 (matmul.py:127-130).
 
 ``ghost_linear`` is the module-level entry: activations [M, K] times an
 already packed weight, with bias and optional GELU fused into the epilogue.
@@ -31,6 +34,7 @@ def ghostweight_matmul(
     *,
     bias: torch.Tensor | None = None,
     activation: str | None = None,
+    strategy: str = "auto",
 ) -> torch.Tensor:
     """Sparse matmul that skips dead neurons.
 
@@ -42,6 +46,7 @@ def ghostweight_matmul(
     BLOCK_M, BLOCK_N, BLOCK_K : accepted for signature compatibility; ignored.
     bias          : optional [N], added in the fp32 epilogue (extension).
     activation    : None, "gelu" or "gelu_tanh", applied after the bias (extension).
+    strategy      : "auto" | "pregather" | "fused" (extension, see module docstring).
 
     Returns
     -------
@@ -62,8 +67,18 @@ def ghostweight_matmul(
     w_packed = pack_weight(weights.t(), alive_indices, dtype=activations.dtype)
     if bias is not None:
         bias = bias.contiguous().to(dtype=activations.dtype)
-    _native.gather_gemm(activations, w_packed, alive_indices, C, bias=bias, activation=activation)
+    _gemm(activations, w_packed, alive_indices, C, bias, activation, strategy)
     return C
+
+
+def _gemm(x, w_packed, idx, y, bias, activation, strategy):
+    ws = None
+    if strategy != "fused" and x.dtype != torch.float32:
+        nbytes = _native.gather_gemm_workspace_bytes(x.shape[0], idx.numel(), x.dtype)
+        if nbytes:
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+    _native.gather_gemm(x, w_packed, idx, y, bias=bias, activation=activation,
+                        strategy=strategy, workspace=ws)
 
 
 def ghost_linear(
@@ -73,6 +88,7 @@ def ghost_linear(
     bias: torch.Tensor | None = None,
     activation: str | None = None,
     out: torch.Tensor | None = None,
+    strategy: str = "auto",
 ) -> torch.Tensor:
     """y = act(x[:, alive] @ w_packed^T + bias) for x [M, K], w_packed [N, K_alive]."""
     assert x.ndim == 2 and x.is_cuda
@@ -81,7 +97,7 @@ def ghost_linear(
     N = w_packed.shape[0]
     y = out if out is not None else torch.empty((M, N), dtype=x.dtype, device=x.device)
     if M and N:
-        _native.gather_gemm(x, w_packed, alive_indices, y, bias=bias, activation=activation)
+        _gemm(x, w_packed, alive_indices, y, bias, activation, strategy)
     return y
 
 

@@ -1,0 +1,145 @@
+"""Column-parallel GhostLinear: output features split across ranks.
+
+For layers too large for one GPU's share of a job (e.g. an MLP up-projection
+x [8192, 8192] -> [8192, 28672]), rank r holds the pre-sharded weight rows
+W[r*n : (r+1)*n, :] and bias slice; x is replicated. Each rank:
+
+  1. computes the dead-column mask of its own shard with K1 and takes the
+     union over ranks (all_reduce MAX of the int32 [K] mask, K*4 bytes), so
+     every rank uses the same alive list -- exactly the list the full weight
+     would give (a column is dead in W iff it is dead in every shard);
+  2. packs its shard's alive columns once (K2);
+  3. runs the tcgen05 gather-GEMM on its rows (K3) -> y_r [M, n];
+  4. if the next op needs full rows, all-gathers y (NCCL over NVLink) into
+     [world, M, n] and re-lays it out to [M, N].
+
+The reference has no multi-GPU code; this is the sharded configuration of the
+same hot path. Uneven splits pad the last shard with zero rows.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from ghostweight_triton_b200.kernels.gather import pack_weight
+from ghostweight_triton_b200.kernels.mask import dead_neuron_mask_compact
+from ghostweight_triton_b200.kernels.matmul import ghost_linear
+
+
+def shard_rows(n_total: int, world: int, rank: int) -> tuple[int, int, int]:
+    """(start, stop, padded) rows owned by `rank`; every rank pads to `padded` rows."""
+    padded = -(-n_total // world)
+    start = min(rank * padded, n_total)
+    stop = min(start + padded, n_total)
+    return start, stop, padded
+
+
+def union_mask(mask: torch.Tensor, group=None) -> torch.Tensor:
+    """Element-wise OR of int32 0/1 masks over the group (in place, returns mask)."""
+    if dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(mask, op=dist.ReduceOp.MAX, group=group)
+    return mask
+
+
+def gather_columns_from_ranks(y_local: torch.Tensor, n_total: int, group=None,
+                              out: torch.Tensor | None = None) -> torch.Tensor:
+    """All-gather row-major [M, n] shards into [M, n_total] (shard r -> columns r*n ..)."""
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    if world == 1:
+        return y_local[:, :n_total]
+    M, n = y_local.shape
+    buf = torch.empty((world * M, n), dtype=y_local.dtype, device=y_local.device)
+    dist.all_gather_into_tensor(buf, y_local.contiguous(), group=group)
+    full = buf.view(world, M, n).permute(1, 0, 2).reshape(M, world * n)
+    if out is None:
+        return full[:, :n_total].contiguous()
+    out.copy_(full[:, :n_total])
+    return out
+
+
+class ColumnParallelGhostLinear(nn.Module):
+    """GhostLinear whose output features are split across the ranks of `group`."""
+
+    def __init__(self, in_features: int, out_features: int, bias: bool = True,
+                 threshold: float = 0.0, gather_output: bool = True, group=None,
+                 device=None, dtype=None):
+        super().__init__()
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.in_features = in_features
+        self.out_features = out_features
+        self.threshold = threshold
+        self.gather_output = gather_output
+        self.row_start, self.row_stop, self.n_local = shard_rows(out_features, self.world, self.rank)
+        factory = {"device": device, "dtype": dtype}
+        self.weight = nn.Parameter(torch.zeros(self.n_local, in_features, **factory))
+        self.bias = nn.Parameter(torch.zeros(self.n_local, **factory)) if bias else None
+        self.alive: torch.Tensor | None = None
+        self.w_packed: torch.Tensor | None = None
+
+    @property
+    def k_alive(self) -> int:
+        return -1 if self.alive is None else int(self.alive.numel())
+
+    # ------------------------------------------------------------------ construction
+    @classmethod
+    def from_full_weight(cls, weight: torch.Tensor, bias: torch.Tensor | None = None,
+                         threshold: float = 0.0, gather_output: bool = True, group=None,
+                         device=None) -> "ColumnParallelGhostLinear":
+        """Take this rank's rows of a full [N, K] weight (and bias) and freeze the mask."""
+        N, K = weight.shape
+        dev = device if device is not None else weight.device
+        m = cls(K, N, bias=bias is not None, threshold=threshold, gather_output=gather_output,
+                group=group, device=dev, dtype=weight.dtype)
+        rows = m.row_stop - m.row_start
+        with torch.no_grad():
+            m.weight[:rows].copy_(weight[m.row_start:m.row_stop])
+            if bias is not None:
+                m.bias[:rows].copy_(bias[m.row_start:m.row_stop])
+        m.freeze_weight_mask()
+        return m
+
+    @classmethod
+    def from_full_weight_seed(cls, out_features: int, in_features: int, seed: int,
+                              dead: np.ndarray, dtype: torch.dtype, device,
+                              group=None) -> "ColumnParallelGhostLinear":
+        """Pre-sharded synthetic weight: each rank draws only its rows, N(0, 1/sqrt(K)),
+        with the global dead columns zeroed (benchmarks; no full weight is built)."""
+        m = cls(in_features, out_features, bias=False, threshold=0.0, group=group,
+                device=device, dtype=dtype)
+        g = torch.Generator(device=device).manual_seed(seed * 1009 + m.rank)
+        rows = m.row_stop - m.row_start
+        with torch.no_grad():
+            w = torch.randn(rows, in_features, device=device, generator=g) / in_features ** 0.5
+            w[:, torch.from_numpy(np.asarray(dead)).to(device)] = 0
+            m.weight[:rows].copy_(w.to(dtype))
+        m.freeze_weight_mask()
+        return m
+
+    # ------------------------------------------------------------------ mask
+    def freeze_weight_mask(self) -> None:
+        """Alive columns = union over ranks of each shard's |W| column mask."""
+        with torch.no_grad():
+            mask, _, _ = dead_neuron_mask_compact(self.weight.detach(), self.threshold)
+            union_mask(mask, self.group)
+            self.alive = torch.nonzero(mask, as_tuple=False).squeeze(-1).to(torch.int64)
+            self.w_packed = pack_weight(self.weight.detach(), self.alive)
+
+    # ------------------------------------------------------------------ forward
+    def local_forward(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """This rank's output columns y[:, start:start+n_local] (padded rows included)."""
+        assert self.alive is not None, "call freeze_weight_mask() first"
+        x2 = x.reshape(-1, self.in_features)
+        return ghost_linear(x2, self.w_packed, self.alive, bias=self.bias, out=out)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        lead = x.shape[:-1]
+        y = self.local_forward(x)
+        if not self.gather_output:
+            return y.reshape(*lead, self.n_local)
+        full = gather_columns_from_ranks(y, self.out_features, self.group)
+        return full.reshape(*lead, self.out_features)

@@ -157,11 +157,27 @@ GW_API int gw_gather_rows_t(const void* src, int dtype, int64_t rows, int64_t co
  * fp16/bf16 run on tcgen05 tensor cores (requires ldw % 8 == 0 and a 16-byte
  * aligned w_packed); fp32 runs an exact-fp32 FFMA kernel (no TF32), as the
  * reference disables TF32 for fp32 (matmul.py:127-130).
+ *
+ * strategy (fp16/bf16 only):
+ *   GW_GEMM_AUTO      pregather when a large-enough workspace is given, else fused;
+ *   GW_GEMM_FUSED     one kernel: producer warps gather x[:, idx] into shared memory;
+ *   GW_GEMM_PREGATHER two launches: x[:, idx] -> workspace (dense [M, K'_pad]),
+ *                     then the GEMM with both operands loaded by TMA.
+ * workspace: device scratch of at least gw_gather_gemm_workspace_bytes(M, n_alive,
+ * dtype) bytes, 16-byte aligned (may be NULL for GW_GEMM_FUSED / fp32). Its
+ * contents on entry do not matter; concurrent calls must not share it.
  */
+typedef enum {
+  GW_GEMM_AUTO = 0,
+  GW_GEMM_FUSED = 1,
+  GW_GEMM_PREGATHER = 2
+} gw_gemm_strategy;
+
+GW_API size_t gw_gather_gemm_workspace_bytes(int64_t M, int64_t n_alive, int dtype);
 GW_API int gw_gather_gemm(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
                           const void* w_packed, int64_t N, int64_t ldw, const int64_t* idx,
                           int64_t n_alive, const void* bias, int epilogue, void* y, int64_t ldy,
-                          void* stream);
+                          int strategy, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Dense GEMM over an already-compacted activation (the two-step path of

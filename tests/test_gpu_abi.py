@@ -34,21 +34,30 @@ def test_shape_dtype_null_errors(lib):
     idx = torch.arange(64, device="cuda")
     s = stream()
     ok = lib.gw_gather_gemm(x.data_ptr(), 0, 8, 64, 64, w.data_ptr(), 32, 64, idx.data_ptr(), 64,
-                            None, 0, y.data_ptr(), 32, s)
+                            None, 0, y.data_ptr(), 32, 1, None, 0, s)
     assert ok == _native.GW_OK
     assert lib.gw_gather_gemm(x.data_ptr(), 7, 8, 64, 64, w.data_ptr(), 32, 64, idx.data_ptr(), 64,
-                              None, 0, y.data_ptr(), 32, s) == _native.GW_ERR_DTYPE
+                              None, 0, y.data_ptr(), 32, 1, None, 0, s) == _native.GW_ERR_DTYPE
     assert lib.gw_gather_gemm(x.data_ptr(), 0, 8, 64, 10, w.data_ptr(), 32, 64, idx.data_ptr(), 64,
-                              None, 0, y.data_ptr(), 32, s) == _native.GW_ERR_SHAPE
+                              None, 0, y.data_ptr(), 32, 1, None, 0, s) == _native.GW_ERR_SHAPE
     assert lib.gw_gather_gemm(x.data_ptr(), 0, 8, 64, 64, w.data_ptr(), 32, 64, idx.data_ptr(), 64,
-                              None, 9, y.data_ptr(), 32, s) == _native.GW_ERR_UNSUPPORTED
+                              None, 9, y.data_ptr(), 32, 1, None, 0, s) == _native.GW_ERR_UNSUPPORTED
     assert lib.gw_gather_gemm(x.data_ptr(), 0, 8, 64, 64, w.data_ptr(), 32, 64, None, 64,
-                              None, 0, y.data_ptr(), 32, s) == _native.GW_ERR_NULL
+                              None, 0, y.data_ptr(), 32, 1, None, 0, s) == _native.GW_ERR_NULL
     # packed weight with ldw % 8 != 0 cannot be a TMA operand
     assert lib.gw_gather_gemm(x.data_ptr(), 0, 8, 64, 64, w.data_ptr(), 32, 65, idx.data_ptr(), 64,
-                              None, 0, y.data_ptr(), 32, s) == _native.GW_ERR_ALIGN
+                              None, 0, y.data_ptr(), 32, 1, None, 0, s) == _native.GW_ERR_ALIGN
     assert lib.gw_packed_gemm(x.data_ptr(), 2, 8, 64, 64, w.data_ptr(), 32, 64, None, 0,
                               y.data_ptr(), 32, s) == _native.GW_ERR_DTYPE
+    # pregather without a (large enough) workspace
+    assert lib.gw_gather_gemm(x.data_ptr(), 0, 8, 64, 64, w.data_ptr(), 32, 64, idx.data_ptr(), 64,
+                              None, 0, y.data_ptr(), 32, 2, None, 0, s) == _native.GW_ERR_NULL
+    ws = torch.empty(64, dtype=torch.uint8, device="cuda")
+    assert lib.gw_gather_gemm(x.data_ptr(), 0, 8, 64, 64, w.data_ptr(), 32, 64, idx.data_ptr(), 64,
+                              None, 0, y.data_ptr(), 32, 2, ws.data_ptr(), 64, s) == _native.GW_ERR_WORKSPACE
+    assert lib.gw_gather_gemm(x.data_ptr(), 0, 8, 64, 64, w.data_ptr(), 32, 64, idx.data_ptr(), 64,
+                              None, 0, y.data_ptr(), 32, 7, None, 0, s) == _native.GW_ERR_UNSUPPORTED
+    assert lib.gw_gather_gemm_workspace_bytes(8, 64, 0) == 1024
     torch.cuda.synchronize()
 
 

@@ -69,7 +69,8 @@ def test_golden_matmul(name):
     (1024, 2048, 1024, 0.5, "random"), (16, 4096, 4096, 0.5, "random"), (77, 130, 33, 0.1, "random"),
 ])
 @pytest.mark.parametrize("bias,act", [(False, None), (True, None), (True, "gelu"), (True, "gelu_tanh")])
-def test_ghost_linear_vs_oracle(dt, M, K, N, sp, pattern, bias, act):
+@pytest.mark.parametrize("strategy", ["pregather", "fused"])
+def test_ghost_linear_vs_oracle(dt, M, K, N, sp, pattern, bias, act, strategy):
     seed = M + 3 * K + 7 * N
     x = rand_matrix((M, K), seed, dt, 0.5)
     w = rand_matrix((N, K), seed + 1, dt, 1.0 / np.sqrt(K))
@@ -77,7 +78,8 @@ def test_ghost_linear_vs_oracle(dt, M, K, N, sp, pattern, bias, act):
     idx = alive_from_dead(K, dead_columns(K, sp, seed, pattern, 64))
     ref = O.ghost_linear(x, w, idx, b, act, dtype=dt)
     xd, wd, idd = to_dev(x), to_dev(w), torch.from_numpy(idx).cuda()
-    y = ghost_linear(xd, pack_weight(wd, idd), idd, bias=to_dev(b) if bias else None, activation=act)
+    y = ghost_linear(xd, pack_weight(wd, idd), idd, bias=to_dev(b) if bias else None, activation=act,
+                     strategy=strategy)
     assert y.dtype == DT[dt] and y.shape == (M, N)
     assert_close(to_np(y), ref, dt, f"{dt} {M}x{K}x{N} s={sp} bias={bias} act={act}")
 
@@ -212,7 +214,8 @@ class TestReferenceSuite:
 @pytest.mark.parametrize("M", [4096, 1024, 128, 16])
 @pytest.mark.parametrize("sp,pattern", [(0.0, "random"), (0.5, "random"), (0.9, "random"),
                                         (0.75, "block")])
-def test_gemm_sweep_size_vs_dense_fp32(M, sp, pattern):
+@pytest.mark.parametrize("strategy", ["pregather", "fused"])
+def test_gemm_sweep_size_vs_dense_fp32(M, sp, pattern, strategy):
     """M x 4096 x 4096 fp16: sparse result equals the dense fp32 product of the zeroed weight."""
     K = N = 4096
     g = torch.Generator(device="cuda").manual_seed(M)
@@ -224,7 +227,7 @@ def test_gemm_sweep_size_vs_dense_fp32(M, sp, pattern):
 
     idx = alive_indices(w, 0.0)
     assert idx.numel() == K - dead.numel()
-    y = ghost_linear(x, pack_weight(w, idx), idx)
+    y = ghost_linear(x, pack_weight(w, idx), idx, strategy=strategy)
     ref = F.linear(x.float(), w.float()).half()
     torch.testing.assert_close(y, ref, **tols(torch.float16))
 
