@@ -45,6 +45,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gw_get_device_error": (_i, [_i, ctypes.POINTER(ctypes.c_uint)]),
     "gw_mask_workspace_bytes": (_sz, [_i64]),
     "gw_mask_compact": (_i, [_vp, _i, _i64, _i64, _i64, _d, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "gw_mask_compact_static": (_i, [_vp, _i, _i64, _i64, _i64, _d, _vp, _vp, _vp, _vp]),
     "gw_gather_columns": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _vp]),
     "gw_gather_rows": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _vp]),
     "gw_gather_rows_t": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _vp]),

@@ -108,6 +108,34 @@ GW_API int gw_mask_compact(const void* x, int dtype, int64_t rows, int64_t cols,
                            void* stream);
 
 /*
+ * Allocation-free variant of gw_mask_compact. It has no counterpart in the
+ * reference, which allocates its outputs with torch on every call.
+ *
+ * For callers that must not allocate device memory after start-up: servers
+ * that reserve all device memory in advance and count any later cudaMalloc as
+ * a failure, plugins whose host process owns every allocation, and code that
+ * runs inside an allocator callback. Same inputs, outputs and semantics as
+ * gw_mask_compact, but the scratch lives in a static device array inside the
+ * library (about 128 KiB per GPU that loads it, held until the process exits),
+ * so no workspace argument is needed and nothing is allocated.
+ *
+ * Limits and rules:
+ *   - cols must be <= GW_MASK_STATIC_MAX_COLS, otherwise GW_ERR_WORKSPACE is
+ *     returned and nothing is launched;
+ *   - the first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture;
+ *   - every call on a device shares the one array and clears the part it uses
+ *     (cudaMemsetAsync) before launching, so calls that overlap on the GPU
+ *     (different streams, no ordering between them) race: order them on one
+ *     stream or use gw_mask_compact with separate workspaces.
+ */
+#define GW_MASK_STATIC_MAX_COLS 1048576
+GW_API int gw_mask_compact_static(const void* x, int dtype, int64_t rows, int64_t cols,
+                                  int64_t ld, double threshold, int32_t* mask,
+                                  int64_t* alive_idx, int32_t* alive_count, void* stream);
+
+/*
  * Column gather: dst[r, j] = src[r, idx[j]] for j < n_idx, and dst[r, j] = 0
  * for n_idx <= j < pad_to (pad_to <= ld_dst; pass pad_to = n_idx for no padding).
  *
