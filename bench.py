@@ -343,12 +343,12 @@ def sweep(device, peaks) -> list[dict]:
 
 
 def traffic_from_profiles() -> float | None:
-    p = REPO / "profiles" / "traffic.json"
+    """DRAM bytes (read + write) per launch of the headline GEMM from the committed ncu summary."""
+    p = REPO / "profiles" / "gemm_tc_tma_4096x4096x2048_fp16.md"
     if p.exists():
-        try:
-            return json.loads(p.read_text()).get("gather_gemm_headline_bytes_per_launch")
-        except Exception:
-            return None
+        for line in p.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1])
     return None
 
 
@@ -393,7 +393,7 @@ def run_ours(args, world, rank, local):
     sampler = ClockSampler(physical_gpu_index(local)).start() if rank == 0 else None
     t_soak = time.perf_counter()
     n_soak = 0
-    while time.perf_counter() - t_soak < 1.0:
+    while not args.no_soak and time.perf_counter() - t_soak < 1.0:
         for i in range(200):
             step(i)
         n_soak += 200
@@ -537,6 +537,8 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-soak", action="store_true",
+                    help="skip the 1 s clock-sampling soak (for short profiler runs)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     world, rank, local = dist_setup(args)
