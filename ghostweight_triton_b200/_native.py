@@ -31,7 +31,7 @@ GW_ERR_WORKSPACE = 5
 GW_ERR_CUDA = 6
 GW_ERR_DEVICE = 7
 GW_ERR_UNSUPPORTED = 8
-GEMM_STRATEGIES = {"auto": 0, "fused": 1, "pregather": 2}
+GEMM_STRATEGIES = {"auto": 0, "fused": 1, "pregather": 2, "overlap": 3}
 DEVICE_ERR_WAIT_TIMEOUT = 1
 DEVICE_ERR_BAD_INDEX = 2
 

@@ -219,10 +219,19 @@ int gw_gather_rows_t(const void* src, int dtype, int64_t rows, int64_t cols, int
   return e == cudaSuccess ? GW_OK : cuda_fail(e);
 }
 
+namespace {
+// GEMM workspace layout: [k-block ready counters, 256-aligned][x' = M x ldp, 16-bit]
+int64_t gemm_ld_pad(int64_t n_alive) { return (n_alive + 63) / 64 * 64; }
+size_t gemm_ws_header(int64_t n_alive) {
+  const size_t kb = static_cast<size_t>((n_alive + 63) / 64);
+  return (kb * sizeof(unsigned int) + 255) / 256 * 256;
+}
+}  // namespace
+
 size_t gw_gather_gemm_workspace_bytes(int64_t M, int64_t n_alive, int dtype) {
   if (M <= 0 || n_alive <= 0 || dtype == GW_DTYPE_F32) return 0;
-  const int64_t ld = (n_alive + 63) / 64 * 64;   // gathered rows start 128-byte aligned
-  return static_cast<size_t>((M * ld * 2 + 255) / 256 * 256);
+  return gemm_ws_header(n_alive) +
+         static_cast<size_t>((M * gemm_ld_pad(n_alive) * 2 + 255) / 256 * 256);
 }
 
 int gw_gather_gemm(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
@@ -231,7 +240,8 @@ int gw_gather_gemm(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
                    int strategy, void* workspace, size_t workspace_bytes, void* stream) {
   if (!valid_dtype(dtype)) return GW_ERR_DTYPE;
   if (!valid_epi(epilogue)) return GW_ERR_UNSUPPORTED;
-  if (strategy != GW_GEMM_AUTO && strategy != GW_GEMM_FUSED && strategy != GW_GEMM_PREGATHER)
+  if (strategy != GW_GEMM_AUTO && strategy != GW_GEMM_FUSED && strategy != GW_GEMM_PREGATHER &&
+      strategy != GW_GEMM_OVERLAP)
     return GW_ERR_UNSUPPORTED;
   if (!matrix_ok(M, K, ldx) || n_alive < 0 || !matrix_ok(N, n_alive, ldw) ||
       !matrix_ok(M, N, ldy))
@@ -259,20 +269,32 @@ int gw_gather_gemm(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
   if (n_alive > 0x7FFFFFFFll - 64) return GW_ERR_SHAPE;
   const size_t need = gw_gather_gemm_workspace_bytes(M, n_alive, dtype);
   const bool ws_ok = workspace != nullptr && workspace_bytes >= need;
-  bool pregather = (strategy == GW_GEMM_PREGATHER) || (strategy == GW_GEMM_AUTO && ws_ok);
-  if (pregather) {
-    if (!workspace) return GW_ERR_NULL;
-    if (!ws_ok) return GW_ERR_WORKSPACE;
-    if (!aligned16(workspace)) return GW_ERR_ALIGN;
-    const int64_t ldp = (n_alive + 63) / 64 * 64;
-    e = gw::launch_gather_columns(x, dtype, M, ldx, K, idx, n_alive, workspace, ldp, n_alive,
+  int strat = strategy;
+  if (strat == GW_GEMM_AUTO) strat = ws_ok ? GW_GEMM_PREGATHER : GW_GEMM_FUSED;
+  if (strat == GW_GEMM_FUSED) {
+    e = gw::launch_gemm_tc(1, x, dtype, M, K, ldx, w_packed, N, ldw, idx, n_alive, bias,
+                           epilogue, y, ldy, d->err_word, d->sm_count, s);
+    return e == cudaSuccess ? GW_OK : cuda_fail(e);
+  }
+  if (!workspace) return GW_ERR_NULL;
+  if (!ws_ok) return GW_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return GW_ERR_ALIGN;
+  const int64_t ldp = gemm_ld_pad(n_alive);
+  unsigned int* counters = static_cast<unsigned int*>(workspace);
+  void* xg = static_cast<char*>(workspace) + gemm_ws_header(n_alive);
+  if (strat == GW_GEMM_PREGATHER) {
+    e = gw::launch_gather_columns(x, dtype, M, ldx, K, idx, n_alive, xg, ldp, n_alive,
                                   d->err_word, d->sm_count, s);
     if (e != cudaSuccess) return cuda_fail(e);
-    e = gw::launch_gemm_tc(false, workspace, dtype, M, n_alive, ldp, w_packed, N, ldw, nullptr,
-                           n_alive, bias, epilogue, y, ldy, d->err_word, d->sm_count, s);
+    if (gw::use_pair_gemm(M, N, d->sm_count))
+      e = gw::launch_gemm_tc2(xg, dtype, M, n_alive, ldp, w_packed, N, ldw, bias, epilogue, y, ldy,
+                              d->err_word, d->sm_count, s);
+    else
+      e = gw::launch_gemm_tc(0, xg, dtype, M, n_alive, ldp, w_packed, N, ldw, nullptr, n_alive,
+                             bias, epilogue, y, ldy, d->err_word, d->sm_count, s);
   } else {
-    e = gw::launch_gemm_tc(true, x, dtype, M, K, ldx, w_packed, N, ldw, idx, n_alive, bias,
-                           epilogue, y, ldy, d->err_word, d->sm_count, s);
+    e = gw::launch_gemm_tc(2, x, dtype, M, K, ldx, w_packed, N, ldw, idx, n_alive, bias,
+                           epilogue, y, ldy, d->err_word, d->sm_count, s, xg, ldp, counters);
   }
   return e == cudaSuccess ? GW_OK : cuda_fail(e);
 }
@@ -298,8 +320,12 @@ int gw_packed_gemm(const void* a, int dtype, int64_t M, int64_t K, int64_t lda,
   if (!a || !w_packed) return GW_ERR_NULL;
   if (!aligned16(a) || !aligned16(w_packed) || (lda % 8) != 0 || (ldw % 8) != 0)
     return GW_ERR_ALIGN;
-  e = gw::launch_gemm_tc(false, a, dtype, M, K, lda, w_packed, N, ldw, nullptr, K, bias,
-                         epilogue, y, ldy, d->err_word, d->sm_count, s);
+  if (gw::use_pair_gemm(M, N, d->sm_count))
+    e = gw::launch_gemm_tc2(a, dtype, M, K, lda, w_packed, N, ldw, bias, epilogue, y, ldy,
+                            d->err_word, d->sm_count, s);
+  else
+    e = gw::launch_gemm_tc(0, a, dtype, M, K, lda, w_packed, N, ldw, nullptr, K, bias,
+                           epilogue, y, ldy, d->err_word, d->sm_count, s);
   return e == cudaSuccess ? GW_OK : cuda_fail(e);
 }
 

@@ -122,6 +122,54 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Orders generic-proxy global accesses against async-proxy (TMA) accesses.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Streaming 16-bit global load that does not allocate in L1.
+__device__ __forceinline__ uint32_t ld_stream_u16(const uint16_t* p) {
+  unsigned short v;
+  asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const unsigned int* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void red_release_gpu_add(unsigned int* p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+
+// Barrier over `nthreads` threads (a multiple of 32) of the CTA, id 1..15.
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
+  asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(nthreads) : "memory");
+}
+
+// Bounded wait until *counter >= target (acquire). Same abort/timeout contract
+// as mbar_wait.
+__device__ __forceinline__ bool wait_counter_geq(const unsigned int* counter, uint32_t target,
+                                                 volatile int* abort_flag, unsigned int* err,
+                                                 unsigned long long limit_ns = GW_WAIT_LIMIT_NS) {
+  if (ld_acquire_gpu(counter) >= target) return true;
+  const unsigned long long t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    __nanosleep(64);
+    if (ld_acquire_gpu(counter) >= target) return true;
+    if ((i & 63u) == 0u) {
+      if (abort_flag && *abort_flag) return false;
+      if (global_timer_ns() - t0 > limit_ns) {
+        if (abort_flag) *abort_flag = 1;
+        raise_error(err, GW_DERR_WAIT_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
 // ----------------------------------------------------------------------------
 // tcgen05 / TMEM
 // ----------------------------------------------------------------------------
@@ -201,6 +249,107 @@ __host__ __device__ constexpr uint32_t idesc_f16(uint32_t ab_format, uint32_t m,
        | (ab_format << 10)         // B format
        | ((n >> 3) << 17)          // N / 8
        | ((m >> 4) << 24);         // M / 16
+}
+
+// ----------------------------------------------------------------------------
+// Clusters of two CTAs (2-SM tcgen05 MMA). No TMA multicast anywhere: each CTA
+// loads its own operand halves; only MMA completion is multicast (commit).
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(saddr), "r"(rank));
+  return out;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+
+// Arrive on an mbarrier of another CTA of the cluster (cluster-window address).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];"
+               :: "r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+
+// Bounded wait with cluster-scope acquire, for barriers that other CTAs (or
+// their TMA/MMA completions) arrive on. Same contract as mbar_wait.
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
+                                                  volatile int* abort_flag, unsigned int* err,
+                                                  unsigned long long limit_ns = GW_WAIT_LIMIT_NS) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const unsigned long long t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((i & 255u) == 0u) {
+      if (abort_flag && *abort_flag) return false;
+      if (global_timer_ns() - t0 > limit_ns) {
+        if (abort_flag) *abort_flag = 1;
+        raise_error(err, GW_DERR_WAIT_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+// 2-D TMA tile load into this CTA's shared memory whose completion bytes are
+// counted on `cluster_bar` (the pair leader's barrier). Not multicast.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void* tmap, int32_t x,
+                                                 int32_t y, uint32_t cluster_bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];"
+      :: "r"(dst), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(cluster_bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+               :: "r"(dst_smem), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;"
+               :: "r"(taddr), "r"(ncols) : "memory");
+}
+
+// D (both CTAs' TMEM) (+)= A (both CTAs' smem) * B (both CTAs' smem)^T, M = 256.
+__device__ __forceinline__ void tc_mma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive once on the barrier at this shared offset in every CTA of `mask` when
+// this thread's prior pair MMAs complete.
+__device__ __forceinline__ void tc_commit_pair_mc(uint32_t bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;"
+      :: "r"(bar), "h"(mask) : "memory");
 }
 
 // ----------------------------------------------------------------------------

@@ -32,6 +32,9 @@ __global__ void __launch_bounds__(kGThreads)
 gather_columns_kernel(const raw* __restrict__ src, int64_t rows, int64_t ld_src, int64_t cols_src,
                       const int64_t* __restrict__ idx, int64_t n_idx, raw* __restrict__ dst,
                       int64_t ld_dst, int64_t pad_to, unsigned int* err) {
+  // Let a dependent kernel (the GEMM that consumes dst) start its prologue
+  // early; it still waits for this grid to finish before reading dst.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int64_t c0 = static_cast<int64_t>(blockIdx.x) * kColChunk;

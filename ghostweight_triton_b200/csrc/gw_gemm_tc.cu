@@ -14,12 +14,19 @@
 //   * warp 1      : TMEM allocator and the single-thread tcgen05.mma issuer
 //                   (128 x BN x 16 per instruction, 4 per k-block), commits
 //                   free smem stages and publish finished accumulators;
-//   * warps 2..9  : gather producers -- two groups of four warps take
-//                   alternate k-blocks; a warp loads 32 rows x 64 alive columns
-//                   of x straight from global memory (lane <-> alive column, so
-//                   a request covers 32 consecutive alive indices of one row),
-//                   waits for the stage to be free, and writes the values into
-//                   the 128B-swizzled K-major layout tcgen05 reads;
+//   * warps 2..9  : A-operand gather, in one of two modes --
+//       SMEM    : two groups of four warps take alternate k-blocks; a warp
+//                 loads 32 rows x 64 alive columns of x straight from global
+//                 memory (lane <-> alive column), waits for the stage to be
+//                 free and writes the values into the 128B-swizzled K-major
+//                 shared-memory layout tcgen05 reads (no scratch, one launch);
+//       OVERLAP : the eight warps of every CTA cooperatively gather x[:, alive]
+//                 into a dense scratch matrix x' (k-block-major order over all
+//                 CTAs, 128 rows x 64 columns per unit) and publish a per-k-block
+//                 ready counter; the TMA warp waits for a k-block's counter the
+//                 first time it needs it and then streams x' like a dense
+//                 operand. The gather runs concurrently with the MMAs; the
+//                 launch is cooperative so every CTA is resident;
 //   * warps 10..13: epilogue -- tcgen05.ld of the fp32 accumulator (one TMEM
 //                   lane per output row), bias, optional GELU, one rounding to
 //                   the output type, 16-byte stores;
@@ -30,6 +37,7 @@
 // their loops, in-flight TMA loads and MMAs are drained, TMEM is freed and the
 // device error word records the event.
 #include <algorithm>
+#include <cstdlib>
 
 #include <cuda.h>
 
@@ -42,20 +50,30 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kStages = 4;
 constexpr int kThreads = 448;
+constexpr int kMaxStages = 8;
 constexpr int kWarpTma = 0;
 constexpr int kWarpMma = 1;
 constexpr int kWarpGather0 = 2;
 constexpr int kGatherWarps = 8;      // two groups of four
 constexpr int kWarpEpi0 = 10;        // four epilogue warps
 
+// How the A operand (x[:, alive]) reaches shared memory.
+constexpr int kATma = 0;        // dense [M, K'] matrix by TMA (already compacted)
+constexpr int kASmemGather = 1; // producer warps gather into shared memory
+constexpr int kAOverlap = 2;    // in-kernel cooperative gather to scratch, then TMA
+
+constexpr int pow2_at_least(int v) { int p = 32; while (p < v) p <<= 1; return p; }
+
 template <int BN>
 struct TcCfg {
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kTmemCols = 2 * BN;
+  // As many stages as fit in ~200 KB of shared memory (4 for BN=256, 5 for 192, 6 for 128).
+  static constexpr int kStagesFit = (200 * 1024) / kStageBytes;
+  static constexpr int kStages = kStagesFit > kMaxStages ? kMaxStages : kStagesFit;
+  static constexpr int kTmemCols = pow2_at_least(2 * BN);   // two accumulator buffers
   static constexpr int kBarBytes = 256;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarBytes;
 };
@@ -78,9 +96,12 @@ struct TcParams {
   int n_tiles;
   int num_tiles;
   unsigned int* err;
+  uint16_t* xg;                 // kAOverlap: scratch x' [M, ldg]
+  int64_t ldg;
+  unsigned int* kb_ready;       // kAOverlap: per-k-block count of gathered 128-row units
 };
 
-template <int BN, int DT, bool GATHER>
+template <int BN, int DT, int AMODE>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
                const __grid_constant__ CUtensorMap tmap_a, const TcParams p) {
@@ -91,15 +112,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
   uint8_t* smem = smem_raw + ((1024u - (raw_s & 1023u)) & 1023u);
   const uint32_t sbase = smem_u32(smem);
 
-  uint8_t* bar_region = smem + kStages * C::kStageBytes;
+  uint8_t* bar_region = smem + C::kStages * C::kStageBytes;
   const uint32_t bar0 = smem_u32(bar_region);
   // barriers: full_a[S] full_b[S] empty[S] tfull[2] tempty[2] drain
   auto full_a = [&](int s) { return bar0 + 8u * s; };
-  auto full_b = [&](int s) { return bar0 + 8u * (kStages + s); };
-  auto empty = [&](int s) { return bar0 + 8u * (2 * kStages + s); };
-  auto tfull = [&](int b) { return bar0 + 8u * (3 * kStages + b); };
-  auto tempty = [&](int b) { return bar0 + 8u * (3 * kStages + 2 + b); };
-  const uint32_t drain_bar = bar0 + 8u * (3 * kStages + 4);
+  auto full_b = [&](int s) { return bar0 + 8u * (C::kStages + s); };
+  auto empty = [&](int s) { return bar0 + 8u * (2 * C::kStages + s); };
+  auto tfull = [&](int b) { return bar0 + 8u * (3 * C::kStages + b); };
+  auto tempty = [&](int b) { return bar0 + 8u * (3 * C::kStages + 2 + b); };
+  const uint32_t drain_bar = bar0 + 8u * (3 * C::kStages + 4);
+  static_assert(8 * (3 * C::kStages + 5) <= 192, "barrier region overflows into the TMEM slot");
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_region + 192);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_region + 196);
 
@@ -107,7 +129,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < C::kStages; ++s) {
       mbar_init(full_a(s), kGatherWarps / 2);
       mbar_init(full_b(s), 1);
       mbar_init(empty(s), 1);
@@ -122,7 +144,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
   }
   if (warp == kWarpTma && lane == 0) {
     tma_prefetch_desc(&tmap_b);
-    if (!GATHER) tma_prefetch_desc(&tmap_a);
+    if (AMODE != kASmemGather) tma_prefetch_desc(&tmap_a);
   }
   if (warp == kWarpMma) {
     tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
@@ -136,18 +158,32 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
   if (warp == kWarpTma) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
+      // A dense A operand may have been written by the previous kernel on the
+      // stream (the pregather launch): with programmatic dependent launch this
+      // CTA got here early, so wait for that grid before reading it.
+      if (AMODE == kATma) asm volatile("griddepcontrol.wait;" ::: "memory");
       uint32_t it = 0;
+      int ready_kb = 0;   // kAOverlap: k-blocks of x' known to be complete
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
         const int m_blk = tile % p.m_tiles;
         const int n_blk = tile / p.m_tiles;
         for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
-          const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1u;
+          const int s = it % C::kStages;
+          const uint32_t ph = (it / C::kStages) & 1u;
+          if (AMODE == kAOverlap && ready_kb <= kb) {
+            while (ready_kb <= kb) {
+              if (!wait_counter_geq(p.kb_ready + ready_kb, static_cast<uint32_t>(p.m_tiles),
+                                    abort_flag, p.err)) { ok = false; break; }
+              ++ready_kb;
+            }
+            if (!ok) break;
+            fence_proxy_async_global();   // generic-proxy writes of x' before our TMA reads
+          }
           if (!mbar_wait(empty(s), ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
           const uint32_t a_s = sbase + s * C::kStageBytes;
           const uint32_t b_s = a_s + C::kABytes;
-          if (GATHER) {
+          if (AMODE == kASmemGather) {
             mbar_arrive_expect_tx(full_b(s), C::kBBytes);
             tma_load_2d(b_s, &tmap_b, kb * kBK, n_blk * BN, full_b(s));
           } else {
@@ -159,9 +195,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
       }
       if (!ok) {
         // Drain loads still in flight before the CTA exits (bounded, 100 ms).
-        const uint32_t first = it > static_cast<uint32_t>(kStages) ? it - kStages : 0u;
+        const uint32_t first = it > static_cast<uint32_t>(C::kStages) ? it - C::kStages : 0u;
         for (uint32_t i = first; i < it; ++i)
-          mbar_wait(full_b(i % kStages), (i / kStages) & 1u, nullptr, p.err, 100000000ull);
+          mbar_wait(full_b(i % C::kStages), (i / C::kStages) & 1u, nullptr, p.err, 100000000ull);
       }
     }
   } else if (warp == kWarpMma) {
@@ -177,10 +213,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + b * BN;
         for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
-          const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1u;
+          const int s = it % C::kStages;
+          const uint32_t ph = (it / C::kStages) & 1u;
           if (!mbar_wait(full_b(s), ph, abort_flag, p.err)) { ok = false; break; }
-          if (GATHER && !mbar_wait(full_a(s), ph, abort_flag, p.err)) { ok = false; break; }
+          if (AMODE == kASmemGather && !mbar_wait(full_a(s), ph, abort_flag, p.err)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_s = sbase + s * C::kStageBytes;
           const uint64_t a_desc = smem_desc_kmajor_sw128(a_s);
@@ -203,7 +239,70 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
     __syncwarp();
   } else if (warp < kWarpEpi0) {
     // ------------------------------------------------------------ gather producers
-    if (GATHER) {
+    if (AMODE == kAOverlap) {
+      // Cooperative gather of x[:, alive] -> x' in k-block-major unit order.
+      // A unit is 128 rows x 64 alive columns; each warp owns 16 of the rows and
+      // each lane two adjacent output columns (one 4-byte store per row). Two
+      // units are handled per iteration so 64 independent loads are in flight
+      // per thread. After the stores, every writer orders them for the async
+      // proxy, the eight warps meet at a named barrier, and one thread
+      // publishes the units with a release increment of their k-block counter.
+      const int gt = warp - kWarpGather0;                  // 0..7, 16 rows each
+      const int units = p.num_kb * p.m_tiles;
+      const int64_t step = p.ldg / 2;
+      bool bad = false;
+      for (int u0 = blockIdx.x; u0 < units; u0 += 2 * gridDim.x) {
+        uint32_t v[2][16];
+        int64_t row0[2];
+        int rows_here[2], kbu[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int u = u0 + h * gridDim.x;
+          const bool has = u < units;
+          const int kb = has ? u / p.m_tiles : 0;
+          const int m_blk = has ? u - kb * p.m_tiles : 0;
+          kbu[h] = has ? kb : -1;
+          const int64_t k0 = static_cast<int64_t>(kb) * kBK + 2 * lane;
+          int64_t c0 = -1, c1 = -1;
+          if (has && k0 < p.n_alive) {
+            c0 = __ldg(p.idx + k0);
+            if (c0 < 0 || c0 >= p.K) { bad = true; c0 = -1; }
+          }
+          if (has && k0 + 1 < p.n_alive) {
+            c1 = __ldg(p.idx + k0 + 1);
+            if (c1 < 0 || c1 >= p.K) { bad = true; c1 = -1; }
+          }
+          row0[h] = static_cast<int64_t>(m_blk) * kBM + gt * 16;
+          const int64_t rem = p.M - row0[h];
+          rows_here[h] = (!has || rem <= 0) ? 0 : (rem >= 16 ? 16 : static_cast<int>(rem));
+          const uint16_t* xr = p.x + (rows_here[h] > 0 ? row0[h] * p.ldx : 0);
+#pragma unroll
+          for (int r = 0; r < 16; ++r) {
+            const bool rv = r < rows_here[h];
+            const uint32_t lo = (rv && c0 >= 0) ? ld_stream_u16(xr + r * p.ldx + c0) : 0u;
+            const uint32_t hi = (rv && c1 >= 0) ? ld_stream_u16(xr + r * p.ldx + c1) : 0u;
+            v[h][r] = lo | (hi << 16);
+          }
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          if (rows_here[h] > 0) {
+            uint32_t* dst = reinterpret_cast<uint32_t*>(p.xg + row0[h] * p.ldg +
+                                                        static_cast<int64_t>(kbu[h]) * kBK) + lane;
+#pragma unroll
+            for (int r = 0; r < 16; ++r)
+              if (r < rows_here[h]) dst[r * step] = v[h][r];
+          }
+        }
+        fence_proxy_async_global();
+        named_bar_sync(1, kGatherWarps * 32);
+        if (warp == kWarpGather0 && lane == 0) {
+          if (kbu[0] >= 0) red_release_gpu_add(p.kb_ready + kbu[0], 1u);
+          if (kbu[1] >= 0) red_release_gpu_add(p.kb_ready + kbu[1], 1u);
+        }
+      }
+      if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) raise_error(p.err, GW_DERR_BAD_INDEX);
+    } else if (AMODE == kASmemGather) {
       const int gw_idx = warp - kWarpGather0;
       const uint32_t grp = static_cast<uint32_t>(gw_idx >> 2);
       const int wrow = (gw_idx & 3) * 32;
@@ -217,8 +316,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
         const uint16_t* xw = p.x + (rows_here > 0 ? row0 * p.ldx : 0);
         for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
           if ((it & 1u) != grp) continue;
-          const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1u;
+          const int s = it % C::kStages;
+          const uint32_t ph = (it / C::kStages) & 1u;
           const int64_t k0 = static_cast<int64_t>(kb) * kBK + lane;
           int64_t c0 = -1, c1 = -1;
           bool bad = false;
@@ -345,36 +444,77 @@ bool make_tmap_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols
   return r == CUDA_SUCCESS;
 }
 
-template <int BN, int DT, bool GATHER>
+template <int BN, int DT, int AMODE>
 cudaError_t launch_tc(const CUtensorMap& tb, const CUtensorMap& ta, const TcParams& p,
                       int sm_count, cudaStream_t stream) {
   using C = TcCfg<BN>;
-  auto kern = gemm_tc_kernel<BN, DT, GATHER>;
+  auto kern = gemm_tc_kernel<BN, DT, AMODE>;
   // Opt in to the large dynamic shared-memory carve-out (idempotent, cheap).
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        C::kSmemBytes);
   if (e != cudaSuccess) return e;
   const int grid = std::min(p.num_tiles, sm_count > 0 ? sm_count : 148);
-  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(tb, ta, p);
-  return cudaGetLastError();
+  if (AMODE == kASmemGather) {
+    kern<<<grid, kThreads, C::kSmemBytes, stream>>>(tb, ta, p);
+    return cudaGetLastError();
+  }
+  if (AMODE == kATma) {
+    // Programmatic dependent launch: the prologue (barriers, TMEM, descriptor
+    // prefetch) overlaps the tail of the previous kernel on the stream; the
+    // TMA warp waits for that kernel before it reads the A operand.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, tb, ta, p);
+  }
+  // The in-kernel gather makes CTAs wait on each other's units: launch
+  // cooperatively so that all of them are resident (the launch fails otherwise).
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, tb, ta, p);
 }
 
 }  // namespace
 
-cudaError_t launch_gemm_tc(bool a_gather, const void* x, int dtype, int64_t M, int64_t K,
+cudaError_t launch_gemm_tc(int a_mode, const void* x, int dtype, int64_t M, int64_t K,
                            int64_t ldx, const void* w, int64_t N, int64_t ldw,
                            const int64_t* idx, int64_t n_alive, const void* bias, int epilogue,
                            void* y, int64_t ldy, unsigned int* err, int sm_count,
-                           cudaStream_t stream) {
-  // BN = 256 unless 128-wide tiles give noticeably more CTAs to spread over the SMs.
+                           cudaStream_t stream, void* scratch_xg, int64_t ldg,
+                           unsigned int* kb_ready) {
+  // Tile width 256 (measured best on B200 even where 128 or 192 balance the
+  // waves better: wider tiles reuse A more per byte moved), 128 for narrow N.
+  // GW_GEMM_BN=128|192|256 overrides the choice (tuning and tests).
   const int64_t m_tiles = (M + kBM - 1) / kBM;
   const int64_t sms = sm_count > 0 ? sm_count : 148;
-  const int64_t t256 = m_tiles * ((N + 255) / 256);
-  const bool use128 = (N <= 128) || (t256 < sms && m_tiles * ((N + 127) / 128) > t256);
-  const int BN = use128 ? 128 : 256;
+  int BN = N <= 128 ? 128 : 256;
+  {
+    static const int forced = [] {
+      const char* v = std::getenv("GW_GEMM_BN");
+      return v ? std::atoi(v) : 0;
+    }();
+    if (forced == 128 || forced == 192 || forced == 256) BN = forced;
+  }
   const int64_t n_tiles = (N + BN - 1) / BN;
   const int64_t num_tiles = m_tiles * n_tiles;
   if (num_tiles > 0x7FFFFFFFll || m_tiles > 0x7FFFFFFFll) return cudaErrorInvalidValue;
+  const int64_t num_kb = (n_alive + kBK - 1) / kBK;
+  if (a_mode == kAOverlap && num_kb * m_tiles > 0x7FFFFFFFll) return cudaErrorInvalidValue;
 
   TcParams p{};
   p.x = static_cast<const uint16_t*>(x);
@@ -389,31 +529,47 @@ cudaError_t launch_gemm_tc(bool a_gather, const void* x, int dtype, int64_t M, i
   p.y = static_cast<uint16_t*>(y);
   p.ldy = ldy;
   p.y_vec_ok = ((reinterpret_cast<uintptr_t>(y) & 15u) == 0 && (ldy % 8) == 0) ? 1 : 0;
-  p.num_kb = static_cast<int>((n_alive + kBK - 1) / kBK);
+  p.num_kb = static_cast<int>(num_kb);
   p.m_tiles = static_cast<int>(m_tiles);
   p.n_tiles = static_cast<int>(n_tiles);
   p.num_tiles = static_cast<int>(num_tiles);
   p.err = err;
+  p.xg = static_cast<uint16_t*>(scratch_xg);
+  p.ldg = ldg;
+  p.kb_ready = kb_ready;
 
   CUtensorMap tb, ta;
   if (!make_tmap_2d(&tb, w, N, n_alive, ldw, kBK, BN)) return cudaErrorInvalidValue;
-  if (a_gather) {
-    ta = tb;   // unused by the gather variant
-  } else {
+  if (a_mode == kASmemGather) {
+    ta = tb;   // unused by the shared-memory gather variant
+  } else if (a_mode == kATma) {
     if (!make_tmap_2d(&ta, x, M, n_alive, ldx, kBK, kBM)) return cudaErrorInvalidValue;
+  } else {
+    if (!scratch_xg || !kb_ready || (ldg % 8) != 0) return cudaErrorInvalidValue;
+    if (!make_tmap_2d(&ta, scratch_xg, M, n_alive, ldg, kBK, kBM)) return cudaErrorInvalidValue;
+    cudaError_t e = cudaMemsetAsync(kb_ready, 0, static_cast<size_t>(num_kb) * sizeof(unsigned int),
+                                    stream);
+    if (e != cudaSuccess) return e;
   }
 
-#define GW_TC_CASE(BNV, DTV)                                                      \
-  return a_gather ? launch_tc<BNV, DTV, true>(tb, ta, p, static_cast<int>(sms), stream) \
-                  : launch_tc<BNV, DTV, false>(tb, ta, p, static_cast<int>(sms), stream)
-  if (BN == 256) {
-    if (dtype == GW_DTYPE_BF16) { GW_TC_CASE(256, GW_DTYPE_BF16); }
-    GW_TC_CASE(256, GW_DTYPE_F16);
-  } else {
-    if (dtype == GW_DTYPE_BF16) { GW_TC_CASE(128, GW_DTYPE_BF16); }
-    GW_TC_CASE(128, GW_DTYPE_F16);
+#define GW_TC_MODES(BNV, DTV)                                                                     \
+  switch (a_mode) {                                                                              \
+    case kATma: return launch_tc<BNV, DTV, kATma>(tb, ta, p, static_cast<int>(sms), stream);      \
+    case kASmemGather:                                                                           \
+      return launch_tc<BNV, DTV, kASmemGather>(tb, ta, p, static_cast<int>(sms), stream);        \
+    default: return launch_tc<BNV, DTV, kAOverlap>(tb, ta, p, static_cast<int>(sms), stream);    \
   }
-#undef GW_TC_CASE
+  if (BN == 256) {
+    if (dtype == GW_DTYPE_BF16) { GW_TC_MODES(256, GW_DTYPE_BF16) }
+    GW_TC_MODES(256, GW_DTYPE_F16)
+  } else if (BN == 192) {
+    if (dtype == GW_DTYPE_BF16) { GW_TC_MODES(192, GW_DTYPE_BF16) }
+    GW_TC_MODES(192, GW_DTYPE_F16)
+  } else {
+    if (dtype == GW_DTYPE_BF16) { GW_TC_MODES(128, GW_DTYPE_BF16) }
+    GW_TC_MODES(128, GW_DTYPE_F16)
+  }
+#undef GW_TC_MODES
 }
 
 }  // namespace gw

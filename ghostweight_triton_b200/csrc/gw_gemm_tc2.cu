@@ -1,0 +1,322 @@
+// K3, CTA-pair variant: y[256-row pair tile, 256 cols] on tcgen05 with cta_group::2.
+//
+// Same product as gemm_tc_kernel's TMA mode (dense A = the gathered x', packed
+// W'), but two CTAs of a cluster share one 256 x 256 accumulator tile:
+//   * each CTA TMA-loads its own 128 rows of A and its own 128 rows of B
+//     (half of the tile's 256 output features) for every 64-wide k-block, so
+//     per SM only 32 KB cross L2 per k-block instead of 48 KB for 128 x 256;
+//     the loads of both CTAs complete on the leader CTA's barrier;
+//   * the leader's MMA thread issues tcgen05.mma.cta_group::2 (M = 256,
+//     N = 256, K = 16) reading both CTAs' shared memory and writing both
+//     CTAs' TMEM (128 lanes x 256 fp32 columns each, double-buffered);
+//   * MMA completion is multicast to both CTAs (tcgen05.commit ... multicast)
+//     to free their stages and publish finished accumulators;
+//   * each CTA's four epilogue warps drain its own TMEM (bias, GELU, one
+//     rounding, 16-byte stores) and arrive on the leader's accumulator-empty
+//     barrier (remote arrive for the second CTA).
+// No TMA multicast: each CTA loads only its own halves.
+// Every wait is bounded (gw_common.cuh); the kernel never hangs on a lost
+// arrival, it records GW_DEVICE_ERR_WAIT_TIMEOUT and unwinds.
+#include <algorithm>
+#include <cstdlib>
+
+#include <cuda.h>
+
+#include "gw_common.cuh"
+#include "gw_internal.h"
+
+namespace gw {
+
+namespace {
+
+constexpr int kHalfM = 128;            // rows per CTA
+constexpr int kHalfN = 128;            // B rows per CTA
+constexpr int kPairM = 2 * kHalfM;
+constexpr int kPairN = 2 * kHalfN;
+constexpr int kBK2 = 64;
+constexpr int kThreads2 = 192;         // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue
+constexpr int kStages2 = 6;
+constexpr int kABytes2 = kHalfM * kBK2 * 2;
+constexpr int kBBytes2 = kHalfN * kBK2 * 2;
+constexpr int kStageBytes2 = kABytes2 + kBBytes2;
+constexpr int kTmemCols2 = 2 * kPairN;  // two 256-column accumulators
+constexpr int kSmemBytes2 = 1024 + kStages2 * kStageBytes2 + 256;
+
+struct Tc2Params {
+  int64_t M;
+  int64_t N;
+  const uint16_t* bias;
+  int epi;
+  int y_vec_ok;
+  uint16_t* y;
+  int64_t ldy;
+  int num_kb;
+  int m_tiles;
+  int n_tiles;
+  int num_tiles;
+  unsigned int* err;
+};
+
+template <int DT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
+gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
+                const __grid_constant__ CUtensorMap tmap_a, const Tc2Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_s = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_s & 1023u)) & 1023u);
+  const uint32_t sbase = smem_u32(smem);
+  uint8_t* bar_region = smem + kStages2 * kStageBytes2;
+  const uint32_t bar0 = smem_u32(bar_region);
+  auto full = [&](int s) { return bar0 + 8u * s; };
+  auto empty = [&](int s) { return bar0 + 8u * (kStages2 + s); };
+  auto tfull = [&](int b) { return bar0 + 8u * (2 * kStages2 + b); };
+  auto tempty = [&](int b) { return bar0 + 8u * (2 * kStages2 + 2 + b); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * kStages2 + 4);
+  static_assert(8 * (2 * kStages2 + 5) <= 192, "barrier region overflows into the TMEM slot");
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_region + 192);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_region + 196);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();          // 0 = leader of the pair
+  const int pair = static_cast<int>(blockIdx.x >> 1);
+  const int num_pairs = static_cast<int>(gridDim.x >> 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages2; ++s) {
+      mbar_init(full(s), 1);      // leader's expect_tx arrival (+ both CTAs' bytes)
+      mbar_init(empty(s), 1);     // leader's multicast MMA commit
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull(b), 1);     // leader's multicast commit
+      mbar_init(tempty(b), 8);    // 4 epilogue warps x 2 CTAs (used on the leader)
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    mbar_init_fence();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols2);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();          // peers' barriers are initialised before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      asm volatile("griddepcontrol.wait;" ::: "memory");   // A may come from the previous kernel
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < p.num_tiles; tile += num_pairs) {
+        const int m_blk = tile % p.m_tiles;
+        const int n_blk = tile / p.m_tiles;
+        const int a_row = m_blk * kPairM + static_cast<int>(rank) * kHalfM;
+        const int b_row = n_blk * kPairN + static_cast<int>(rank) * kHalfN;
+        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+          const int s = it % kStages2;
+          const uint32_t ph = (it / kStages2) & 1u;
+          if (!mbar_wait_cluster(empty(s), ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
+          const uint32_t a_s = sbase + s * kStageBytes2;
+          const uint32_t b_s = a_s + kABytes2;
+          const uint32_t leader_full = mapa_shared(full(s), 0);
+          if (rank == 0) mbar_arrive_expect_tx(full(s), 2 * kStageBytes2);
+          tma_load_2d_pair(a_s, &tmap_a, kb * kBK2, a_row, leader_full);
+          tma_load_2d_pair(b_s, &tmap_b, kb * kBK2, b_row, leader_full);
+        }
+      }
+      if (!ok && rank == 0) {
+        const uint32_t first = it > static_cast<uint32_t>(kStages2) ? it - kStages2 : 0u;
+        for (uint32_t i = first; i < it; ++i)
+          mbar_wait_cluster(full(i % kStages2), (i / kStages2) & 1u, nullptr, p.err, 100000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = idesc_f16(DT == GW_DTYPE_BF16 ? 1u : 0u, kPairM, kPairN);
+      uint32_t it = 0, lt = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < p.num_tiles; tile += num_pairs, ++lt) {
+        const uint32_t b = lt & 1u;
+        const uint32_t aph = (lt >> 1) & 1u;
+        if (!mbar_wait_cluster(tempty(b), aph ^ 1u, abort_flag, p.err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + b * kPairN;
+        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+          const int s = it % kStages2;
+          const uint32_t ph = (it / kStages2) & 1u;
+          if (!mbar_wait_cluster(full(s), ph, abort_flag, p.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_s = sbase + s * kStageBytes2;
+          const uint64_t a_desc = smem_desc_kmajor_sw128(a_s);
+          const uint64_t b_desc = smem_desc_kmajor_sw128(a_s + kABytes2);
+#pragma unroll
+          for (int k = 0; k < kBK2 / 16; ++k)
+            tc_mma_f16_pair(d_tmem, a_desc + 2u * k, b_desc + 2u * k, idesc,
+                            (kb > 0 || k > 0) ? 1u : 0u);
+          tc_commit_pair_mc(empty(s), 0x3);
+        }
+        if (!ok) break;
+        tc_commit_pair_mc(tfull(b), 0x3);
+      }
+      tc_commit_pair_mc(drain_bar, 0x1);
+      mbar_wait(drain_bar, 0u, nullptr, p.err, 100000000ull);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;
+    const uint32_t leader_tempty0 = mapa_shared(tempty(0), 0);
+    const uint32_t leader_tempty1 = mapa_shared(tempty(1), 0);
+    uint32_t lt = 0;
+    for (int tile = pair; tile < p.num_tiles; tile += num_pairs, ++lt) {
+      const int m_blk = tile % p.m_tiles;
+      const int n_blk = tile / p.m_tiles;
+      const uint32_t b = lt & 1u;
+      const uint32_t aph = (lt >> 1) & 1u;
+      if (!mbar_wait_cluster(tfull(b), aph, abort_flag, p.err)) break;
+      tc_fence_after();
+      const int64_t row = static_cast<int64_t>(m_blk) * kPairM + rank * kHalfM + q * 32 + lane;
+      const bool row_ok = row < p.M;
+      uint16_t* yrow = p.y + (row_ok ? row * p.ldy : 0);
+#pragma unroll 1
+      for (int c = 0; c < kPairN / 32; ++c) {
+        uint32_t acc[32];
+        tc_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * kPairN + c * 32, acc);
+        tc_wait_ld();
+        const int64_t n_base = static_cast<int64_t>(n_blk) * kPairN + c * 32;
+        float f[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(acc[j]);
+        if (p.bias) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n_base + j < p.N) f[j] += Elem<DT>::to_f(__ldg(p.bias + n_base + j));
+        }
+        if (p.epi != GW_EPI_NONE) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[j] = apply_epilogue(f[j], p.epi);
+        }
+        if (row_ok) {
+          if (p.y_vec_ok && n_base + 32 <= p.N) {
+            uint32_t packed[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              packed[j] = static_cast<uint32_t>(Elem<DT>::from_f(f[2 * j])) |
+                          (static_cast<uint32_t>(Elem<DT>::from_f(f[2 * j + 1])) << 16);
+            uint4* dst = reinterpret_cast<uint4*>(yrow + n_base);
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n_base + j < p.N) yrow[n_base + j] = Elem<DT>::from_f(f[j]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (rank == 0) mbar_arrive(tempty(b));
+        else mbar_arrive_cluster(b ? leader_tempty1 : leader_tempty0);
+      }
+    }
+  }
+
+  __syncthreads();
+  cluster_sync();          // the leader's MMAs into our TMEM and reads of our smem are done
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols2);
+  }
+}
+
+using EncodeTiledFn2 = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+bool make_tmap_2d_pair(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
+                       int box_cols, int box_rows) {
+  auto encode = reinterpret_cast<EncodeTiledFn2>(tensor_map_encoder());
+  if (!encode) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2u};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides,
+                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool use_pair_gemm(int64_t M, int64_t N, int sm_count) {
+  // GW_GEMM_PAIR=0 forces the single-CTA kernel, =1 the pair kernel (tuning, tests).
+  static const int forced = [] {
+    const char* v = std::getenv("GW_GEMM_PAIR");
+    return v ? std::atoi(v) : -1;
+  }();
+  if (forced == 0) return false;
+  if (forced == 1) return true;
+  // Pairs pay off once there are at least as many 256 x 256 tiles as SM pairs;
+  // below that, 128-row tiles spread the work over more SMs (measured).
+  const int64_t pair_tiles = ((M + kPairM - 1) / kPairM) * ((N + kPairN - 1) / kPairN);
+  return M > kHalfM && N > kHalfN && pair_tiles >= (sm_count > 0 ? sm_count : 148) / 2;
+}
+
+cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int64_t lda,
+                            const void* w, int64_t N, int64_t ldw, const void* bias, int epilogue,
+                            void* y, int64_t ldy, unsigned int* err, int sm_count,
+                            cudaStream_t stream) {
+  const int64_t m_tiles = (M + kPairM - 1) / kPairM;
+  const int64_t n_tiles = (N + kPairN - 1) / kPairN;
+  const int64_t num_tiles = m_tiles * n_tiles;
+  if (num_tiles > 0x7FFFFFFFll) return cudaErrorInvalidValue;
+  Tc2Params p{};
+  p.M = M;
+  p.N = N;
+  p.bias = static_cast<const uint16_t*>(bias);
+  p.epi = epilogue;
+  p.y = static_cast<uint16_t*>(y);
+  p.ldy = ldy;
+  p.y_vec_ok = ((reinterpret_cast<uintptr_t>(y) & 15u) == 0 && (ldy % 8) == 0) ? 1 : 0;
+  p.num_kb = static_cast<int>((K + kBK2 - 1) / kBK2);
+  p.m_tiles = static_cast<int>(m_tiles);
+  p.n_tiles = static_cast<int>(n_tiles);
+  p.num_tiles = static_cast<int>(num_tiles);
+  p.err = err;
+
+  CUtensorMap ta, tb;
+  if (!make_tmap_2d_pair(&ta, a, M, K, lda, kBK2, kHalfM)) return cudaErrorInvalidValue;
+  if (!make_tmap_2d_pair(&tb, w, N, K, ldw, kBK2, kHalfN)) return cudaErrorInvalidValue;
+
+  auto kern = dtype == GW_DTYPE_BF16 ? gemm_tc2_kernel<GW_DTYPE_BF16> : gemm_tc2_kernel<GW_DTYPE_F16>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes2);
+  if (e != cudaSuccess) return e;
+  const int64_t pairs = std::max<int64_t>(1, (sm_count > 0 ? sm_count : 148) / 2);
+  const int grid = static_cast<int>(2 * std::min<int64_t>(num_tiles, pairs));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kThreads2);
+  cfg.dynamicSmemBytes = kSmemBytes2;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, tb, ta, p);
+}
+
+}  // namespace gw

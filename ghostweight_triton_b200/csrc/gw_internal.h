@@ -42,13 +42,27 @@ cudaError_t launch_validate_indices(const int64_t* idx, int64_t n, int64_t K, in
                                     cudaStream_t stream);
 
 // gw_gemm_tc.cu: tcgen05 gather-GEMM / packed GEMM (fp16, bf16).
-// a_gather: true  -> A is gathered from x via idx (producer warps)
-//           false -> A is a dense [M, n_alive] matrix loaded by TMA (idx unused)
-cudaError_t launch_gemm_tc(bool a_gather, const void* x, int dtype, int64_t M, int64_t K,
+// a_mode: 0 -> A is a dense [M, n_alive] matrix loaded by TMA (idx unused)
+//         1 -> producer warps gather x[:, idx] into shared memory
+//         2 -> warps gather x[:, idx] into scratch_xg [M, ldg] inside the kernel
+//              (per-k-block counters kb_ready[num_kb], zeroed by the launcher),
+//              then TMA streams it; cooperative launch
+cudaError_t launch_gemm_tc(int a_mode, const void* x, int dtype, int64_t M, int64_t K,
                            int64_t ldx, const void* w, int64_t N, int64_t ldw,
                            const int64_t* idx, int64_t n_alive, const void* bias, int epilogue,
                            void* y, int64_t ldy, unsigned int* err, int sm_count,
-                           cudaStream_t stream);
+                           cudaStream_t stream, void* scratch_xg = nullptr, int64_t ldg = 0,
+                           unsigned int* kb_ready = nullptr);
+
+// gw_gemm_tc2.cu: CTA-pair (cta_group::2) tcgen05 GEMM, dense A [M, K] by TMA,
+// 256 x 256 tiles per pair. Chained to the previous kernel by programmatic
+// dependent launch.
+cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int64_t lda,
+                            const void* w, int64_t N, int64_t ldw, const void* bias, int epilogue,
+                            void* y, int64_t ldy, unsigned int* err, int sm_count,
+                            cudaStream_t stream);
+// Whether the CTA-pair kernel serves a dense-A GEMM of this shape.
+bool use_pair_gemm(int64_t M, int64_t N, int sm_count);
 
 // gw_gemm_simt.cu: exact-fp32 gather-GEMM.
 cudaError_t launch_gemm_f32(const float* x, int64_t M, int64_t K, int64_t ldx, const float* w,

@@ -187,10 +187,13 @@ GW_API int gw_gather_rows_t(const void* src, int dtype, int64_t rows, int64_t co
  * reference disables TF32 for fp32 (matmul.py:127-130).
  *
  * strategy (fp16/bf16 only):
- *   GW_GEMM_AUTO      pregather when a large-enough workspace is given, else fused;
+ *   GW_GEMM_AUTO      GW_GEMM_PREGATHER when a large-enough workspace is given, else fused;
  *   GW_GEMM_FUSED     one kernel: producer warps gather x[:, idx] into shared memory;
  *   GW_GEMM_PREGATHER two launches: x[:, idx] -> workspace (dense [M, K'_pad]),
- *                     then the GEMM with both operands loaded by TMA.
+ *                     then the GEMM with both operands loaded by TMA;
+ *   GW_GEMM_OVERLAP   one cooperative kernel: its gather warps write x[:, idx] to
+ *                     the workspace k-block by k-block while the TMA/MMA warps
+ *                     already consume the finished k-blocks.
  * workspace: device scratch of at least gw_gather_gemm_workspace_bytes(M, n_alive,
  * dtype) bytes, 16-byte aligned (may be NULL for GW_GEMM_FUSED / fp32). Its
  * contents on entry do not matter; concurrent calls must not share it.
@@ -198,7 +201,8 @@ GW_API int gw_gather_rows_t(const void* src, int dtype, int64_t rows, int64_t co
 typedef enum {
   GW_GEMM_AUTO = 0,
   GW_GEMM_FUSED = 1,
-  GW_GEMM_PREGATHER = 2
+  GW_GEMM_PREGATHER = 2,
+  GW_GEMM_OVERLAP = 3
 } gw_gemm_strategy;
 
 GW_API size_t gw_gather_gemm_workspace_bytes(int64_t M, int64_t n_alive, int dtype);

@@ -70,6 +70,14 @@ def test_mask_workspace_sizing(lib):
     assert lib.gw_mask_workspace_bytes(1) >= 16 + 4
 
 
+def test_gemm_workspace_sizing(lib):
+    # 256-byte header of k-block counters + x' [M, round_up(K', 64)] 16-bit
+    assert lib.gw_gather_gemm_workspace_bytes(8, 64, 0) == 256 + 8 * 64 * 2
+    assert lib.gw_gather_gemm_workspace_bytes(4096, 2048, 0) == 256 + 4096 * 2048 * 2
+    assert lib.gw_gather_gemm_workspace_bytes(4096, 2048, 2) == 0     # fp32 needs none
+    assert lib.gw_gather_gemm_workspace_bytes(0, 2048, 0) == 0
+
+
 def test_no_gpu_reports_unsupported(lib):
     import torch
 

@@ -57,7 +57,7 @@ def test_shape_dtype_null_errors(lib):
                               None, 0, y.data_ptr(), 32, 2, ws.data_ptr(), 64, s) == _native.GW_ERR_WORKSPACE
     assert lib.gw_gather_gemm(x.data_ptr(), 0, 8, 64, 64, w.data_ptr(), 32, 64, idx.data_ptr(), 64,
                               None, 0, y.data_ptr(), 32, 7, None, 0, s) == _native.GW_ERR_UNSUPPORTED
-    assert lib.gw_gather_gemm_workspace_bytes(8, 64, 0) == 1024
+    assert lib.gw_gather_gemm_workspace_bytes(8, 64, 0) == 256 + 1024
     torch.cuda.synchronize()
 
 

@@ -69,7 +69,7 @@ def test_golden_matmul(name):
     (1024, 2048, 1024, 0.5, "random"), (16, 4096, 4096, 0.5, "random"), (77, 130, 33, 0.1, "random"),
 ])
 @pytest.mark.parametrize("bias,act", [(False, None), (True, None), (True, "gelu"), (True, "gelu_tanh")])
-@pytest.mark.parametrize("strategy", ["pregather", "fused"])
+@pytest.mark.parametrize("strategy", ["overlap", "pregather", "fused"])
 def test_ghost_linear_vs_oracle(dt, M, K, N, sp, pattern, bias, act, strategy):
     seed = M + 3 * K + 7 * N
     x = rand_matrix((M, K), seed, dt, 0.5)
@@ -133,6 +133,20 @@ def test_repeated_indices_and_out_of_range():
     keep = torch.tensor([3, 7], device="cuda")
     torch.testing.assert_close(C, (x.float()[:, keep] @ w.float()[keep, :]).half(), **tols(torch.float16))
     assert _native.device_error(reset=True) & _native.DEVICE_ERR_BAD_INDEX
+
+
+@pytest.mark.parametrize("strategy", ["overlap", "pregather"])
+def test_workspace_reuse_between_shapes(strategy):
+    """One workspace serves successive calls of different K' (stale counters must not leak)."""
+    ws = torch.empty(64 << 20, dtype=torch.uint8, device="cuda")
+    for M, K, N, kp in [(512, 1024, 384, 1000), (300, 512, 256, 64), (1024, 2048, 512, 1536)]:
+        x = torch.randn(M, K, device="cuda", dtype=torch.float16)
+        w = (torch.randn(N, K, device="cuda") / K ** 0.5).half()
+        idx = torch.sort(torch.randperm(K, device="cuda")[:kp]).values
+        y = torch.empty(M, N, device="cuda", dtype=torch.float16)
+        _native.gather_gemm(x, pack_weight(w, idx), idx, y, strategy=strategy, workspace=ws)
+        ref = (x.float()[:, idx] @ w.float()[:, idx].t()).half()
+        torch.testing.assert_close(y, ref, **tols(torch.float16))
 
 
 def test_no_wait_timeouts_after_suite():
@@ -214,7 +228,7 @@ class TestReferenceSuite:
 @pytest.mark.parametrize("M", [4096, 1024, 128, 16])
 @pytest.mark.parametrize("sp,pattern", [(0.0, "random"), (0.5, "random"), (0.9, "random"),
                                         (0.75, "block")])
-@pytest.mark.parametrize("strategy", ["pregather", "fused"])
+@pytest.mark.parametrize("strategy", ["overlap", "pregather", "fused"])
 def test_gemm_sweep_size_vs_dense_fp32(M, sp, pattern, strategy):
     """M x 4096 x 4096 fp16: sparse result equals the dense fp32 product of the zeroed weight."""
     K = N = 4096
