@@ -8,6 +8,7 @@
 #pragma once
 
 #include <cstdint>
+#include <utility>
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
@@ -120,6 +121,28 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int3
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 2-D tile store shared -> global through the TMA unit, tracked by the
+// thread's bulk async-group. x * sizeof(elem) must be a multiple of 16 bytes
+// and x, y non-negative; elements outside the tensor map's extent are not
+// written.
+__device__ __forceinline__ void tma_store_2d(const void* tmap, uint32_t src, int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];"
+      :: "l"(reinterpret_cast<uint64_t>(tmap)), "r"(src), "r"(x), "r"(y) : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until at most N of this thread's bulk groups still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" :: "n"(N) : "memory");
+}
+// Wait until all of this thread's bulk groups have completed.
+__device__ __forceinline__ void bulk_wait_group_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 // Orders generic-proxy global accesses against async-proxy (TMA) accesses.
@@ -274,8 +297,12 @@ __device__ __forceinline__ void cluster_sync() {
 }
 
 // Arrive on an mbarrier of another CTA of the cluster (cluster-window address).
+// Default semantics (release at CTA scope): the arrivals this is used for only
+// publish "my tensor-memory reads are complete" (ordered by tcgen05.wait::ld
+// and tcgen05.fence::before_thread_sync), so they need not wait for the
+// thread's outstanding global stores as a cluster-scope release would.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];"
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];"
                :: "r"(cluster_addr) : "memory");
 }
 
@@ -350,6 +377,25 @@ __device__ __forceinline__ void tc_commit_pair_mc(uint32_t bar, uint16_t mask) {
       "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
       " [%0], %1;"
       :: "r"(bar), "h"(mask) : "memory");
+}
+
+// Host: launch `kern` as a programmatic dependent of the previous work of the
+// stream (it may start before that work completes and must execute
+// griddepcontrol.wait before touching its results).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t stream,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 // ----------------------------------------------------------------------------

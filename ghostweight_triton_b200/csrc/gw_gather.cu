@@ -32,8 +32,11 @@ __global__ void __launch_bounds__(kGThreads)
 gather_columns_kernel(const raw* __restrict__ src, int64_t rows, int64_t ld_src, int64_t cols_src,
                       const int64_t* __restrict__ idx, int64_t n_idx, raw* __restrict__ dst,
                       int64_t ld_dst, int64_t pad_to, unsigned int* err) {
-  // Let a dependent kernel (the GEMM that consumes dst) start its prologue
-  // early; it still waits for this grid to finish before reading dst.
+  // Launched as a programmatic dependent of the previous kernel of the stream
+  // (which may have produced src or idx): wait for it to complete. Then let a
+  // dependent kernel (the GEMM that consumes dst) start its prologue early;
+  // it still waits for this grid to finish before reading dst.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -176,15 +179,13 @@ cudaError_t launch_gather_columns(const void* src, int dtype, int64_t rows, int6
                                  65535);
   dim3 grid(static_cast<unsigned>(col_blocks), gy);
   if (dtype == GW_DTYPE_F32) {
-    gather_columns_kernel<uint32_t><<<grid, kGThreads, 0, stream>>>(
-        static_cast<const uint32_t*>(src), rows, ld_src, cols_src, idx, n_idx,
-        static_cast<uint32_t*>(dst), ld_dst, pad_to, err);
-  } else {
-    gather_columns_kernel<uint16_t><<<grid, kGThreads, 0, stream>>>(
-        static_cast<const uint16_t*>(src), rows, ld_src, cols_src, idx, n_idx,
-        static_cast<uint16_t*>(dst), ld_dst, pad_to, err);
+    return launch_pdl(gather_columns_kernel<uint32_t>, grid, dim3(kGThreads), stream,
+                      static_cast<const uint32_t*>(src), rows, ld_src, cols_src, idx, n_idx,
+                      static_cast<uint32_t*>(dst), ld_dst, pad_to, err);
   }
-  return cudaGetLastError();
+  return launch_pdl(gather_columns_kernel<uint16_t>, grid, dim3(kGThreads), stream,
+                    static_cast<const uint16_t*>(src), rows, ld_src, cols_src, idx, n_idx,
+                    static_cast<uint16_t*>(dst), ld_dst, pad_to, err);
 }
 
 cudaError_t launch_gather_rows(const void* src, int dtype, int64_t rows_src, int64_t cols,

@@ -12,8 +12,12 @@
 //   * MMA completion is multicast to both CTAs (tcgen05.commit ... multicast)
 //     to free their stages and publish finished accumulators;
 //   * each CTA's four epilogue warps drain its own TMEM (bias, GELU, one
-//     rounding, 16-byte stores) and arrive on the leader's accumulator-empty
-//     barrier (remote arrive for the second CTA).
+//     rounding) into swizzled staging tiles that the TMA unit stores to y,
+//     and arrive on the leader's accumulator-empty barrier (remote arrive for
+//     the second CTA) as soon as their TMEM reads are done;
+//   * launch_dependents right after the prologue lets the next kernel of the
+//     stream (the next layer's gather, another GEMM) be scheduled onto SMs as
+//     they drain in the last wave; it waits for this grid's completion itself.
 // No TMA multicast: each CTA loads only its own halves.
 // Every wait is bounded (gw_common.cuh); the kernel never hangs on a lost
 // arrival, it records GW_DEVICE_ERR_WAIT_TIMEOUT and unwinds.
@@ -40,7 +44,13 @@ constexpr int kABytes2 = kHalfM * kBK2 * 2;
 constexpr int kBBytes2 = kHalfN * kBK2 * 2;
 constexpr int kStageBytes2 = kABytes2 + kBBytes2;
 constexpr int kTmemCols2 = 2 * kPairN;  // two 256-column accumulators
-constexpr int kSmemBytes2 = 1024 + kStages2 * kStageBytes2 + 256;
+// Epilogue staging for TMA stores: per epilogue warp two 32-row x 64-column
+// 16-bit tiles (4 KB each, 128-byte swizzled rows).
+constexpr int kEpiCols = 64;
+constexpr int kEpiTileBytes = 32 * kEpiCols * 2;
+constexpr int kEpiBytes = 4 * 2 * kEpiTileBytes;
+constexpr int kSmemBytes2 = 1024 + kStages2 * kStageBytes2 + kEpiBytes + 256;
+static_assert(kSmemBytes2 <= 232448, "shared memory budget per CTA");
 
 struct Tc2Params {
   int64_t M;
@@ -48,6 +58,7 @@ struct Tc2Params {
   const uint16_t* bias;
   int epi;
   int y_vec_ok;
+  int y_tma;                 // y stored through tmap_y (16-byte aligned rows)
   uint16_t* y;
   int64_t ldy;
   int num_kb;
@@ -60,12 +71,14 @@ struct Tc2Params {
 template <int DT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
 gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
-                const __grid_constant__ CUtensorMap tmap_a, const Tc2Params p) {
+                const __grid_constant__ CUtensorMap tmap_a,
+                const __grid_constant__ CUtensorMap tmap_y, const Tc2Params p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_s = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_s & 1023u)) & 1023u);
   const uint32_t sbase = smem_u32(smem);
-  uint8_t* bar_region = smem + kStages2 * kStageBytes2;
+  uint8_t* epi_stage = smem + kStages2 * kStageBytes2;     // 1024-byte aligned
+  uint8_t* bar_region = epi_stage + kEpiBytes;
   const uint32_t bar0 = smem_u32(bar_region);
   auto full = [&](int s) { return bar0 + 8u * s; };
   auto empty = [&](int s) { return bar0 + 8u * (kStages2 + s); };
@@ -98,6 +111,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
+    if (p.y_tma) tma_prefetch_desc(&tmap_y);
   }
   if (warp == 1) {
     tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols2);
@@ -108,6 +122,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
   cluster_sync();          // peers' barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (both CTAs)
@@ -173,9 +188,15 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
+    // Warp q drains TMEM lanes 32q..32q+31 (rows of this CTA's half tile) in
+    // 64-column chunks: two 32-column tcgen05 loads, bias + activation + one
+    // rounding in registers, then a TMA store from a 128-byte-swizzled staging
+    // tile (two per warp, alternating), or direct stores when y's rows are not
+    // 16-byte aligned.
     const int q = warp & 3;
     const uint32_t leader_tempty0 = mapa_shared(tempty(0), 0);
     const uint32_t leader_tempty1 = mapa_shared(tempty(1), 0);
+    uint8_t* stage_w = epi_stage + q * 2 * kEpiTileBytes;
     uint32_t lt = 0;
     for (int tile = pair; tile < p.num_tiles; tile += num_pairs, ++lt) {
       const int m_blk = tile % p.m_tiles;
@@ -184,45 +205,76 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
       const uint32_t aph = (lt >> 1) & 1u;
       if (!mbar_wait_cluster(tfull(b), aph, abort_flag, p.err)) break;
       tc_fence_after();
-      const int64_t row = static_cast<int64_t>(m_blk) * kPairM + rank * kHalfM + q * 32 + lane;
+      const int64_t warp_row0 = static_cast<int64_t>(m_blk) * kPairM + rank * kHalfM + q * 32;
+      const int64_t row = warp_row0 + lane;
       const bool row_ok = row < p.M;
       uint16_t* yrow = p.y + (row_ok ? row * p.ldy : 0);
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * kPairN;
 #pragma unroll 1
-      for (int c = 0; c < kPairN / 32; ++c) {
-        uint32_t acc[32];
-        tc_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * kPairN + c * 32, acc);
-        tc_wait_ld();
-        const int64_t n_base = static_cast<int64_t>(n_blk) * kPairN + c * 32;
-        float f[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(acc[j]);
-        if (p.bias) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (n_base + j < p.N) f[j] += Elem<DT>::to_f(__ldg(p.bias + n_base + j));
+      for (int c = 0; c < kPairN / kEpiCols; ++c) {
+        const int64_t n_chunk = static_cast<int64_t>(n_blk) * kPairN + c * kEpiCols;
+        uint8_t* sb = stage_w + (c & 1) * kEpiTileBytes;
+        if (p.y_tma) {
+          // The staging tile written two chunks ago must have been read by its TMA store.
+          if (lane == 0) bulk_wait_group_read<1>();
+          __syncwarp();
         }
-        if (p.epi != GW_EPI_NONE) {
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+          uint32_t acc[32];
+          tc_ld_32x32b_x32(t_row + c * kEpiCols + h * 32, acc);
+          tc_wait_ld();
+          float f[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) f[j] = apply_epilogue(f[j], p.epi);
-        }
-        if (row_ok) {
-          if (p.y_vec_ok && n_base + 32 <= p.N) {
-            uint32_t packed[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-              packed[j] = static_cast<uint32_t>(Elem<DT>::from_f(f[2 * j])) |
-                          (static_cast<uint32_t>(Elem<DT>::from_f(f[2 * j + 1])) << 16);
-            uint4* dst = reinterpret_cast<uint4*>(yrow + n_base);
-#pragma unroll
-            for (int v = 0; v < 4; ++v)
-              dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
-          } else {
+          for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(acc[j]);
+          const int64_t n_base = n_chunk + h * 32;
+          if (p.bias) {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (n_base + j < p.N) yrow[n_base + j] = Elem<DT>::from_f(f[j]);
+              if (n_base + j < p.N) f[j] += Elem<DT>::to_f(__ldg(p.bias + n_base + j));
+          }
+          if (p.epi != GW_EPI_NONE) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) f[j] = apply_epilogue(f[j], p.epi);
+          }
+          uint32_t packed[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            packed[j] = static_cast<uint32_t>(Elem<DT>::from_f(f[2 * j])) |
+                        (static_cast<uint32_t>(Elem<DT>::from_f(f[2 * j + 1])) << 16);
+          if (p.y_tma) {
+            // Row `lane` of the staging tile, 128-byte swizzle: 16-byte unit
+            // v of the row lives at unit (v ^ (row & 7)).
+            uint4* srow = reinterpret_cast<uint4*>(sb + lane * (kEpiCols * 2));
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              srow[(h * 4 + v) ^ (lane & 7)] =
+                  make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+          } else if (row_ok) {
+            if (p.y_vec_ok && n_base + 32 <= p.N) {
+              uint4* dst = reinterpret_cast<uint4*>(yrow + n_base);
+#pragma unroll
+              for (int v = 0; v < 4; ++v)
+                dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (n_base + j < p.N) yrow[n_base + j] = Elem<DT>::from_f(f[j]);
+            }
+          }
+        }
+        if (p.y_tma) {
+          fence_proxy_async_smem();      // staging writes -> visible to the TMA unit
+          __syncwarp();
+          if (lane == 0) {
+            if (warp_row0 < p.M && n_chunk < p.N)
+              tma_store_2d(&tmap_y, smem_u32(sb), static_cast<int32_t>(n_chunk),
+                           static_cast<int32_t>(warp_row0));
+            bulk_commit_group();
           }
         }
       }
+      // All TMEM reads of this accumulator are complete: hand it back.
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -230,6 +282,9 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
         else mbar_arrive_cluster(b ? leader_tempty1 : leader_tempty0);
       }
     }
+    // Staging tiles stay valid (and y complete) until every TMA store has finished.
+    if (lane == 0) bulk_wait_group_all();
+    __syncwarp();
   }
 
   __syncthreads();
@@ -297,9 +352,12 @@ cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int6
   p.num_tiles = static_cast<int>(num_tiles);
   p.err = err;
 
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, ty;
   if (!make_tmap_2d_pair(&ta, a, M, K, lda, kBK2, kHalfM)) return cudaErrorInvalidValue;
   if (!make_tmap_2d_pair(&tb, w, N, K, ldw, kBK2, kHalfN)) return cudaErrorInvalidValue;
+  // TMA-store epilogue when y's rows are 16-byte aligned (else direct stores).
+  p.y_tma = p.y_vec_ok && make_tmap_2d_pair(&ty, y, M, N, ldy, kEpiCols, 32) ? 1 : 0;
+  if (!p.y_tma) ty = ta;     // not read by the kernel
 
   auto kern = dtype == GW_DTYPE_BF16 ? gemm_tc2_kernel<GW_DTYPE_BF16> : gemm_tc2_kernel<GW_DTYPE_F16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes2);
@@ -316,7 +374,7 @@ cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int6
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, tb, ta, p);
+  return cudaLaunchKernelEx(&cfg, kern, tb, ta, ty, p);
 }
 
 }  // namespace gw

@@ -139,7 +139,8 @@ def test_repeated_indices_and_out_of_range():
 def test_workspace_reuse_between_shapes(strategy):
     """One workspace serves successive calls of different K' (stale counters must not leak)."""
     ws = torch.empty(64 << 20, dtype=torch.uint8, device="cuda")
-    for M, K, N, kp in [(512, 1024, 384, 1000), (300, 512, 256, 64), (1024, 2048, 512, 1536)]:
+    for M, K, N, kp in [(512, 1024, 384, 1000), (300, 512, 256, 64), (1024, 2048, 512, 1536),
+                        (4096, 4096, 4096, 2048), (2500, 1024, 4000, 900), (4096, 4096, 4096, 1024)]:
         x = torch.randn(M, K, device="cuda", dtype=torch.float16)
         w = (torch.randn(N, K, device="cuda") / K ** 0.5).half()
         idx = torch.sort(torch.randperm(K, device="cuda")[:kp]).values
@@ -147,6 +148,70 @@ def test_workspace_reuse_between_shapes(strategy):
         _native.gather_gemm(x, pack_weight(w, idx), idx, y, strategy=strategy, workspace=ws)
         ref = (x.float()[:, idx] @ w.float()[:, idx].t()).half()
         torch.testing.assert_close(y, ref, **tols(torch.float16))
+
+
+# ----------------------------------------------------------------- CTA-pair GEMM, TMA-store epilogue
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("M,K,N,kp,bias,act", [
+    (4096, 4096, 4096, 2048, False, None),      # 256 whole 256 x 256 pair tiles
+    (2500, 4096, 4000, 2048, True, "gelu"),     # ragged last tile row and column: TMA clips the store
+    (2500, 512, 4000, 100, True, "gelu_tanh"),  # 2 k-blocks, the second one zero-filled past K'
+    (4096, 1024, 4608, 1000, True, None),       # 288 tiles, 3.9 waves
+])
+def test_pair_gemm_ragged_vs_fp32(dt, M, K, N, kp, bias, act):
+    torch_dt = DT[dt]
+    g = torch.Generator(device="cuda").manual_seed(M + N + kp)
+    x = torch.randn(M, K, device="cuda", dtype=torch_dt, generator=g)
+    w = (torch.randn(N, K, device="cuda", generator=g) / kp ** 0.5).to(torch_dt)
+    b = torch.randn(N, device="cuda", generator=g).to(torch_dt) if bias else None
+    idx = torch.sort(torch.randperm(K, device="cuda", generator=g)[:kp]).values
+    wp = pack_weight(w, idx)
+    ws = torch.empty(_native.gather_gemm_workspace_bytes(M, kp, torch_dt), dtype=torch.uint8, device="cuda")
+    big = torch.full((M, N + 8), float("nan"), device="cuda", dtype=torch_dt)
+    y = big[:, :N]                             # ldy = N + 8: still 16-byte rows, columns past N untouched
+    _native.gather_gemm(x, wp, idx, y, bias=b, activation=act, strategy="pregather", workspace=ws)
+    ref = F.linear(x.float()[:, idx], w.float()[:, idx], None if b is None else b.float())
+    if act == "gelu":
+        ref = F.gelu(ref)
+    elif act == "gelu_tanh":
+        ref = F.gelu(ref, approximate="tanh")
+    torch.testing.assert_close(y, ref.to(torch_dt), **tols(torch_dt))
+    assert torch.isnan(big[:, N:]).all()
+    assert _native.device_error(reset=False) & _native.DEVICE_ERR_WAIT_TIMEOUT == 0
+
+
+def test_pair_gemm_unaligned_ldy_direct_stores():
+    """ldy not a multiple of 8 on a pair-kernel shape: the epilogue falls back to direct stores."""
+    M, K, N, kp = 2048, 1024, 2048, 512
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(M, K, device="cuda", dtype=torch.float16, generator=g)
+    w = (torch.randn(N, K, device="cuda", generator=g) / kp ** 0.5).half()
+    idx = torch.sort(torch.randperm(K, device="cuda", generator=g)[:kp]).values
+    big = torch.zeros(M, N + 3, device="cuda", dtype=torch.float16)
+    y = big[:, :N]
+    ws = torch.empty(_native.gather_gemm_workspace_bytes(M, kp, torch.float16), dtype=torch.uint8, device="cuda")
+    _native.gather_gemm(x, pack_weight(w, idx), idx, y, strategy="pregather", workspace=ws)
+    ref = (x.float()[:, idx] @ w.float()[:, idx].t()).half()
+    torch.testing.assert_close(y, ref, **tols(torch.float16))
+    assert torch.count_nonzero(big[:, N:]).item() == 0
+
+
+def test_chained_layers_pdl():
+    """Layer 2's gather reads layer 1's output: the programmatic-dependent launches must order them."""
+    M, K = 4096, 4096
+    g = torch.Generator(device="cuda").manual_seed(9)
+    x = torch.randn(M, K, device="cuda", dtype=torch.float16, generator=g)
+    ws = torch.empty(64 << 20, dtype=torch.uint8, device="cuda")
+    h = x
+    ref = x.float()
+    for layer in range(4):
+        w = (torch.randn(K, K, device="cuda", generator=g) / 45.0).half()
+        idx = torch.sort(torch.randperm(K, device="cuda", generator=g)[:2048]).values
+        out = torch.empty(M, K, device="cuda", dtype=torch.float16)
+        _native.gather_gemm(h, pack_weight(w, idx), idx, out, strategy="pregather", workspace=ws)
+        h = out
+        ref = (ref.half().float()[:, idx] @ w.float()[:, idx].t())
+    torch.testing.assert_close(h, ref.half(), **tols(torch.float16))
 
 
 def test_no_wait_timeouts_after_suite():
