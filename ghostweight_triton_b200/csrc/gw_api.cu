@@ -59,6 +59,24 @@ void* tensor_map_encoder() {
   return fn;
 }
 
+bool make_tmap_kmajor(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
+                      int box_cols, int box_rows) {
+  using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                     const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                     const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                     CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  auto encode = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
+  if (!encode) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2u};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides,
+                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
 }  // namespace gw
 
 namespace {
@@ -228,6 +246,26 @@ size_t gemm_ws_header(int64_t n_alive) {
 }
 }  // namespace
 
+namespace {
+// Dense-A GEMM y = act(a @ w^T + bias) on the kernel that suits the shape:
+// the CTA-pair kernel when there are enough 256 x 256 tiles for every SM
+// pair, cluster split-K when the output has too few tiles to occupy half of
+// the SMs (decode-sized M), else the single-CTA persistent kernel.
+cudaError_t launch_dense_gemm(const void* a, int dtype, int64_t M, int64_t K, int64_t lda,
+                              const void* w, int64_t N, int64_t ldw, const void* bias, int epilogue,
+                              void* y, int64_t ldy, const gw::DeviceInfo* d, cudaStream_t s) {
+  if (gw::use_pair_gemm(M, N, d->sm_count))
+    return gw::launch_gemm_tc2(a, dtype, M, K, lda, w, N, ldw, bias, epilogue, y, ldy,
+                               d->err_word, d->sm_count, s);
+  const gw::SplitKPlan sk = gw::plan_splitk(M, N, K, d->sm_count);
+  if (sk.split >= 2)
+    return gw::launch_gemm_splitk(sk, a, dtype, M, K, lda, w, N, ldw, bias, epilogue, y, ldy,
+                                  d->err_word, s);
+  return gw::launch_gemm_tc(0, a, dtype, M, K, lda, w, N, ldw, nullptr, K, bias, epilogue, y, ldy,
+                            d->err_word, d->sm_count, s);
+}
+}  // namespace
+
 size_t gw_gather_gemm_workspace_bytes(int64_t M, int64_t n_alive, int dtype) {
   if (M <= 0 || n_alive <= 0 || dtype == GW_DTYPE_F32) return 0;
   return gemm_ws_header(n_alive) +
@@ -286,12 +324,8 @@ int gw_gather_gemm(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
     e = gw::launch_gather_columns(x, dtype, M, ldx, K, idx, n_alive, xg, ldp, n_alive,
                                   d->err_word, d->sm_count, s);
     if (e != cudaSuccess) return cuda_fail(e);
-    if (gw::use_pair_gemm(M, N, d->sm_count))
-      e = gw::launch_gemm_tc2(xg, dtype, M, n_alive, ldp, w_packed, N, ldw, bias, epilogue, y, ldy,
-                              d->err_word, d->sm_count, s);
-    else
-      e = gw::launch_gemm_tc(0, xg, dtype, M, n_alive, ldp, w_packed, N, ldw, nullptr, n_alive,
-                             bias, epilogue, y, ldy, d->err_word, d->sm_count, s);
+    e = launch_dense_gemm(xg, dtype, M, n_alive, ldp, w_packed, N, ldw, bias, epilogue, y, ldy,
+                          d, s);
   } else {
     e = gw::launch_gemm_tc(2, x, dtype, M, K, ldx, w_packed, N, ldw, idx, n_alive, bias,
                            epilogue, y, ldy, d->err_word, d->sm_count, s, xg, ldp, counters);
@@ -320,12 +354,7 @@ int gw_packed_gemm(const void* a, int dtype, int64_t M, int64_t K, int64_t lda,
   if (!a || !w_packed) return GW_ERR_NULL;
   if (!aligned16(a) || !aligned16(w_packed) || (lda % 8) != 0 || (ldw % 8) != 0)
     return GW_ERR_ALIGN;
-  if (gw::use_pair_gemm(M, N, d->sm_count))
-    e = gw::launch_gemm_tc2(a, dtype, M, K, lda, w_packed, N, ldw, bias, epilogue, y, ldy,
-                            d->err_word, d->sm_count, s);
-  else
-    e = gw::launch_gemm_tc(0, a, dtype, M, K, lda, w_packed, N, ldw, nullptr, K, bias,
-                           epilogue, y, ldy, d->err_word, d->sm_count, s);
+  e = launch_dense_gemm(a, dtype, M, K, lda, w_packed, N, ldw, bias, epilogue, y, ldy, d, s);
   return e == cudaSuccess ? GW_OK : cuda_fail(e);
 }
 

@@ -1,0 +1,448 @@
+// K3, decode-sized variant: split-K over a thread-block cluster, reduced in
+// distributed shared memory.
+//
+//   y[m, n] = act( sum_j a[m, j] * w[n, j] + bias[n] )      a = x' (dense, compacted)
+//
+// When the output has too few 128 x BN tiles to occupy the SMs (M of a few
+// rows to a few hundred: decoding, small batches), the persistent kernels
+// leave most SMs idle and each busy SM streams a long k range alone. Here a
+// cluster of S CTAs (S = 2, 4 or 8) shares one output tile: CTA s of the
+// cluster accumulates k-blocks [s * nkb / S, (s + 1) * nkb / S) on its tensor
+// cores (tcgen05, TMEM accumulator), so S times as many SMs stream W' and x'.
+// The partial tiles never leave the chip:
+//   1. each CTA drains its accumulator (valid rows only) into its own shared
+//      memory, fp32, row stride BN + 4 words (bank-conflict-free 16-byte rows);
+//   2. cluster barrier;
+//   3. CTA s reduces column slice [s * BN / S, (s + 1) * BN / S) of the tile,
+//      reading the S partial tiles over DSMEM in fixed order s' = 0..S-1 (the
+//      result does not depend on timing), adds bias, applies the activation,
+//      rounds once and stores y;
+//   4. cluster barrier (peers' shared memory stays valid until every read).
+// The cluster is gang-scheduled, so its barriers cannot wait on a CTA that is
+// not running; every other wait is bounded (gw_common.cuh). No TMA multicast.
+//
+// Roles (192 threads): warp 0 TMA producer, warp 1 TMEM allocator + MMA
+// issuer, warps 2..5 TMEM drain; all six warps share the reduction.
+#include <algorithm>
+#include <initializer_list>
+#include <mutex>
+
+#include <cuda.h>
+
+#include "gw_common.cuh"
+#include "gw_internal.h"
+
+namespace gw {
+
+namespace {
+
+constexpr int kSkBM = 128;
+constexpr int kSkBK = 64;
+constexpr int kSkThreads = 192;
+
+template <int BN>
+struct SkCfg {
+  static constexpr int kABytes = kSkBM * kSkBK * 2;
+  static constexpr int kBBytes = BN * kSkBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStagesFit = (196 * 1024) / kStageBytes;
+  static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
+  static constexpr int kRedStride = BN + 4;                       // floats per partial row
+  static constexpr int kRedBytes = kSkBM * kRedStride * 4;
+  static constexpr int kRingBytes =
+      kStages * kStageBytes > kRedBytes ? kStages * kStageBytes : kRedBytes;
+  static constexpr int kTmemCols = BN < 32 ? 32 : BN;             // power of two >= 32
+  static constexpr int kSmemBytes = 1024 + kRingBytes + 256;
+  static_assert(kSmemBytes <= 232448, "shared memory budget per CTA");
+};
+
+struct SkParams {
+  int64_t M;
+  int64_t N;
+  const uint16_t* bias;
+  int epi;
+  uint16_t* y;
+  int64_t ldy;
+  int y_vec_ok;              // 8-byte stores of four outputs allowed
+  int num_kb;
+  int m_tiles;
+  int split;                 // cluster size S
+  int a_tx_bytes;            // bytes of one x' box (its rows: min(M rounded up to 8, 128))
+  unsigned int* err;
+};
+
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t cluster_addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(cluster_addr) : "memory");
+  return v;
+}
+
+// CTA `rank` of the cluster sums column slice [rank * BN / S, (rank + 1) * BN / S)
+// of the S partial tiles (row stride BN + 4 floats at `red_local` in every
+// CTA) and emits it. A task is one row x four columns; a thread takes
+// 16 / S tasks per round and issues all their DSMEM loads before the first
+// add, so the latencies overlap; each task is summed in rank order.
+template <int S, int BN, int DT>
+__device__ __forceinline__ void reduce_slice(const SkParams& p, uint32_t red_local, int rank,
+                                             int m_blk, int n_blk, int rows_valid, bool ok) {
+  constexpr int kStride = SkCfg<BN>::kRedStride;
+  constexpr int kSlice = BN / 4 / S;   // float4 groups per row in this CTA's slice
+  constexpr int kPerRound = 16 / S;
+  const int g0 = rank * kSlice;
+  const int tasks = rows_valid * kSlice;
+  for (int t0 = threadIdx.x; t0 < tasks; t0 += kPerRound * kSkThreads) {
+    float4 v[kPerRound][S];
+#pragma unroll
+    for (int u = 0; u < kPerRound; ++u) {
+      const int t = t0 + u * kSkThreads;
+      if (t < tasks) {
+        const int r = t / kSlice;
+        const int g = g0 + (t - r * kSlice);
+        const uint32_t off = static_cast<uint32_t>((r * kStride + g * 4) * 4);
+#pragma unroll
+        for (int s = 0; s < S; ++s) v[u][s] = ld_dsmem_f4(mapa_shared(red_local + off, s));
+      }
+    }
+    if (!ok) continue;                 // this CTA's accumulator never arrived (error recorded)
+#pragma unroll
+    for (int u = 0; u < kPerRound; ++u) {
+      const int t = t0 + u * kSkThreads;
+      if (t >= tasks) continue;
+      float4 acc = v[u][0];
+#pragma unroll
+      for (int s = 1; s < S; ++s) {
+        acc.x += v[u][s].x; acc.y += v[u][s].y; acc.z += v[u][s].z; acc.w += v[u][s].w;
+      }
+      const int r = t / kSlice;
+      const int g = g0 + (t - r * kSlice);
+      float f[4] = {acc.x, acc.y, acc.z, acc.w};
+      const int64_t n0 = static_cast<int64_t>(n_blk) * BN + g * 4;
+      const int64_t m = static_cast<int64_t>(m_blk) * kSkBM + r;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (p.bias && n0 + j < p.N) f[j] += Elem<DT>::to_f(__ldg(p.bias + n0 + j));
+        if (p.epi != GW_EPI_NONE) f[j] = apply_epilogue(f[j], p.epi);
+      }
+      uint16_t* yp = p.y + m * p.ldy + n0;
+      if (p.y_vec_ok && n0 + 4 <= p.N) {
+        const uint32_t lo = static_cast<uint32_t>(Elem<DT>::from_f(f[0])) |
+                            (static_cast<uint32_t>(Elem<DT>::from_f(f[1])) << 16);
+        const uint32_t hi = static_cast<uint32_t>(Elem<DT>::from_f(f[2])) |
+                            (static_cast<uint32_t>(Elem<DT>::from_f(f[3])) << 16);
+        *reinterpret_cast<uint2*>(yp) = make_uint2(lo, hi);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (n0 + j < p.N) yp[j] = Elem<DT>::from_f(f[j]);
+      }
+    }
+  }
+}
+
+template <int BN, int DT>
+__global__ void __launch_bounds__(kSkThreads, 1)
+gemm_splitk_kernel(const __grid_constant__ CUtensorMap tmap_b,
+                   const __grid_constant__ CUtensorMap tmap_a, const SkParams p) {
+  using C = SkCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_s = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_s & 1023u)) & 1023u);
+  const uint32_t sbase = smem_u32(smem);
+  uint8_t* bar_region = smem + C::kRingBytes;
+  const uint32_t bar0 = smem_u32(bar_region);
+  auto full = [&](int s) { return bar0 + 8u * s; };
+  auto empty = [&](int s) { return bar0 + 8u * (C::kStages + s); };
+  const uint32_t tfull = bar0 + 8u * (2 * C::kStages);
+  const uint32_t drain_bar = tfull + 8u;
+  static_assert(8 * (2 * 8 + 2) <= 192, "barrier region overflows into the TMEM slot");
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_region + 192);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_region + 196);
+  volatile int* acc_ok = reinterpret_cast<volatile int*>(bar_region + 200);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int rank = static_cast<int>(cluster_ctarank());   // == blockIdx.x, the k split
+  const int tile = static_cast<int>(blockIdx.y);
+  const int m_blk = tile % p.m_tiles;
+  const int n_blk = tile / p.m_tiles;
+  const int kb0 = static_cast<int>(static_cast<int64_t>(rank) * p.num_kb / p.split);
+  const int kb1 = static_cast<int>(static_cast<int64_t>(rank + 1) * p.num_kb / p.split);
+  const int64_t rows_left = p.M - static_cast<int64_t>(m_blk) * kSkBM;
+  const int rows_valid = rows_left >= kSkBM ? kSkBM : static_cast<int>(rows_left);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(empty(s), 1);
+    }
+    mbar_init(tfull, 1);
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    *acc_ok = 0;
+    mbar_init_fence();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      asm volatile("griddepcontrol.wait;" ::: "memory");   // x' may come from the previous kernel
+      int issued = 0;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb, ++issued) {
+        const int s = issued % C::kStages;
+        const uint32_t ph = (issued / C::kStages) & 1u;
+        if (!mbar_wait(empty(s), ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
+        const uint32_t a_s = sbase + s * C::kStageBytes;
+        mbar_arrive_expect_tx(full(s), C::kBBytes + p.a_tx_bytes);
+        tma_load_2d(a_s + C::kABytes, &tmap_b, kb * kSkBK, n_blk * BN, full(s));
+        tma_load_2d(a_s, &tmap_a, kb * kSkBK, m_blk * kSkBM, full(s));
+      }
+      if (!ok) {
+        // Loads still in flight complete before the ring is reused or the CTA exits.
+        const int first = issued > C::kStages ? issued - C::kStages : 0;
+        for (int i = first; i < issued; ++i)
+          mbar_wait(full(i % C::kStages), (i / C::kStages) & 1u, nullptr, p.err, 100000000ull);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(DT == GW_DTYPE_BF16 ? 1u : 0u, kSkBM, BN);
+      bool ok = true;
+      int used = 0;
+      for (int kb = kb0; kb < kb1; ++kb, ++used) {
+        const int s = used % C::kStages;
+        const uint32_t ph = (used / C::kStages) & 1u;
+        if (!mbar_wait(full(s), ph, abort_flag, p.err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a_s = sbase + s * C::kStageBytes;
+        const uint64_t a_desc = smem_desc_kmajor_sw128(a_s);
+        const uint64_t b_desc = smem_desc_kmajor_sw128(a_s + C::kABytes);
+#pragma unroll
+        for (int k = 0; k < kSkBK / 16; ++k)
+          tc_mma_f16(tmem_base, a_desc + 2u * k, b_desc + 2u * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+        tc_commit(empty(s));
+      }
+      if (ok) tc_commit(tfull);
+      else *abort_flag = 1;            // the drain warps stop waiting for tfull
+      // Every MMA has finished reading shared memory and writing TMEM before
+      // the ring is reused as the reduction buffer and TMEM is freed.
+      tc_commit(drain_bar);
+      mbar_wait(drain_bar, 0u, nullptr, p.err, 100000000ull);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ TMEM drain
+    // Warp w reads TMEM lanes 32 (w % 4) .. +31 = rows of the tile.
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    if (mbar_wait(tfull, 0u, abort_flag, p.err)) {
+      tc_fence_after();
+      if (q * 32 < rows_valid) {
+        float* red_row = reinterpret_cast<float*>(smem) + row * C::kRedStride;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t acc[32];
+          tc_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + c * 32, acc);
+          tc_wait_ld();
+          if (row < rows_valid) {
+            float4* dst = reinterpret_cast<float4*>(red_row + c * 32);
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              dst[v] = make_float4(__uint_as_float(acc[4 * v]), __uint_as_float(acc[4 * v + 1]),
+                                   __uint_as_float(acc[4 * v + 2]), __uint_as_float(acc[4 * v + 3]));
+          }
+        }
+      }
+      if (q == 0 && lane == 0) *acc_ok = 1;
+    }
+    tc_fence_before();
+  }
+
+  // The ring must be idle before it is overwritten: the drain above runs only
+  // after tfull, which follows the last MMA; on an error path the MMA warp has
+  // drained the tensor pipe and the producer its loads before this barrier.
+  __syncthreads();
+  cluster_sync();                      // every partial tile of the cluster is in shared memory
+
+  // ------------------------------------------------------------ reduce-scatter over DSMEM
+  {
+    const bool ok = *acc_ok != 0;
+    if (p.split == 8) reduce_slice<8, BN, DT>(p, smem_u32(smem), rank, m_blk, n_blk, rows_valid, ok);
+    else if (p.split == 4) reduce_slice<4, BN, DT>(p, smem_u32(smem), rank, m_blk, n_blk, rows_valid, ok);
+    else reduce_slice<2, BN, DT>(p, smem_u32(smem), rank, m_blk, n_blk, rows_valid, ok);
+  }
+
+  cluster_sync();                      // peers have finished reading this CTA's partial tile
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+template <int BN, int DT>
+cudaError_t launch_sk(const CUtensorMap& tb, const CUtensorMap& ta, const SkParams& p,
+                      int64_t tiles, cudaStream_t stream) {
+  using C = SkCfg<BN>;
+  auto kern = gemm_splitk_kernel<BN, DT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       C::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.split), static_cast<unsigned>(tiles));
+  cfg.blockDim = dim3(kSkThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(p.split);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kern, tb, ta, p);
+}
+
+// Clusters of S CTAs of the BN-wide kernel that fit on the current device at
+// once (occupancy query, cached per device). Clusters of 8 CTAs that each
+// need most of an SM's shared memory do not tile every GPC: on a 148-SM B200
+// only 15 fit, not 18.
+int max_active_clusters(int bn, int s) {
+  static std::mutex mu;
+  static int cache[64][4][4];
+  static bool init[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  const int bi = bn == 256 ? 0 : bn == 128 ? 1 : bn == 64 ? 2 : 3;
+  const int si = s == 8 ? 0 : s == 4 ? 1 : s == 2 ? 2 : 3;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!init[dev]) {
+    for (auto& row : cache[dev])
+      for (int& v : row) v = -1;
+    init[dev] = true;
+  }
+  int& slot = cache[dev][bi][si];
+  if (slot >= 0) return slot;
+  auto query = [&](auto kern, int smem) {
+    int n = 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(s), 1);
+    cfg.blockDim = dim3(kSkThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(s);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+    return n;
+  };
+  int n = 0;
+  switch (bn) {
+    case 256: n = query(gemm_splitk_kernel<256, GW_DTYPE_F16>, SkCfg<256>::kSmemBytes); break;
+    case 128: n = query(gemm_splitk_kernel<128, GW_DTYPE_F16>, SkCfg<128>::kSmemBytes); break;
+    case 64: n = query(gemm_splitk_kernel<64, GW_DTYPE_F16>, SkCfg<64>::kSmemBytes); break;
+    default: n = query(gemm_splitk_kernel<32, GW_DTYPE_F16>, SkCfg<32>::kSmemBytes); break;
+  }
+  (void)cudaGetLastError();
+  slot = n > 0 ? n : 0;
+  return slot;
+}
+
+}  // namespace
+
+SplitKPlan plan_splitk(int64_t M, int64_t N, int64_t K, int sm_count) {
+  SplitKPlan best;
+  const int64_t sms = sm_count > 0 ? sm_count : 148;
+  const int64_t m_tiles = (M + kSkBM - 1) / kSkBM;
+  const int64_t num_kb = (K + kSkBK - 1) / kSkBK;
+  if (M <= 0 || N <= 0 || num_kb < 2) return best;
+  // The persistent kernels already fill at least half of the SMs.
+  if (m_tiles * ((N + 255) / 256) * 2 > sms) return best;
+  // Most CTAs in a single wave of clusters; ties keep the wider tile (less
+  // re-reading of x') and then the larger cluster.
+  int64_t best_ctas = 0;
+  for (int bn : {256, 128, 64, 32}) {
+    const int64_t tiles = m_tiles * ((N + bn - 1) / bn);
+    for (int s : {8, 4, 2}) {
+      if (s > num_kb || tiles * s > sms) continue;
+      if (tiles > max_active_clusters(bn, s)) continue;
+      const int64_t ctas = tiles * s;
+      if (ctas > best_ctas) {
+        best_ctas = ctas;
+        best.bn = bn;
+        best.split = s;
+        best.tiles = tiles;
+      }
+    }
+  }
+  return best;
+}
+
+cudaError_t launch_gemm_splitk(const SplitKPlan& plan, const void* a, int dtype, int64_t M,
+                               int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,
+                               const void* bias, int epilogue, void* y, int64_t ldy,
+                               unsigned int* err, cudaStream_t stream) {
+  if (plan.split < 2 || plan.split > 8 || plan.tiles <= 0 || plan.tiles > 65535)
+    return cudaErrorInvalidValue;
+  SkParams p{};
+  p.M = M;
+  p.N = N;
+  p.bias = static_cast<const uint16_t*>(bias);
+  p.epi = epilogue;
+  p.y = static_cast<uint16_t*>(y);
+  p.ldy = ldy;
+  p.y_vec_ok = ((reinterpret_cast<uintptr_t>(y) & 7u) == 0 && (ldy % 4) == 0) ? 1 : 0;
+  p.num_kb = static_cast<int>((K + kSkBK - 1) / kSkBK);
+  p.m_tiles = static_cast<int>((M + kSkBM - 1) / kSkBM);
+  p.split = plan.split;
+  p.err = err;
+  if (p.num_kb < plan.split) return cudaErrorInvalidValue;
+  // With fewer than 128 rows the x' box covers only the rows that exist; the
+  // MMA still reads 128 rows of shared memory, and the rows past the box hold
+  // stale data that reaches only output rows that are never stored.
+  const int a_rows = M >= kSkBM ? kSkBM : static_cast<int>((M + 7) / 8 * 8);
+  p.a_tx_bytes = a_rows * kSkBK * 2;
+
+  CUtensorMap ta, tb;
+  if (!make_tmap_kmajor(&ta, a, M, K, lda, kSkBK, a_rows)) return cudaErrorInvalidValue;
+  if (!make_tmap_kmajor(&tb, w, N, K, ldw, kSkBK, plan.bn)) return cudaErrorInvalidValue;
+  const bool bf = dtype == GW_DTYPE_BF16;
+  switch (plan.bn) {
+    case 256: return bf ? launch_sk<256, GW_DTYPE_BF16>(tb, ta, p, plan.tiles, stream)
+                        : launch_sk<256, GW_DTYPE_F16>(tb, ta, p, plan.tiles, stream);
+    case 128: return bf ? launch_sk<128, GW_DTYPE_BF16>(tb, ta, p, plan.tiles, stream)
+                        : launch_sk<128, GW_DTYPE_F16>(tb, ta, p, plan.tiles, stream);
+    case 64: return bf ? launch_sk<64, GW_DTYPE_BF16>(tb, ta, p, plan.tiles, stream)
+                       : launch_sk<64, GW_DTYPE_F16>(tb, ta, p, plan.tiles, stream);
+    case 32: return bf ? launch_sk<32, GW_DTYPE_BF16>(tb, ta, p, plan.tiles, stream)
+                       : launch_sk<32, GW_DTYPE_F16>(tb, ta, p, plan.tiles, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace gw

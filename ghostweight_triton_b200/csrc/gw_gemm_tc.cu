@@ -422,28 +422,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-// 2-D K-major tile map over a [rows, cols] 16-bit matrix with row stride ld,
-// box = box_cols x box_rows, 128-byte swizzle, zero fill outside the matrix.
-bool make_tmap_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
-                  int box_cols, int box_rows) {
-  auto encode = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
-  if (!encode) return false;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2u};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims,
-                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
-
 template <int BN, int DT, int AMODE>
 cudaError_t launch_tc(const CUtensorMap& tb, const CUtensorMap& ta, const TcParams& p,
                       int sm_count, cudaStream_t stream) {
@@ -539,14 +517,14 @@ cudaError_t launch_gemm_tc(int a_mode, const void* x, int dtype, int64_t M, int6
   p.kb_ready = kb_ready;
 
   CUtensorMap tb, ta;
-  if (!make_tmap_2d(&tb, w, N, n_alive, ldw, kBK, BN)) return cudaErrorInvalidValue;
+  if (!make_tmap_kmajor(&tb, w, N, n_alive, ldw, kBK, BN)) return cudaErrorInvalidValue;
   if (a_mode == kASmemGather) {
     ta = tb;   // unused by the shared-memory gather variant
   } else if (a_mode == kATma) {
-    if (!make_tmap_2d(&ta, x, M, n_alive, ldx, kBK, kBM)) return cudaErrorInvalidValue;
+    if (!make_tmap_kmajor(&ta, x, M, n_alive, ldx, kBK, kBM)) return cudaErrorInvalidValue;
   } else {
     if (!scratch_xg || !kb_ready || (ldg % 8) != 0) return cudaErrorInvalidValue;
-    if (!make_tmap_2d(&ta, scratch_xg, M, n_alive, ldg, kBK, kBM)) return cudaErrorInvalidValue;
+    if (!make_tmap_kmajor(&ta, scratch_xg, M, n_alive, ldg, kBK, kBM)) return cudaErrorInvalidValue;
     cudaError_t e = cudaMemsetAsync(kb_ready, 0, static_cast<size_t>(num_kb) * sizeof(unsigned int),
                                     stream);
     if (e != cudaSuccess) return e;

@@ -295,25 +295,6 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
   }
 }
 
-using EncodeTiledFn2 = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-bool make_tmap_2d_pair(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
-                       int box_cols, int box_rows) {
-  auto encode = reinterpret_cast<EncodeTiledFn2>(tensor_map_encoder());
-  if (!encode) return false;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2u};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
-  cuuint32_t estr[2] = {1, 1};
-  return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides,
-                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
-         CUDA_SUCCESS;
-}
-
 }  // namespace
 
 bool use_pair_gemm(int64_t M, int64_t N, int sm_count) {
@@ -353,10 +334,10 @@ cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int6
   p.err = err;
 
   CUtensorMap ta, tb, ty;
-  if (!make_tmap_2d_pair(&ta, a, M, K, lda, kBK2, kHalfM)) return cudaErrorInvalidValue;
-  if (!make_tmap_2d_pair(&tb, w, N, K, ldw, kBK2, kHalfN)) return cudaErrorInvalidValue;
+  if (!make_tmap_kmajor(&ta, a, M, K, lda, kBK2, kHalfM)) return cudaErrorInvalidValue;
+  if (!make_tmap_kmajor(&tb, w, N, K, ldw, kBK2, kHalfN)) return cudaErrorInvalidValue;
   // TMA-store epilogue when y's rows are 16-byte aligned (else direct stores).
-  p.y_tma = p.y_vec_ok && make_tmap_2d_pair(&ty, y, M, N, ldy, kEpiCols, 32) ? 1 : 0;
+  p.y_tma = p.y_vec_ok && make_tmap_kmajor(&ty, y, M, N, ldy, kEpiCols, 32) ? 1 : 0;
   if (!p.y_tma) ty = ta;     // not read by the kernel
 
   auto kern = dtype == GW_DTYPE_BF16 ? gemm_tc2_kernel<GW_DTYPE_BF16> : gemm_tc2_kernel<GW_DTYPE_F16>;

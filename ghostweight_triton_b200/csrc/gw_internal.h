@@ -4,6 +4,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace gw {
@@ -70,7 +71,24 @@ cudaError_t launch_gemm_f32(const float* x, int64_t M, int64_t K, int64_t ldx, c
                             const float* bias, int epilogue, float* y, int64_t ldy,
                             unsigned int* err, cudaStream_t stream);
 
+// gw_gemm_splitk.cu: split-K over a cluster of `split` CTAs reduced in DSMEM,
+// for dense-A GEMMs whose output has too few tiles to occupy the SMs.
+struct SplitKPlan {
+  int bn = 0;            // tile width (32 .. 256)
+  int split = 1;         // cluster size; 1 = not worth it (use the persistent kernels)
+  int64_t tiles = 0;
+};
+SplitKPlan plan_splitk(int64_t M, int64_t N, int64_t K, int sm_count);
+cudaError_t launch_gemm_splitk(const SplitKPlan& plan, const void* a, int dtype, int64_t M,
+                               int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,
+                               const void* bias, int epilogue, void* y, int64_t ldy,
+                               unsigned int* err, cudaStream_t stream);
+
 // Driver entry point for cuTensorMapEncodeTiled (resolved once, no libcuda link).
 void* tensor_map_encoder();
+// 2-D tile map over a [rows, cols] 16-bit row-major matrix with row stride ld
+// (elements): box = box_cols x box_rows, 128-byte swizzle, zero fill outside.
+bool make_tmap_kmajor(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
+                      int box_cols, int box_rows);
 
 }  // namespace gw

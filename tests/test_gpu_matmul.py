@@ -214,6 +214,67 @@ def test_chained_layers_pdl():
     torch.testing.assert_close(h, ref.half(), **tols(torch.float16))
 
 
+# ----------------------------------------------------------------- cluster split-K (decode-sized M)
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("M,K,N,kp,bias,act", [
+    (16, 4096, 4096, 2048, False, None),        # 16 tiles of 256, clusters of 8
+    (1, 4096, 768, 2048, True, "gelu"),         # 12 tiles of 64, clusters of 8; one valid row
+    (100, 4096, 1000, 1500, True, "gelu_tanh"), # ragged last tile, 3 k-blocks per CTA
+    (128, 1024, 4096, 130, True, None),         # 3 k-blocks: clusters of 2, uneven ranges
+    (256, 4096, 2304, 4096, False, "gelu"),     # 2 m-tiles x 9 n-tiles, clusters of 8
+    (33, 768, 3072, 384, True, None),           # GPT-2 MLP-in at decode: tiles of 128, clusters of 4
+    (16, 3072, 768, 1536, True, None),          # GPT-2 MLP-out at decode
+    (512, 4096, 4096, 2048, True, None),        # 64 tiles of 256, clusters of 2
+])
+def test_cluster_split_k_vs_fp32(dt, M, K, N, kp, bias, act):
+    torch_dt = DT[dt]
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + kp)
+    x = torch.randn(M, K, device="cuda", dtype=torch_dt, generator=g)
+    w = (torch.randn(N, K, device="cuda", generator=g) / kp ** 0.5).to(torch_dt)
+    b = torch.randn(N, device="cuda", generator=g).to(torch_dt) if bias else None
+    idx = torch.sort(torch.randperm(K, device="cuda", generator=g)[:kp]).values
+    wp = pack_weight(w, idx)
+    ws = torch.empty(_native.gather_gemm_workspace_bytes(M, kp, torch_dt), dtype=torch.uint8, device="cuda")
+    ys = []
+    for _ in range(3):                          # fixed reduction order: bitwise reproducible
+        y = torch.full((M, N), float("nan"), device="cuda", dtype=torch_dt)
+        _native.gather_gemm(x, wp, idx, y, bias=b, activation=act, strategy="pregather", workspace=ws)
+        ys.append(y)
+    ref = F.linear(x.float()[:, idx], w.float()[:, idx], None if b is None else b.float())
+    if act == "gelu":
+        ref = F.gelu(ref)
+    elif act == "gelu_tanh":
+        ref = F.gelu(ref, approximate="tanh")
+    torch.testing.assert_close(ys[0], ref.to(torch_dt), **tols(torch_dt))
+    assert torch.equal(ys[0], ys[1]) and torch.equal(ys[1], ys[2])
+
+
+@pytest.mark.parametrize("M,N,K", [(16, 4096, 2048), (128, 4096, 1024), (7, 768, 3072), (300, 1000, 640)])
+def test_packed_gemm_decode_shapes(M, N, K):
+    g = torch.Generator(device="cuda").manual_seed(N + K)
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16, generator=g)
+    w = (torch.randn(N, K, device="cuda", generator=g) / K ** 0.5).bfloat16()
+    b = torch.randn(N, device="cuda", generator=g).bfloat16()
+    y = packed_linear(a, pack_weight(w, torch.arange(K, device="cuda")), bias=b, activation="gelu")
+    ref = F.gelu(F.linear(a.float(), w.float(), b.float())).bfloat16()
+    torch.testing.assert_close(y, ref, **tols(torch.bfloat16))
+
+
+def test_cluster_split_k_unaligned_ldy():
+    """ldy odd: the reduce-scatter falls back to 2-byte stores."""
+    M, K, N, kp = 16, 2048, 1000, 1024
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.randn(M, K, device="cuda", dtype=torch.float16, generator=g)
+    w = (torch.randn(N, K, device="cuda", generator=g) / kp ** 0.5).half()
+    idx = torch.sort(torch.randperm(K, device="cuda", generator=g)[:kp]).values
+    big = torch.zeros(M, N + 1, device="cuda", dtype=torch.float16)
+    y = big[:, :N]
+    _native.gather_gemm(x, pack_weight(w, idx), idx, y)
+    ref = (x.float()[:, idx] @ w.float()[:, idx].t()).half()
+    torch.testing.assert_close(y, ref, **tols(torch.float16))
+    assert torch.count_nonzero(big[:, N]).item() == 0
+
+
 def test_no_wait_timeouts_after_suite():
     assert _native.device_error(reset=False) & _native.DEVICE_ERR_WAIT_TIMEOUT == 0
 
