@@ -90,6 +90,55 @@ def test_out_of_range_index_reads_zero_and_flags():
     assert _native.validate_indices(idx, 16) == 1
 
 
+# ----------------------------------------------------------------- window gather (TMA, >= 256 rows)
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("rows,cols,sp,pattern", [
+    (4096, 4096, 0.5, "random"),    # 128-column chunks, one 256-column box per window
+    (4096, 4096, 0.0, "random"),    # dense: 256-column chunks, windows straddle two boxes
+    (1000, 4096, 0.9, "random"),    # sparse: 32-column chunks; ragged last row block
+    (300, 4096, 0.75, "block"),     # 64-column dead blocks
+    (257, 1000, 0.33, "random"),    # columns not a multiple of the box: zero fill past K
+    (512, 8192, 0.6875, "block"),   # the sharded-MLP pattern (128-column blocks)
+])
+def test_window_gather_bit_exact(dt, rows, cols, sp, pattern):
+    x = rand_matrix((rows, cols), rows + cols, dt)
+    idx = alive_from_dead(cols, dead_columns(cols, sp, rows, pattern, 128 if cols == 8192 else 64))
+    xd = to_dev(x)
+    idd = torch.from_numpy(idx).cuda()
+    ld = max(-(-len(idx) // 64) * 64, 64)
+    out = torch.full((rows, ld), 7, dtype=xd.dtype, device="cuda")
+    _native.gather_columns(xd, idd, out, pad_to=ld)
+    ref = O.gather_columns(x, idx)
+    got = to_np(out)
+    assert np.array_equal(got[:, :len(idx)].view(np.uint8), np.ascontiguousarray(ref).view(np.uint8))
+    assert (got[:, len(idx):] == 0).all()          # padding columns written as zeros
+
+
+@pytest.mark.parametrize("case", ["unsorted", "repeated", "bad_index", "wide_window"])
+def test_window_gather_fallbacks(case):
+    """Chunks whose window does not fit (or holds a bad index) are gathered directly."""
+    rows, cols = 512, 4096
+    x = rand_matrix((rows, cols), 11, "f16")
+    rng = np.random.default_rng(5)
+    if case == "unsorted":
+        idx = rng.permutation(cols)[:2048]
+    elif case == "repeated":
+        idx = np.sort(rng.integers(0, cols, 2048))
+    elif case == "bad_index":
+        idx = np.sort(rng.permutation(cols)[:2048])
+        idx[700] = cols + 5
+    else:                                          # dense, then every 8th column: windows too wide
+        idx = np.concatenate([np.arange(0, 1024), np.arange(1024, cols, 8)])
+    _native.device_error(reset=True)
+    out = torch.empty(rows, len(idx), dtype=torch.float16, device="cuda")
+    _native.gather_columns(to_dev(x), torch.from_numpy(idx).cuda(), out)
+    ref = O.gather_columns(x, np.where(idx < cols, idx, 0))
+    if case == "bad_index":
+        ref[:, 700] = 0
+        assert _native.device_error(reset=True) & _native.DEVICE_ERR_BAD_INDEX
+    assert np.array_equal(to_np(out), ref)
+
+
 class TestReferenceSuite:
     """ghostweight_triton tests/test_gather.py:66-216, on B200."""
 

@@ -153,8 +153,9 @@ def test_workspace_reuse_between_shapes(strategy):
 # ----------------------------------------------------------------- CTA-pair GEMM, TMA-store epilogue
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
 @pytest.mark.parametrize("M,K,N,kp,bias,act", [
-    (4096, 4096, 4096, 2048, False, None),      # 256 whole 256 x 256 pair tiles
+    (4096, 4096, 4096, 2048, False, None),      # 256 pair tiles: 222 whole, the last 34 as 68 halves
     (2500, 4096, 4000, 2048, True, "gelu"),     # ragged last tile row and column: TMA clips the store
+    (4096, 1024, 3900, 512, True, None),        # a last-wave half tile entirely past N is skipped
     (2500, 512, 4000, 100, True, "gelu_tanh"),  # 2 k-blocks, the second one zero-filled past K'
     (4096, 1024, 4608, 1000, True, None),       # 288 tiles, 3.9 waves
 ])
