@@ -7,7 +7,8 @@ zeroed, K' = 2048 alive columns found by the mask kernel and packed once.
 Metric: useful TFLOP/s = 2*M*N*K' / time (dense-equivalent 2*M*N*K also shown).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload gemm|mlp-sharded] [--no-sweep] [--no-cpu-baseline]
+                  [--workload gemm|mlp-sharded|ghostlinear-fp32|gpt2|distilbert]
+                  [--no-sweep] [--no-cpu-baseline]
 
 * Inputs are resident in HBM: 4 independent layers (x, W', y) rotate so every
   step reads cold data (4 x 80 MB > 126 MB L2).
@@ -537,13 +538,270 @@ def run_mlp_sharded(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------- config 1: fp32 GhostLinear
+def run_fp32_linear(args, world, rank, local):
+    """Single GhostLinear fp32 through the reference's default (dynamic) path.
+
+    X [8, 128, 768] ~ N(0,1), W [3072, 768] ~ N(0, 0.02), bias ~ N(0, 0.02); 384
+    seeded-random input columns zeroed in W and in X, threshold 0, so the
+    per-forward activation mask (mask kernel -> alive list) finds exactly the
+    zeroed columns. Step = one GhostLinear.forward: mask + compaction + weight
+    packing + exact-fp32 gather-GEMM + bias.
+    """
+    from ghostweight_triton_b200 import GhostLinear
+
+    device = torch.device("cuda", torch.cuda.current_device())
+    B, T, K, N = 8, 128, 768, 3072
+    g = torch.Generator(device=device).manual_seed(1 + rank)
+    dead = torch.from_numpy(dead_columns(K, 0.5, 1, "random")).to(device)
+    layer = GhostLinear(K, N, bias=True, threshold=0.0, device=device, dtype=torch.float32)
+    with torch.no_grad():
+        layer.weight.normal_(0.0, 0.02, generator=g)
+        layer.bias.normal_(0.0, 0.02, generator=g)
+        layer.weight[:, dead] = 0
+    xs = []
+    for s in range(N_SETS):
+        x = torch.randn(B, T, K, device=device, generator=g)
+        x[..., dead] = 0
+        xs.append(x)
+    kp = K - dead.numel()
+    useful = 2.0 * B * T * N * kp
+
+    def step(i):
+        with torch.no_grad():
+            layer(xs[i % N_SETS])
+
+    for i in range(args.warmup):
+        step(i)
+    t = timed(step, args.steps, world)
+    per = t / args.steps
+    with torch.no_grad():
+        y = layer(xs[0])
+        ref = torch.nn.functional.linear(xs[0].double(), layer.weight.double(), layer.bias.double())
+        err = float((y.double() - ref).abs().max().item())
+    # The same forward with the mask frozen (alive list and packed weight reused).
+    layer.freeze_mask(xs[0])
+    t_frozen = timed(step, args.steps, world) / args.steps
+    hx = [x.cpu().pin_memory() for x in xs]
+    hy = torch.empty(B, T, N).pin_memory()
+
+    def e2e_step(i):
+        with torch.no_grad():
+            hy.copy_(layer(hx[i % N_SETS].to(device, non_blocking=True)), non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
+    te = timed(e2e_step, args.steps, world) / args.steps
+    if rank == 0:
+        cpu = cpu_linear_fp32(dead.cpu().numpy(), B * T, K, N)
+        line = {
+            "metric": "useful TFLOP/s of GhostLinear.forward fp32 (2*M*N*K')",
+            "value": round(world * useful / per / 1e12, 4), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per * 1e3, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic: X ~ N(0,1), W, b ~ N(0,0.02), 384 of 768 input columns zeroed (seeded)",
+            "config": {"workload": "single GhostLinear fp32, X [8,128,768], W [3072,768], 50% dead, dynamic mask",
+                       "M": B * T, "N": N, "K": K, "K_alive": kp, "threshold": 0.0,
+                       "l2": "inputs 3 MB: L2-resident"},
+            "frozen_mask_ms_per_step": round(t_frozen * 1e3, 4),
+            "frozen_mask_tflops": round(world * useful / t_frozen / 1e12, 4),
+            "max_abs_err_vs_fp64": err,
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(world * useful / te / 1e12, 4), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": B * T * K * 4, "d2h_bytes_per_step": B * T * N * 4,
+                    "ms_per_step": round(te * 1e3, 4)},
+            "gpu_launches": 5 * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def cpu_linear_fp32(dead: np.ndarray, M: int, K: int, N: int) -> dict:
+    """The reference's CPU path for config 1 (mask from |x|, x[:, alive] @ W[alive].T + b) on all cores."""
+    from oracle import gw_oracle as O
+
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    x[:, dead] = 0
+    w = (rng.standard_normal((N, K), dtype=np.float32) * 0.02)
+    w[:, dead] = 0
+    b = (rng.standard_normal(N, dtype=np.float32) * 0.02)
+    idx = O.alive_indices(O.dead_neuron_mask(x, 0.0))
+    times = []
+    for _ in range(8):
+        t0 = time.perf_counter()
+        idx = O.alive_indices(O.dead_neuron_mask(x, 0.0))
+        y = x[:, idx] @ w[:, idx].T + b
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": round(2.0 * M * N * len(idx) / t / 1e12, 6), "unit": "TFLOP/s",
+            "cores": os.cpu_count() or 1, "kind": "port",
+            "sample": f"the whole config ({M} rows): oracle mask + numpy fp32 gather-GEMM + bias, median of 8"}
+
+
+# ---------------------------------------------------------------------------- configs 3, 4: models
+MODELS = {
+    "gpt2": dict(batch=8, seq=512, sparsity=0.5, vocab=50257,
+                 desc="GPT-2 small random init (12 layers, d 768, 12 heads, MLP 3072), fp16 prefill "
+                      "batch 8 x seq 512; all 48 Conv1D rewritten; 50% dead input columns per layer"),
+    "distilbert": dict(batch=64, seq=128, sparsity=0.6, vocab=30522,
+                       desc="DistilBERT-base random init (6 layers, d 768, 12 heads, FFN 3072), fp16 "
+                            "encoder batch 64 x seq 128; all 36 linears rewritten; 60% dead input columns"),
+}
+
+
+def build_model(which: str, device, seed: int = 0):
+    """Random-init model in fp16 on `device` with each projection's dead input columns zeroed."""
+    import torch.nn as nn
+
+    torch.manual_seed(seed)
+    if which == "gpt2":
+        from transformers import GPT2Config, GPT2Model
+        model = GPT2Model(GPT2Config())
+    else:
+        from transformers import DistilBertConfig, DistilBertModel
+        model = DistilBertModel(DistilBertConfig())
+    from transformers.pytorch_utils import Conv1D
+
+    sp = MODELS[which]["sparsity"]
+    rng = np.random.default_rng(seed + 17)
+    with torch.no_grad():
+        for mod in model.modules():
+            if isinstance(mod, nn.Linear) and mod.in_features >= 128:
+                k = mod.in_features
+                dead = torch.from_numpy(np.sort(rng.permutation(k)[:int(k * sp)]))
+                mod.weight[:, dead] = 0
+            elif isinstance(mod, Conv1D):
+                k = mod.weight.shape[0]
+                dead = torch.from_numpy(np.sort(rng.permutation(k)[:int(k * sp)]))
+                mod.weight[dead, :] = 0
+    return model.half().to(device).eval()
+
+
+def run_model(args, world, rank, local, which: str):
+    import copy
+
+    from ghostweight_triton_b200 import replace_linears
+
+    device = torch.device("cuda", torch.cuda.current_device())
+    cfg = MODELS[which]
+    dense = build_model(which, device)
+    ghost = copy.deepcopy(dense)
+    replaced = replace_linears(ghost, threshold=0.0, include_conv1d=True, freeze_from_weight=True)
+    tokens = cfg["batch"] * cfg["seq"]
+    g = torch.Generator(device=device).manual_seed(3 + rank)
+    ids = [torch.randint(0, cfg["vocab"], (cfg["batch"], cfg["seq"]), device=device, generator=g)
+           for _ in range(2)]
+    kwargs = {}
+    if which == "distilbert":
+        kwargs["attention_mask"] = torch.ones(cfg["batch"], cfg["seq"], dtype=torch.long, device=device)
+
+    def fwd(model, i):
+        with torch.no_grad():
+            return model(input_ids=ids[i % 2], **kwargs).last_hidden_state
+
+    for i in range(args.warmup):
+        fwd(ghost, i)
+        fwd(dense, i)
+    steps = max(1, min(args.steps, 50))
+    t = timed(lambda i: fwd(ghost, i), steps, world) / steps
+    t_dense = timed(lambda i: fwd(dense, i), steps, world) / steps
+    with torch.no_grad():
+        a = fwd(ghost, 0).float()
+        b = fwd(dense, 0).float()
+        rel = float(((a - b).norm() / b.norm()).item())
+    # The same forwards captured in CUDA graphs: no per-call host overhead.
+    t_graph = graph_time(lambda: fwd(ghost, 0), steps, world)
+    t_graph_dense = graph_time(lambda: fwd(dense, 0), steps, world)
+    # Linear-layer FLOPs of one forward over the alive columns (what the kernels compute).
+    useful = 0.0
+    for mod in ghost.modules():
+        if mod.__class__.__name__ == "GhostLinear" and mod.mask_frozen:
+            useful += 2.0 * tokens * mod.out_features * mod._frozen_indices.numel()
+    hids = [x.cpu().pin_memory() for x in ids]
+    hout = torch.empty(cfg["batch"], cfg["seq"], 768, dtype=torch.float16).pin_memory()
+
+    def e2e_step(i):
+        with torch.no_grad():
+            out = ghost(input_ids=hids[i % 2].to(device, non_blocking=True), **kwargs).last_hidden_state
+        hout.copy_(out, non_blocking=True)
+
+    for i in range(2):
+        e2e_step(i)
+    te = timed(e2e_step, steps, world) / steps
+    if rank == 0:
+        cpu = cpu_model_sample(which)
+        line = {
+            "metric": f"{which} {'prefill' if which == 'gpt2' else 'encoder'} tokens/s",
+            "value": round(world * tokens / t, 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": round(t * 1e3, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+            "data": "synthetic: random-init weights, token ids uniform in [0, vocab)",
+            "config": {"workload": cfg["desc"], "tokens_per_step": tokens,
+                       "layers_replaced": len(replaced), "parallelism": f"independent batches x{world}"},
+            "dense_tokens_per_s": round(world * tokens / t_dense, 1),
+            "speedup_vs_dense": round(t_dense / t, 3),
+            "cuda_graph": {"tokens_per_s": round(world * tokens / t_graph, 1),
+                           "dense_tokens_per_s": round(world * tokens / t_graph_dense, 1),
+                           "speedup_vs_dense": round(t_graph_dense / t_graph, 3),
+                           "ms_per_step": round(t_graph * 1e3, 4)},
+            "linear_useful_tflops": round(useful / t / 1e12, 2),
+            "rel_err_vs_dense_model": rel,
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(world * tokens / te, 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": tokens * 8, "d2h_bytes_per_step": tokens * 768 * 2,
+                    "ms_per_step": round(te * 1e3, 4)},
+            "gpu_launches": None,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def graph_time(fn, steps: int, world: int) -> float:
+    """Seconds per call of fn() replayed from a CUDA graph (CUDA events, max over ranks)."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            fn()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    graph.replay()
+    t = timed(lambda i: graph.replay(), steps, world) / steps
+    del graph
+    return t
+
+
+def cpu_model_sample(which: str) -> dict:
+    """The reference's CPU path for the model (dense PyTorch fp32; its kernels have no CPU path)."""
+    cfg = MODELS[which]
+    model = build_model(which, torch.device("cpu")).float()
+    torch.set_num_threads(os.cpu_count() or 1)
+    seq = cfg["seq"]
+    ids = torch.randint(0, cfg["vocab"], (1, seq))
+    kwargs = {"attention_mask": torch.ones(1, seq, dtype=torch.long)} if which == "distilbert" else {}
+    with torch.no_grad():
+        model(input_ids=ids, **kwargs)
+        times = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            model(input_ids=ids, **kwargs)
+            times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": round(seq / t, 1), "unit": "tokens/s", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"one sequence of {seq} tokens through the dense fp32 model "
+                                      f"(PyTorch CPU), median of 3"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["gemm", "mlp-sharded"], default="gemm")
+    ap.add_argument("--workload", choices=["gemm", "mlp-sharded", "ghostlinear-fp32", "gpt2", "distilbert"],
+                    default="gemm")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -557,8 +815,12 @@ def main():
             run_reference(args, world, rank)
         elif args.workload == "gemm":
             run_ours(args, world, rank, local)
-        else:
+        elif args.workload == "mlp-sharded":
             run_mlp_sharded(args, world, rank, local)
+        elif args.workload == "ghostlinear-fp32":
+            run_fp32_linear(args, world, rank, local)
+        else:
+            run_model(args, world, rank, local, args.workload)
     finally:
         if world > 1:
             import torch.distributed as dist

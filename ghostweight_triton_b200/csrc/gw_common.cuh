@@ -406,11 +406,20 @@ template <> struct Elem<GW_DTYPE_F16> {
   using raw = uint16_t;
   static __device__ __forceinline__ float to_f(raw v) { return __half2float(__ushort_as_half(v)); }
   static __device__ __forceinline__ raw from_f(float f) { return __half_as_ushort(__float2half_rn(f)); }
+  // Two values rounded in one packed conversion: lo in bits 0-15, hi in 16-31.
+  static __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
 };
 template <> struct Elem<GW_DTYPE_BF16> {
   using raw = uint16_t;
   static __device__ __forceinline__ float to_f(raw v) { return __uint_as_float(static_cast<uint32_t>(v) << 16); }
   static __device__ __forceinline__ raw from_f(float f) { return __bfloat16_as_ushort(__float2bfloat16_rn(f)); }
+  static __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
 };
 template <> struct Elem<GW_DTYPE_F32> {
   using raw = uint32_t;

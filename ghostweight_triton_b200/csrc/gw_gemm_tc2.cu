@@ -38,17 +38,25 @@ constexpr int kHalfN = 128;            // B rows per CTA
 constexpr int kPairM = 2 * kHalfM;
 constexpr int kPairN = 2 * kHalfN;
 constexpr int kBK2 = 64;
-constexpr int kThreads2 = 192;         // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue
-constexpr int kStages2 = 6;
-constexpr int kABytes2 = kHalfM * kBK2 * 2;
-constexpr int kBBytes2 = kHalfN * kBK2 * 2;
+constexpr int kThreads2 = 320;         // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
+constexpr int kEpiWarps2 = 8;          // two per TMEM lane quadrant, 128 columns each
+// A stage holds two 64-wide k atoms (128 of K) of A and of B: the single MMA
+// thread waits once and issues 8 MMAs per stage, so its per-stage overhead
+// (barrier wait, fence, commit) is paid once per 1024 tensor cycles.
+constexpr int kAtoms2 = 2;
+constexpr int kStageK2 = kAtoms2 * kBK2;
+constexpr int kStages2 = 3;
+constexpr int kAtomBytes2 = kHalfM * kBK2 * 2;       // one 128-row x 64-col atom (16 KB)
+static_assert(kHalfM == kHalfN, "A and B atoms have the same size");
+constexpr int kABytes2 = kAtoms2 * kAtomBytes2;
+constexpr int kBBytes2 = kAtoms2 * kAtomBytes2;
 constexpr int kStageBytes2 = kABytes2 + kBBytes2;
 constexpr int kTmemCols2 = 2 * kPairN;  // two 256-column accumulators
-// Epilogue staging for TMA stores: per epilogue warp two 32-row x 64-column
-// 16-bit tiles (4 KB each, 128-byte swizzled rows).
+// Epilogue staging for TMA stores: per epilogue warp one 32-row x 64-column
+// 16-bit tile (4 KB, 128-byte swizzled rows).
 constexpr int kEpiCols = 64;
 constexpr int kEpiTileBytes = 32 * kEpiCols * 2;
-constexpr int kEpiBytes = 4 * 2 * kEpiTileBytes;
+constexpr int kEpiBytes = kEpiWarps2 * kEpiTileBytes;
 constexpr int kSmemBytes2 = 1024 + kStages2 * kStageBytes2 + kEpiBytes + 256;
 static_assert(kSmemBytes2 <= 232448, "shared memory budget per CTA");
 
@@ -61,7 +69,8 @@ struct Tc2Params {
   int y_tma;                 // y stored through tmap_y (16-byte aligned rows)
   uint16_t* y;
   int64_t ldy;
-  int num_kb;
+  int num_kb;               // 64-wide k atoms of K
+  int num_ks;               // stages of kStageK2 per tile
   int m_tiles;
   int n_tiles;
   int num_tiles;
@@ -102,7 +111,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull(b), 1);     // leader's multicast commit
-      mbar_init(tempty(b), 8);    // 4 epilogue warps x 2 CTAs (used on the leader)
+      mbar_init(tempty(b), 2 * kEpiWarps2);   // every epilogue warp of both CTAs (on the leader)
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -135,16 +144,21 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
         const int n_blk = tile / p.m_tiles;
         const int a_row = m_blk * kPairM + static_cast<int>(rank) * kHalfM;
         const int b_row = n_blk * kPairN + static_cast<int>(rank) * kHalfN;
-        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+        for (int ks = 0; ks < p.num_ks; ++ks, ++it) {
           const int s = it % kStages2;
           const uint32_t ph = (it / kStages2) & 1u;
           if (!mbar_wait_cluster(empty(s), ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
           const uint32_t a_s = sbase + s * kStageBytes2;
           const uint32_t b_s = a_s + kABytes2;
           const uint32_t leader_full = mapa_shared(full(s), 0);
-          if (rank == 0) mbar_arrive_expect_tx(full(s), 2 * kStageBytes2);
-          tma_load_2d_pair(a_s, &tmap_a, kb * kBK2, a_row, leader_full);
-          tma_load_2d_pair(b_s, &tmap_b, kb * kBK2, b_row, leader_full);
+          // The last stage of an odd number of atoms carries one atom.
+          const int atoms = min(kAtoms2, p.num_kb - ks * kAtoms2);
+          if (rank == 0) mbar_arrive_expect_tx(full(s), 2u * 2u * atoms * kAtomBytes2);
+          for (int a = 0; a < atoms; ++a) {
+            const int kx = (ks * kAtoms2 + a) * kBK2;
+            tma_load_2d_pair(a_s + a * kAtomBytes2, &tmap_a, kx, a_row, leader_full);
+            tma_load_2d_pair(b_s + a * kAtomBytes2, &tmap_b, kx, b_row, leader_full);
+          }
         }
       }
       if (!ok && rank == 0) {
@@ -165,7 +179,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
         if (!mbar_wait_cluster(tempty(b), aph ^ 1u, abort_flag, p.err)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + b * kPairN;
-        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+        for (int ks = 0; ks < p.num_ks; ++ks, ++it) {
           const int s = it % kStages2;
           const uint32_t ph = (it / kStages2) & 1u;
           if (!mbar_wait_cluster(full(s), ph, abort_flag, p.err)) { ok = false; break; }
@@ -173,10 +187,19 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
           const uint32_t a_s = sbase + s * kStageBytes2;
           const uint64_t a_desc = smem_desc_kmajor_sw128(a_s);
           const uint64_t b_desc = smem_desc_kmajor_sw128(a_s + kABytes2);
+          const bool two = ks * kAtoms2 + 1 < p.num_kb;
+          // Atom a starts kAtomBytes2 further on (>> 4 in the descriptor); each
+          // 16-wide k step advances 32 bytes inside the swizzle atom.
 #pragma unroll
           for (int k = 0; k < kBK2 / 16; ++k)
             tc_mma_f16_pair(d_tmem, a_desc + 2u * k, b_desc + 2u * k, idesc,
-                            (kb > 0 || k > 0) ? 1u : 0u);
+                            (ks > 0 || k > 0) ? 1u : 0u);
+          if (two) {
+#pragma unroll
+            for (int k = 0; k < kBK2 / 16; ++k)
+              tc_mma_f16_pair(d_tmem, a_desc + (kAtomBytes2 >> 4) + 2u * k,
+                              b_desc + (kAtomBytes2 >> 4) + 2u * k, idesc, 1u);
+          }
           tc_commit_pair_mc(empty(s), 0x3);
         }
         if (!ok) break;
@@ -188,15 +211,17 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
-    // Warp q drains TMEM lanes 32q..32q+31 (rows of this CTA's half tile) in
-    // 64-column chunks: two 32-column tcgen05 loads, bias + activation + one
-    // rounding in registers, then a TMA store from a 128-byte-swizzled staging
-    // tile (two per warp, alternating), or direct stores when y's rows are not
-    // 16-byte aligned.
+    // Eight warps: warp w drains TMEM lanes 32 (w % 4) .. +31 (rows of this
+    // CTA's half tile) and columns [128 h, 128 h + 128), h = (w - 2) / 4, in
+    // 64-column chunks. Each 32-column tcgen05 load is issued before the
+    // previous one is converted; bias + activation + one packed rounding per
+    // pair of values; then a TMA store from the warp's 128-byte-swizzled
+    // staging tile, or direct stores when y's rows are not 16-byte aligned.
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
     const uint32_t leader_tempty0 = mapa_shared(tempty(0), 0);
     const uint32_t leader_tempty1 = mapa_shared(tempty(1), 0);
-    uint8_t* stage_w = epi_stage + q * 2 * kEpiTileBytes;
+    uint8_t* sb = epi_stage + (warp - 2) * kEpiTileBytes;
     uint32_t lt = 0;
     for (int tile = pair; tile < p.num_tiles; tile += num_pairs, ++lt) {
       const int m_blk = tile % p.m_tiles;
@@ -209,68 +234,67 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
       const int64_t row = warp_row0 + lane;
       const bool row_ok = row < p.M;
       uint16_t* yrow = p.y + (row_ok ? row * p.ldy : 0);
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * kPairN;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * kPairN + half * (kPairN / 2);
+      const int64_t n_warp = static_cast<int64_t>(n_blk) * kPairN + half * (kPairN / 2);
+      constexpr int kSteps = (kPairN / 2) / 32;        // 32-column loads per warp and tile
+      uint32_t acc[32];
+      tc_ld_32x32b_x32(t_row, acc);
 #pragma unroll 1
-      for (int c = 0; c < kPairN / kEpiCols; ++c) {
-        const int64_t n_chunk = static_cast<int64_t>(n_blk) * kPairN + c * kEpiCols;
-        uint8_t* sb = stage_w + (c & 1) * kEpiTileBytes;
-        if (p.y_tma) {
-          // The staging tile written two chunks ago must have been read by its TMA store.
-          if (lane == 0) bulk_wait_group_read<1>();
+      for (int st = 0; st < kSteps; ++st) {
+        tc_wait_ld();
+        float f[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(acc[j]);
+        if (st + 1 < kSteps) tc_ld_32x32b_x32(t_row + (st + 1) * 32, acc);
+        const int c = st >> 1;                          // 64-column chunk
+        const int h = st & 1;                           // its 32-column half
+        const int64_t n_chunk = n_warp + c * kEpiCols;
+        const int64_t n_base = n_chunk + h * 32;
+        if (p.y_tma && h == 0) {
+          // The staging tile's previous TMA store must have read it.
+          if (lane == 0) bulk_wait_group_read<0>();
           __syncwarp();
         }
-#pragma unroll 1
-        for (int h = 0; h < 2; ++h) {
-          uint32_t acc[32];
-          tc_ld_32x32b_x32(t_row + c * kEpiCols + h * 32, acc);
-          tc_wait_ld();
-          float f[32];
+        if (p.bias) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(acc[j]);
-          const int64_t n_base = n_chunk + h * 32;
-          if (p.bias) {
+          for (int j = 0; j < 32; ++j)
+            if (n_base + j < p.N) f[j] += Elem<DT>::to_f(__ldg(p.bias + n_base + j));
+        }
+        if (p.epi != GW_EPI_NONE) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (n_base + j < p.N) f[j] += Elem<DT>::to_f(__ldg(p.bias + n_base + j));
-          }
-          if (p.epi != GW_EPI_NONE) {
+          for (int j = 0; j < 32; ++j) f[j] = apply_epilogue(f[j], p.epi);
+        }
+        uint32_t packed[16];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) f[j] = apply_epilogue(f[j], p.epi);
-          }
-          uint32_t packed[16];
+        for (int j = 0; j < 16; ++j) packed[j] = Elem<DT>::pack2(f[2 * j], f[2 * j + 1]);
+        if (p.y_tma) {
+          // Row `lane` of the staging tile, 128-byte swizzle: 16-byte unit
+          // v of the row lives at unit (v ^ (row & 7)).
+          uint4* srow = reinterpret_cast<uint4*>(sb + lane * (kEpiCols * 2));
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            packed[j] = static_cast<uint32_t>(Elem<DT>::from_f(f[2 * j])) |
-                        (static_cast<uint32_t>(Elem<DT>::from_f(f[2 * j + 1])) << 16);
-          if (p.y_tma) {
-            // Row `lane` of the staging tile, 128-byte swizzle: 16-byte unit
-            // v of the row lives at unit (v ^ (row & 7)).
-            uint4* srow = reinterpret_cast<uint4*>(sb + lane * (kEpiCols * 2));
-#pragma unroll
-            for (int v = 0; v < 4; ++v)
-              srow[(h * 4 + v) ^ (lane & 7)] =
-                  make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
-          } else if (row_ok) {
-            if (p.y_vec_ok && n_base + 32 <= p.N) {
-              uint4* dst = reinterpret_cast<uint4*>(yrow + n_base);
-#pragma unroll
-              for (int v = 0; v < 4; ++v)
-                dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (n_base + j < p.N) yrow[n_base + j] = Elem<DT>::from_f(f[j]);
+          for (int v = 0; v < 4; ++v)
+            srow[(h * 4 + v) ^ (lane & 7)] =
+                make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+          if (h == 1) {
+            fence_proxy_async_smem();    // staging writes -> visible to the TMA unit
+            __syncwarp();
+            if (lane == 0) {
+              if (warp_row0 < p.M && n_chunk < p.N)
+                tma_store_2d(&tmap_y, smem_u32(sb), static_cast<int32_t>(n_chunk),
+                             static_cast<int32_t>(warp_row0));
+              bulk_commit_group();
             }
           }
-        }
-        if (p.y_tma) {
-          fence_proxy_async_smem();      // staging writes -> visible to the TMA unit
-          __syncwarp();
-          if (lane == 0) {
-            if (warp_row0 < p.M && n_chunk < p.N)
-              tma_store_2d(&tmap_y, smem_u32(sb), static_cast<int32_t>(n_chunk),
-                           static_cast<int32_t>(warp_row0));
-            bulk_commit_group();
+        } else if (row_ok) {
+          if (p.y_vec_ok && n_base + 32 <= p.N) {
+            uint4* dst = reinterpret_cast<uint4*>(yrow + n_base);
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n_base + j < p.N) yrow[n_base + j] = Elem<DT>::from_f(f[j]);
           }
         }
       }
@@ -328,6 +352,7 @@ cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int6
   p.ldy = ldy;
   p.y_vec_ok = ((reinterpret_cast<uintptr_t>(y) & 15u) == 0 && (ldy % 8) == 0) ? 1 : 0;
   p.num_kb = static_cast<int>((K + kBK2 - 1) / kBK2);
+  p.num_ks = (p.num_kb + kAtoms2 - 1) / kAtoms2;
   p.m_tiles = static_cast<int>(m_tiles);
   p.n_tiles = static_cast<int>(n_tiles);
   p.num_tiles = static_cast<int>(num_tiles);
