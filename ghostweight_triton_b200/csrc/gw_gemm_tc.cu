@@ -56,7 +56,11 @@ constexpr int kWarpTma = 0;
 constexpr int kWarpMma = 1;
 constexpr int kWarpGather0 = 2;
 constexpr int kGatherWarps = 8;      // two groups of four
-constexpr int kWarpEpi0 = 10;        // four epilogue warps
+constexpr int kWarpEpi0 = 10;        // four epilogue warps (gather modes)
+// With a dense A operand the gather warps are free: warps 6..13 drain TMEM,
+// two per lane quadrant, each with half of the tile's columns.
+constexpr int kWarpEpi0Dense = 6;
+template <int AMODE> constexpr int epi_warps() { return AMODE == 0 ? 8 : 4; }
 
 // How the A operand (x[:, alive]) reaches shared memory.
 constexpr int kATma = 0;        // dense [M, K'] matrix by TMA (already compacted)
@@ -136,7 +140,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull(b), 1);
-      mbar_init(tempty(b), 4);
+      mbar_init(tempty(b), epi_warps<AMODE>());
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -237,7 +241,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
       mbar_wait(drain_bar, 0u, nullptr, p.err, 100000000ull);
     }
     __syncwarp();
-  } else if (warp < kWarpEpi0) {
+  } else if (warp < (AMODE == kATma ? kWarpEpi0Dense : kWarpEpi0)) {
     // ------------------------------------------------------------ gather producers
     if (AMODE == kAOverlap) {
       // Cooperative gather of x[:, alive] -> x' in k-block-major unit order.
@@ -357,7 +361,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // Warp w drains TMEM lanes 32 (w % 4) .. +31 (its rows of the tile); with
+    // eight epilogue warps each takes half of the BN columns. The next
+    // 32-column tcgen05 load is issued before the current one is converted;
+    // bias, activation, one packed rounding per pair, 16-byte stores.
+    constexpr int kEpiWarps = epi_warps<AMODE>();
+    constexpr int kCols = BN / (kEpiWarps / 4);         // columns per warp
+    constexpr int kSteps = kCols / 32;
     const int q = warp & 3;                       // TMEM lane quarter this warp may access
+    const int part = (warp - (AMODE == kATma ? kWarpEpi0Dense : kWarpEpi0)) >> 2;
     const int row_in_tile = q * 32 + lane;
     uint32_t lt = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++lt) {
@@ -370,15 +382,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
       const int64_t row = static_cast<int64_t>(m_blk) * kBM + row_in_tile;
       const bool row_ok = row < p.M;
       uint16_t* yrow = p.y + (row_ok ? row * p.ldy : 0);
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * BN + part * kCols;
+      const int64_t n_warp = static_cast<int64_t>(n_blk) * BN + part * kCols;
+      uint32_t acc[32];
+      tc_ld_32x32b_x32(t_row, acc);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t acc[32];
-        tc_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * BN + c * 32, acc);
+      for (int c = 0; c < kSteps; ++c) {
         tc_wait_ld();
-        const int64_t n_base = static_cast<int64_t>(n_blk) * BN + c * 32;
         float f[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(acc[j]);
+        if (c + 1 < kSteps) tc_ld_32x32b_x32(t_row + (c + 1) * 32, acc);
+        const int64_t n_base = n_warp + c * 32;
         if (p.bias) {
 #pragma unroll
           for (int j = 0; j < 32; ++j)
@@ -392,9 +407,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
           if (p.y_vec_ok && n_base + 32 <= p.N) {
             uint32_t packed[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-              packed[j] = static_cast<uint32_t>(Elem<DT>::from_f(f[2 * j])) |
-                          (static_cast<uint32_t>(Elem<DT>::from_f(f[2 * j + 1])) << 16);
+            for (int j = 0; j < 16; ++j) packed[j] = Elem<DT>::pack2(f[2 * j], f[2 * j + 1]);
             uint4* dst = reinterpret_cast<uint4*>(yrow + n_base);
 #pragma unroll
             for (int v = 0; v < 4; ++v)
