@@ -345,7 +345,7 @@ def sweep(device, peaks) -> list[dict]:
 
 def traffic_from_profiles() -> float | None:
     """DRAM bytes (read + write) per launch of the headline GEMM from the committed ncu summary."""
-    p = REPO / "profiles" / "gemm_tc_tma_4096x4096x2048_fp16.md"
+    p = REPO / "profiles" / "gemm_tc2_pair_4096x4096x2048_fp16.md"
     if p.exists():
         for line in p.read_text().splitlines():
             if line.startswith("traffic_bytes_per_launch:"):
@@ -472,9 +472,11 @@ def run_ours(args, world, rank, local):
             "dense_equiv_tflops": round(world * 2.0 * M * N * K / per_step / 1e12, 3),
             "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
                          "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
-                         "peak_source": f"{peak_src} bf16_tflops (fp16 taken equal)",
+                         "peak_source": f"{peak_src} bf16_tflops burst (fp16 taken equal)",
+                         "frac_of_sustained": (round(achieved / float(peaks["bf16_tflops_sustained"]), 4)
+                                               if "bf16_tflops_sustained" in peaks else None),
                          "traffic": traffic,
-                         "kernel": "gemm_tc_kernel<BN, f16, TMA A> (csrc/gw_gemm_tc.cu), timed alone"},
+                         "kernel": "gemm_tc2_kernel<f16> (csrc/gw_gemm_tc2.cu: CTA pair, 256x256 tiles), timed alone"},
             "cpu_baseline": cpu,
             "e2e": e2e,
             "clocks": clocks,

@@ -488,12 +488,17 @@ cudaError_t launch_gemm_tc(int a_mode, const void* x, int dtype, int64_t M, int6
                            void* y, int64_t ldy, unsigned int* err, int sm_count,
                            cudaStream_t stream, void* scratch_xg, int64_t ldg,
                            unsigned int* kb_ready) {
-  // Tile width 256 (measured best on B200 even where 128 or 192 balance the
-  // waves better: wider tiles reuse A more per byte moved), 128 for narrow N.
+  // Tile width 256 (measured best on B200 where there are several waves:
+  // wider tiles reuse A more per byte moved), 128 for narrow N. When 256-wide
+  // tiles leave SMs idle in a single wave and 192-wide ones still fit in one
+  // (N = 768: 3 -> 4 column tiles), 192 (measured faster for such layers).
   // GW_GEMM_BN=128|192|256 overrides the choice (tuning and tests).
   const int64_t m_tiles = (M + kBM - 1) / kBM;
   const int64_t sms = sm_count > 0 ? sm_count : 148;
   int BN = N <= 128 ? 128 : 256;
+  if (BN == 256 && m_tiles * ((N + 255) / 256) < sms && m_tiles * ((N + 191) / 192) <= sms &&
+      (N + 191) / 192 > (N + 255) / 256)
+    BN = 192;
   {
     static const int forced = [] {
       const char* v = std::getenv("GW_GEMM_BN");
