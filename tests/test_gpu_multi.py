@@ -1,0 +1,95 @@
+"""GPU, 2 ranks over NCCL: the column-parallel layer equals the dense layer on every rank.
+
+Runs only where at least two GPUs are visible (skipped otherwise). Each rank is
+a spawned process with a short process-group timeout; the parent joins them
+with a deadline and terminates the ones it started if a rank stalls, so a
+failure ends the test instead of hanging it. NVLS is off (plain peer
+transfers), and no kernel of this package waits on another rank.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank: int, world: int, port: int, q) -> None:
+    import datetime
+
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    try:
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        from ghostweight_triton_b200.sharded import ColumnParallelGhostLinear
+
+        device = torch.device("cuda", rank)
+        results = {}
+        for dtype, (M, N, K) in ((torch.bfloat16, (2048, 4096, 2048)), (torch.float16, (300, 1000, 768))):
+            g = torch.Generator(device=device).manual_seed(7)      # identical full tensors on all ranks
+            w = (torch.randn(N, K, device=device, generator=g) / K ** 0.5).to(dtype)
+            b = torch.randn(N, device=device, generator=g).to(dtype)
+            x = torch.randn(M, K, device=device, generator=g).to(dtype)
+            perm = torch.randperm(K, device=device, generator=g)
+            dead = perm[: K // 2]
+            w[:, dead] = 0
+            # Column perm[-1] is zero in rank 0's rows only: the union mask keeps it alive
+            # on both ranks, so every rank sees K - K/2 alive columns.
+            w[: N // 2, perm[-1]] = 0
+            layer = ColumnParallelGhostLinear.from_full_weight(w, b, device=device)
+            y = layer(x)
+            ref = F.linear(x.float(), w.float(), b.float())
+            err = (y.float() - ref).abs().max().item()
+            results[str(dtype)] = (err, layer.k_alive, tuple(y.shape))
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, results, None))
+    except Exception as e:  # reported to the parent, which fails the test
+        q.put((rank, None, repr(e)))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs two GPUs")
+def test_column_parallel_two_ranks_nccl():
+    import torch.multiprocessing as mp
+
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    try:
+        for _ in range(world):
+            rank, res, err = q.get(timeout=240)
+            assert err is None, f"rank {rank}: {err}"
+            got[rank] = res
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.terminate()
+                p.join(timeout=10)
+    for rank, res in got.items():
+        for dt, (err, k_alive, shape) in res.items():
+            tol = 0.1 if "bfloat16" in dt else 0.02
+            assert err < tol, f"rank {rank} {dt}: max err {err}"
+        assert res["torch.bfloat16"][1] == 1024 and res["torch.bfloat16"][2] == (2048, 4096)
+        assert res["torch.float16"][1] == 384 and res["torch.float16"][2] == (300, 1000)
