@@ -329,15 +329,24 @@ def sweep(device, peaks) -> list[dict]:
             for sp in (0.0, 0.25, 0.5, 0.75, 0.9):
                 L = build_layer(M, N, K, sp, pattern, torch.float16, 100 + M, device)
                 kp = L["idx"].numel()
-                t = event_time(lambda i: ghost_linear(L["x"], L["wp"], L["idx"], out=L["y"]), iters=20)
+                yd = torch.empty(M, N, dtype=torch.float16, device=device)
+                ours = lambda: ghost_linear(L["x"], L["wp"], L["idx"], out=L["y"])
+                dense = lambda: torch.mm(L["x"], L["w"].t(), out=yd)
+                t = event_time(lambda i: ours(), iters=20)
                 td = event_time(lambda i: F.linear(L["x"], L["w"]), iters=20)
+                # The same calls replayed from CUDA graphs: kernel time without
+                # the per-call host overhead (which dominates at M <= 128).
+                tg = graph_time(ours, 20, 1)
+                tdg = graph_time(dense, 20, 1)
                 useful = 2.0 * M * N * kp
                 rows.append({"M": M, "pattern": pattern, "sparsity": sp, "K_alive": kp,
                              "us": round(t * 1e6, 2), "useful_tflops": round(useful / t / 1e12, 1),
                              "dense_equiv_tflops": round(2.0 * M * N * K / t / 1e12, 1),
                              "frac_tensor_peak": round(useful / t / 1e12 / peaks["bf16_tflops"], 3),
                              "cublas_dense_us": round(td * 1e6, 2),
-                             "speedup_vs_dense": round(td / t, 3), "ideal": round(K / kp, 3)})
+                             "speedup_vs_dense": round(td / t, 3), "ideal": round(K / kp, 3),
+                             "graph_us": round(tg * 1e6, 2), "graph_cublas_dense_us": round(tdg * 1e6, 2),
+                             "graph_speedup_vs_dense": round(tdg / tg, 3)})
                 del L
     torch.cuda.empty_cache()
     return rows

@@ -133,7 +133,16 @@ def _rowmajor(*ts: torch.Tensor) -> None:
             f"expected a row-major matrix, got shape {tuple(t.shape)} strides {t.stride()}")
 
 
+try:  # the raw cudaStream_t of torch's current stream, without building a Stream object
+    _raw_stream = torch._C._cuda_getCurrentRawStream
+except AttributeError:  # pragma: no cover - older torch
+    _raw_stream = None
+
+
 def _stream(device: torch.device) -> int:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if _raw_stream is not None:
+        return _raw_stream(idx)
     return torch.cuda.current_stream(device).cuda_stream
 
 
@@ -237,6 +246,28 @@ def gather_gemm_workspace_bytes(M: int, n_alive: int, dtype: torch.dtype) -> int
     return int(load().gw_gather_gemm_workspace_bytes(int(M), int(n_alive), dtype_code(dtype)))
 
 
+# GEMM workspaces reused across calls: one per (device, stream), grown as
+# needed. Calls on one stream are ordered, so they may share it; under CUDA
+# graph capture a fresh buffer is allocated instead (from the graph's pool), so
+# a captured graph never refers to a buffer that a later call replaces.
+_gemm_ws: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def gemm_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    if torch.cuda.is_current_stream_capturing():
+        return torch.empty(nbytes, dtype=torch.uint8, device=device)
+    dev = device.index if device.index is not None else torch.cuda.current_device()
+    key = (dev, _stream(device))
+    ws = _gemm_ws.get(key)
+    if ws is None or ws.numel() < nbytes:
+        with _ws_lock:
+            ws = _gemm_ws.get(key)
+            if ws is None or ws.numel() < nbytes:
+                ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+                _gemm_ws[key] = ws
+    return ws
+
+
 def gather_gemm(x: torch.Tensor, w_packed: torch.Tensor, idx: torch.Tensor, y: torch.Tensor,
                 bias: torch.Tensor | None = None, activation: str | None = None,
                 strategy: str = "auto", workspace: torch.Tensor | None = None) -> None:
@@ -251,13 +282,21 @@ def gather_gemm(x: torch.Tensor, w_packed: torch.Tensor, idx: torch.Tensor, y: t
     N = w_packed.shape[0]
     n = idx.numel()
     ws_ptr, ws_bytes = (None, 0) if workspace is None else (workspace.data_ptr(), workspace.numel() * workspace.element_size())
-    with _on_device(x.device):
+    dev = x.get_device()
+    cur = torch.cuda.current_device()
+    if dev != cur:
+        torch.cuda.set_device(dev)
+    try:
         st = load().gw_gather_gemm(
-            _ptr(x), dtype_code(x.dtype), M, K, max(x.stride(0), K), _ptr(w_packed), N,
-            max(w_packed.stride(0), n), _ptr(idx), n, _ptr(bias), epilogue_code(activation),
-            _ptr(y), max(y.stride(0), N), GEMM_STRATEGIES[strategy], ws_ptr, ws_bytes,
-            _stream(x.device))
-    _check(st, "gw_gather_gemm")
+            x.data_ptr(), dtype_code(x.dtype), M, K, max(x.stride(0), K), w_packed.data_ptr(), N,
+            max(w_packed.stride(0), n), idx.data_ptr(), n, _ptr(bias), epilogue_code(activation),
+            y.data_ptr(), max(y.stride(0), N), GEMM_STRATEGIES[strategy], ws_ptr, ws_bytes,
+            _raw_stream(dev) if _raw_stream is not None else torch.cuda.current_stream().cuda_stream)
+    finally:
+        if dev != cur:
+            torch.cuda.set_device(cur)
+    if st:
+        _check(st, "gw_gather_gemm")
 
 
 def packed_gemm(a: torch.Tensor, w_packed: torch.Tensor, y: torch.Tensor,

@@ -61,6 +61,25 @@ void* tensor_map_encoder() {
 
 bool make_tmap_kmajor(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld,
                       int box_cols, int box_rows) {
+  // A few recently encoded maps per host thread: the packed weight and the
+  // reused workspace recur from call to call, and encoding is a driver call.
+  struct Entry {
+    const void* base;
+    int64_t rows, cols, ld;
+    int box_cols, box_rows;
+    CUtensorMap map;
+  };
+  constexpr int kCache = 8;
+  thread_local Entry cache[kCache];
+  thread_local int filled = 0, next = 0;
+  for (int i = 0; i < filled; ++i) {
+    const Entry& e = cache[i];
+    if (e.base == base && e.rows == rows && e.cols == cols && e.ld == ld &&
+        e.box_cols == box_cols && e.box_rows == box_rows) {
+      *map = e.map;
+      return true;
+    }
+  }
   using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                      const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                      const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -71,10 +90,15 @@ bool make_tmap_kmajor(CUtensorMap* map, const void* base, int64_t rows, int64_t 
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2u};
   cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
-  return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides,
-                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
-         CUDA_SUCCESS;
+  if (encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides,
+             box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  Entry& e = cache[next];
+  e = Entry{base, rows, cols, ld, box_cols, box_rows, *map};
+  next = (next + 1) % kCache;
+  if (filled < kCache) ++filled;
+  return true;
 }
 
 }  // namespace gw

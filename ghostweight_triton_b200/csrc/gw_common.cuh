@@ -8,6 +8,8 @@
 #pragma once
 
 #include <cstdint>
+#include <mutex>
+#include <unordered_map>
 #include <utility>
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
@@ -377,6 +379,28 @@ __device__ __forceinline__ void tc_commit_pair_mc(uint32_t bar, uint16_t mask) {
       "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
       " [%0], %1;"
       :: "r"(bar), "h"(mask) : "memory");
+}
+
+// Host: raise `kern`'s dynamic shared-memory limit to `bytes` once per device
+// (the attribute sticks to the function; re-setting it on every launch costs a
+// driver call).
+inline cudaError_t ensure_smem_attr(const void* kern, int bytes) {
+  static std::mutex mu;
+  static std::unordered_map<const void*, uint64_t> done;   // bit d: set on device d
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = dev < 64 ? (uint64_t{1} << dev) : 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = done.find(kern);
+    if (bit && it != done.end() && (it->second & bit)) return cudaSuccess;
+  }
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  done[kern] |= bit;
+  return cudaSuccess;
 }
 
 // Host: launch `kern` as a programmatic dependent of the previous work of the

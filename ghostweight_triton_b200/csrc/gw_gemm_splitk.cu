@@ -300,8 +300,7 @@ cudaError_t launch_sk(const CUtensorMap& tb, const CUtensorMap& ta, const SkPara
                       int64_t tiles, cudaStream_t stream) {
   using C = SkCfg<BN>;
   auto kern = gemm_splitk_kernel<BN, DT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       C::kSmemBytes);
+  cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), C::kSmemBytes);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p.split), static_cast<unsigned>(tiles));
@@ -321,56 +320,56 @@ cudaError_t launch_sk(const CUtensorMap& tb, const CUtensorMap& ta, const SkPara
 }
 
 // Clusters of S CTAs of the BN-wide kernel that fit on the current device at
-// once (occupancy query, cached per device). Clusters of 8 CTAs that each
-// need most of an SM's shared memory do not tile every GPC: on a 148-SM B200
-// only 15 fit, not 18.
-int max_active_clusters(int bn, int s) {
+// once, for BN in {256, 128, 64, 32} x S in {8, 4, 2} (occupancy queries, run
+// once per device). Clusters of 8 CTAs that each need most of an SM's shared
+// memory do not tile every GPC: on a 148-SM B200 only 15 fit, not 18.
+struct ClusterTable {
+  int n[4][3];
+};
+
+template <int BN>
+int query_active_clusters(int s) {
+  auto kern = gemm_splitk_kernel<BN, GW_DTYPE_F16>;
+  constexpr int smem = SkCfg<BN>::kSmemBytes;
+  if (ensure_smem_attr(reinterpret_cast<const void*>(kern), smem) != cudaSuccess) return 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(s), 1);
+  cfg.blockDim = dim3(kSkThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(s);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+  return n > 0 ? n : 0;
+}
+
+const ClusterTable* cluster_table() {
   static std::mutex mu;
-  static int cache[64][4][4];
-  static bool init[64] = {};
+  static ClusterTable tables[64];
+  static bool ready[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
     (void)cudaGetLastError();
-    return 0;
+    return nullptr;
   }
-  const int bi = bn == 256 ? 0 : bn == 128 ? 1 : bn == 64 ? 2 : 3;
-  const int si = s == 8 ? 0 : s == 4 ? 1 : s == 2 ? 2 : 3;
   std::lock_guard<std::mutex> lock(mu);
-  if (!init[dev]) {
-    for (auto& row : cache[dev])
-      for (int& v : row) v = -1;
-    init[dev] = true;
+  if (!ready[dev]) {
+    const int ss[3] = {8, 4, 2};
+    for (int si = 0; si < 3; ++si) {
+      tables[dev].n[0][si] = query_active_clusters<256>(ss[si]);
+      tables[dev].n[1][si] = query_active_clusters<128>(ss[si]);
+      tables[dev].n[2][si] = query_active_clusters<64>(ss[si]);
+      tables[dev].n[3][si] = query_active_clusters<32>(ss[si]);
+    }
+    (void)cudaGetLastError();
+    ready[dev] = true;
   }
-  int& slot = cache[dev][bi][si];
-  if (slot >= 0) return slot;
-  auto query = [&](auto kern, int smem) {
-    int n = 0;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-      return 0;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(s), 1);
-    cfg.blockDim = dim3(kSkThreads);
-    cfg.dynamicSmemBytes = smem;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = static_cast<unsigned>(s);
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
-    return n;
-  };
-  int n = 0;
-  switch (bn) {
-    case 256: n = query(gemm_splitk_kernel<256, GW_DTYPE_F16>, SkCfg<256>::kSmemBytes); break;
-    case 128: n = query(gemm_splitk_kernel<128, GW_DTYPE_F16>, SkCfg<128>::kSmemBytes); break;
-    case 64: n = query(gemm_splitk_kernel<64, GW_DTYPE_F16>, SkCfg<64>::kSmemBytes); break;
-    default: n = query(gemm_splitk_kernel<32, GW_DTYPE_F16>, SkCfg<32>::kSmemBytes); break;
-  }
-  (void)cudaGetLastError();
-  slot = n > 0 ? n : 0;
-  return slot;
+  return &tables[dev];
 }
 
 }  // namespace
@@ -385,12 +384,18 @@ SplitKPlan plan_splitk(int64_t M, int64_t N, int64_t K, int sm_count) {
   if (m_tiles * ((N + 255) / 256) * 2 > sms) return best;
   // Most CTAs in a single wave of clusters; ties keep the wider tile (less
   // re-reading of x') and then the larger cluster.
+  const ClusterTable* table = cluster_table();
+  if (!table) return best;
   int64_t best_ctas = 0;
-  for (int bn : {256, 128, 64, 32}) {
+  const int bns[4] = {256, 128, 64, 32};
+  const int ss[3] = {8, 4, 2};
+  for (int bi = 0; bi < 4; ++bi) {
+    const int bn = bns[bi];
     const int64_t tiles = m_tiles * ((N + bn - 1) / bn);
-    for (int s : {8, 4, 2}) {
+    for (int si = 0; si < 3; ++si) {
+      const int s = ss[si];
       if (s > num_kb || tiles * s > sms) continue;
-      if (tiles > max_active_clusters(bn, s)) continue;
+      if (tiles > table->n[bi][si]) continue;
       const int64_t ctas = tiles * s;
       if (ctas > best_ctas) {
         best_ctas = ctas;

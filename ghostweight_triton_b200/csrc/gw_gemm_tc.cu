@@ -441,8 +441,7 @@ cudaError_t launch_tc(const CUtensorMap& tb, const CUtensorMap& ta, const TcPara
   using C = TcCfg<BN>;
   auto kern = gemm_tc_kernel<BN, DT, AMODE>;
   // Opt in to the large dynamic shared-memory carve-out (idempotent, cheap).
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       C::kSmemBytes);
+  cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), C::kSmemBytes);
   if (e != cudaSuccess) return e;
   const int grid = std::min(p.num_tiles, sm_count > 0 ? sm_count : 148);
   if (AMODE == kASmemGather) {

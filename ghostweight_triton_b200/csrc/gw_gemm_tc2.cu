@@ -366,7 +366,7 @@ cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int6
   if (!p.y_tma) ty = ta;     // not read by the kernel
 
   auto kern = dtype == GW_DTYPE_BF16 ? gemm_tc2_kernel<GW_DTYPE_BF16> : gemm_tc2_kernel<GW_DTYPE_F16>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes2);
+  cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), kSmemBytes2);
   if (e != cudaSuccess) return e;
   const int64_t pairs = std::max<int64_t>(1, (sm_count > 0 ? sm_count : 148) / 2);
   const int grid = static_cast<int>(2 * std::min<int64_t>(num_tiles, pairs));

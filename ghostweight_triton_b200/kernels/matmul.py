@@ -76,7 +76,7 @@ def _gemm(x, w_packed, idx, y, bias, activation, strategy):
     if strategy != "fused" and x.dtype != torch.float32:
         nbytes = _native.gather_gemm_workspace_bytes(x.shape[0], idx.numel(), x.dtype)
         if nbytes:
-            ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+            ws = _native.gemm_workspace(x.device, nbytes)
     _native.gather_gemm(x, w_packed, idx, y, bias=bias, activation=activation,
                         strategy=strategy, workspace=ws)
 
