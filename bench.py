@@ -522,13 +522,23 @@ def run_mlp_sharded(args, world, rank, local):
     def step_gemm(i):
         layer.local_forward(x)
 
-    def step_full(i):
+    def step_nccl(i):
+        layer.gather_output = True
+        layer(x)
+
+    def step_peers(i):
+        layer.gather_output = "peers"
         layer(x)
 
     for i in range(args.warmup):
-        step_full(i)
+        step_nccl(i)
+        if world > 1:
+            step_peers(i)
     t_gemm = timed(step_gemm, args.steps, world)
-    t_full = timed(step_full, args.steps, world)
+    t_nccl = timed(step_nccl, args.steps, world)
+    t_peers = timed(step_peers, args.steps, world) if world > 1 else t_nccl
+    layer.close()
+    t_full = min(t_nccl, t_peers)
     if rank == 0:
         per = t_full / args.steps
         line = {
@@ -537,7 +547,11 @@ def run_mlp_sharded(args, world, rank, local):
             "ms_per_step": round(per * 1e3, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic, seeded",
             "config": {"workload": "sharded MLP projection x[8192,8192] W[28672,8192] bf16, 70% dead 128-col blocks",
-                       "K_alive": kp, "parallelism": f"column-parallel N over {world} GPUs + NCCL all-gather"},
+                       "K_alive": kp, "parallelism": f"column-parallel N over {world} GPUs, full output on every rank"},
+            "gather": ("GEMM epilogue stores every tile into all ranks' outputs over NVLink (CUDA IPC)"
+                       if world > 1 and t_peers <= t_nccl else "NCCL all-gather + re-layout"),
+            "peer_fused_ms": round(t_peers / args.steps * 1e3, 4) if world > 1 else None,
+            "nccl_allgather_ms": round(t_nccl / args.steps * 1e3, 4),
             "gemm_only_tflops": round(useful / (t_gemm / args.steps) / 1e12, 3),
             "gemm_only_ms": round(t_gemm / args.steps * 1e3, 4),
             "roofline": {"bound": "tensor", "achieved": round(useful / world / (t_gemm / args.steps) / 1e12, 2),

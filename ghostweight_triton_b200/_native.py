@@ -52,6 +52,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gw_gather_gemm_workspace_bytes": (_sz, [_i64, _i64, _i]),
     "gw_gather_gemm": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _i,
                             _vp, _i64, _i, _vp, _sz, _vp]),
+    "gw_gather_gemm_peers": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _i,
+                                  _vp, _i64, _vp, _i, _vp, _sz, _vp]),
     "gw_packed_gemm": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i, _vp, _i64, _vp]),
     "gw_validate_indices": (_i, [_vp, _i64, _i64, _vp, _vp]),
 }
@@ -297,6 +299,34 @@ def gather_gemm(x: torch.Tensor, w_packed: torch.Tensor, idx: torch.Tensor, y: t
             torch.cuda.set_device(cur)
     if st:
         _check(st, "gw_gather_gemm")
+
+
+def gather_gemm_peers(x: torch.Tensor, w_packed: torch.Tensor, idx: torch.Tensor, y: torch.Tensor,
+                      peer_addresses: list[int], bias: torch.Tensor | None = None,
+                      activation: str | None = None, workspace: torch.Tensor | None = None) -> None:
+    """gather_gemm (pregather) whose output block y also goes to each peer address.
+
+    y is this rank's block of a full output (a column slice view, row stride
+    ldy); peer_addresses are device addresses of the same block in the other
+    ranks' full outputs (same row stride), valid in this process.
+    """
+    _rowmajor(x, w_packed)
+    assert y.ndim == 2 and y.stride(1) == 1
+    assert idx.dtype == torch.int64 and idx.is_contiguous()
+    M, K = x.shape
+    N = y.shape[1]
+    n = idx.numel()
+    if workspace is None:
+        nbytes = gather_gemm_workspace_bytes(M, n, x.dtype)
+        workspace = gemm_workspace(x.device, nbytes) if nbytes else None
+    ws_ptr, ws_bytes = (None, 0) if workspace is None else (workspace.data_ptr(), workspace.numel() * workspace.element_size())
+    peers = (ctypes.c_void_p * max(1, len(peer_addresses)))(*[ctypes.c_void_p(a) for a in peer_addresses])
+    with _on_device(x.device):
+        st = load().gw_gather_gemm_peers(
+            _ptr(x), dtype_code(x.dtype), M, K, max(x.stride(0), K), _ptr(w_packed), N,
+            max(w_packed.stride(0), n), _ptr(idx), n, _ptr(bias), epilogue_code(activation),
+            _ptr(y), y.stride(0), peers, len(peer_addresses), ws_ptr, ws_bytes, _stream(x.device))
+    _check(st, "gw_gather_gemm_peers")
 
 
 def packed_gemm(a: torch.Tensor, w_packed: torch.Tensor, y: torch.Tensor,

@@ -275,18 +275,25 @@ namespace {
 // the CTA-pair kernel when there are enough 256 x 256 tiles for every SM
 // pair, cluster split-K when the output has too few tiles to occupy half of
 // the SMs (decode-sized M), else the single-CTA persistent kernel.
+// With peers, the output is also written into each peer buffer: by the pair
+// kernel's epilogue, tile by tile, or by a copy kernel after the other kernels.
 cudaError_t launch_dense_gemm(const void* a, int dtype, int64_t M, int64_t K, int64_t lda,
                               const void* w, int64_t N, int64_t ldw, const void* bias, int epilogue,
-                              void* y, int64_t ldy, const gw::DeviceInfo* d, cudaStream_t s) {
+                              void* y, int64_t ldy, const gw::DeviceInfo* d, cudaStream_t s,
+                              void* const* peers = nullptr, int n_peers = 0) {
   if (gw::use_pair_gemm(M, N, d->sm_count))
     return gw::launch_gemm_tc2(a, dtype, M, K, lda, w, N, ldw, bias, epilogue, y, ldy,
-                               d->err_word, d->sm_count, s);
+                               d->err_word, d->sm_count, s, peers, n_peers);
+  cudaError_t e;
   const gw::SplitKPlan sk = gw::plan_splitk(M, N, K, d->sm_count);
   if (sk.split >= 2)
-    return gw::launch_gemm_splitk(sk, a, dtype, M, K, lda, w, N, ldw, bias, epilogue, y, ldy,
-                                  d->err_word, s);
-  return gw::launch_gemm_tc(0, a, dtype, M, K, lda, w, N, ldw, nullptr, K, bias, epilogue, y, ldy,
-                            d->err_word, d->sm_count, s);
+    e = gw::launch_gemm_splitk(sk, a, dtype, M, K, lda, w, N, ldw, bias, epilogue, y, ldy,
+                               d->err_word, s);
+  else
+    e = gw::launch_gemm_tc(0, a, dtype, M, K, lda, w, N, ldw, nullptr, K, bias, epilogue, y, ldy,
+                           d->err_word, d->sm_count, s);
+  if (e != cudaSuccess || n_peers == 0) return e;
+  return gw::launch_copy_to_peers(y, M, N, ldy, peers, n_peers, d->sm_count, s);
 }
 }  // namespace
 
@@ -354,6 +361,50 @@ int gw_gather_gemm(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
     e = gw::launch_gemm_tc(2, x, dtype, M, K, ldx, w_packed, N, ldw, idx, n_alive, bias,
                            epilogue, y, ldy, d->err_word, d->sm_count, s, xg, ldp, counters);
   }
+  return e == cudaSuccess ? GW_OK : cuda_fail(e);
+}
+
+int gw_gather_gemm_peers(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
+                         const void* w_packed, int64_t N, int64_t ldw, const int64_t* idx,
+                         int64_t n_alive, const void* bias, int epilogue, void* y, int64_t ldy,
+                         void* const* peer_y, int n_peers, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  if (dtype != GW_DTYPE_F16 && dtype != GW_DTYPE_BF16) return GW_ERR_DTYPE;
+  if (!valid_epi(epilogue)) return GW_ERR_UNSUPPORTED;
+  if (n_peers < 0 || n_peers > GW_MAX_PEERS) return GW_ERR_UNSUPPORTED;
+  if (!matrix_ok(M, K, ldx) || n_alive < 0 || !matrix_ok(N, n_alive, ldw) ||
+      !matrix_ok(M, N, ldy))
+    return GW_ERR_SHAPE;
+  const gw::DeviceInfo* d = nullptr;
+  int st = current_device(&d);
+  if (st != GW_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (M == 0 || N == 0) return GW_OK;
+  if (!y || (n_peers > 0 && !peer_y)) return GW_ERR_NULL;
+  for (int i = 0; i < n_peers; ++i) {
+    if (!peer_y[i]) return GW_ERR_NULL;
+    if (!aligned16(peer_y[i])) return GW_ERR_ALIGN;
+  }
+  if (!aligned16(y) || (ldy % 8) != 0) return GW_ERR_ALIGN;
+  cudaError_t e;
+  if (n_alive == 0) {
+    e = gw::launch_fill_bias(y, dtype, M, N, ldy, bias, epilogue, s);
+    if (e == cudaSuccess) e = gw::launch_copy_to_peers(y, M, N, ldy, peer_y, n_peers, d->sm_count, s);
+    return e == cudaSuccess ? GW_OK : cuda_fail(e);
+  }
+  if (!x || !w_packed || !idx) return GW_ERR_NULL;
+  if (!aligned16(w_packed) || (ldw % 8) != 0) return GW_ERR_ALIGN;
+  if (n_alive > 0x7FFFFFFFll - 64) return GW_ERR_SHAPE;
+  if (!workspace) return GW_ERR_NULL;
+  if (workspace_bytes < gw_gather_gemm_workspace_bytes(M, n_alive, dtype)) return GW_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return GW_ERR_ALIGN;
+  const int64_t ldp = gemm_ld_pad(n_alive);
+  void* xg = static_cast<char*>(workspace) + gemm_ws_header(n_alive);
+  e = gw::launch_gather_columns(x, dtype, M, ldx, K, idx, n_alive, xg, ldp, n_alive,
+                                d->err_word, d->sm_count, s);
+  if (e != cudaSuccess) return cuda_fail(e);
+  e = launch_dense_gemm(xg, dtype, M, n_alive, ldp, w_packed, N, ldw, bias, epilogue, y, ldy, d, s,
+                        peer_y, n_peers);
   return e == cudaSuccess ? GW_OK : cuda_fail(e);
 }
 

@@ -188,6 +188,50 @@ cudaError_t launch_gather_columns(const void* src, int dtype, int64_t rows, int6
                     static_cast<uint16_t*>(dst), ld_dst, pad_to, err);
 }
 
+namespace {
+// y [rows, cols] -> each peer buffer at the same offsets, 16 bytes per thread
+// and step (rows are 16-byte aligned; a ragged row end is copied per element).
+struct PeerList {
+  uint16_t* p[kMaxPeers];
+};
+
+__global__ void __launch_bounds__(kGThreads)
+copy_to_peers_kernel(const uint16_t* __restrict__ y, int64_t rows, int64_t cols, int64_t ld,
+                     PeerList peers, int n_peers) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int64_t vec_per_row = (cols + 7) / 8;
+  const int64_t total = rows * vec_per_row;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * kGThreads + threadIdx.x; v < total;
+       v += static_cast<int64_t>(gridDim.x) * kGThreads) {
+    const int64_t r = v / vec_per_row;
+    const int64_t c = (v - r * vec_per_row) * 8;
+    const uint16_t* src = y + r * ld + c;
+    if (c + 8 <= cols) {
+      const uint4 q = __ldg(reinterpret_cast<const uint4*>(src));
+      for (int i = 0; i < n_peers; ++i) *reinterpret_cast<uint4*>(peers.p[i] + r * ld + c) = q;
+    } else {
+      for (int i = 0; i < n_peers; ++i)
+        for (int64_t j = c; j < cols; ++j) peers.p[i][r * ld + j] = y[r * ld + j];
+    }
+  }
+  __threadfence_system();
+}
+}  // namespace
+
+cudaError_t launch_copy_to_peers(const void* y, int64_t rows, int64_t cols, int64_t ld,
+                                 void* const* peers, int n_peers, int sm_count, cudaStream_t stream) {
+  if (rows == 0 || cols == 0 || n_peers == 0) return cudaSuccess;
+  if (n_peers < 0 || n_peers > kMaxPeers) return cudaErrorInvalidValue;
+  PeerList list{};
+  for (int i = 0; i < n_peers; ++i) list.p[i] = static_cast<uint16_t*>(peers[i]);
+  const int64_t total = rows * ((cols + 7) / 8);
+  const unsigned grid = clamp_grid(std::min<int64_t>((total + kGThreads - 1) / kGThreads,
+                                                     static_cast<int64_t>(sm_count > 0 ? sm_count : 148) * 8),
+                                   1 << 20);
+  return launch_pdl(copy_to_peers_kernel, dim3(grid), dim3(kGThreads), stream,
+                    static_cast<const uint16_t*>(y), rows, cols, ld, list, n_peers);
+}
+
 cudaError_t launch_gather_rows(const void* src, int dtype, int64_t rows_src, int64_t cols,
                                int64_t ld_src, const int64_t* idx, int64_t n_idx, void* dst,
                                int64_t ld_dst, unsigned int* err, int sm_count,

@@ -75,6 +75,10 @@ struct Tc2Params {
   int n_tiles;
   int num_tiles;
   unsigned int* err;
+  // Peer outputs: every finished tile is also stored, at the same place, into
+  // these buffers of other GPUs (same ldy; device addresses valid here).
+  int n_peers;
+  uint16_t* peers[kMaxPeers];
 };
 
 template <int DT>
@@ -284,6 +288,29 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
                              static_cast<int32_t>(warp_row0));
               bulk_commit_group();
             }
+            if (p.n_peers > 0 && warp_row0 < p.M && n_chunk < p.N) {
+              // The same 32 x 64 tile to every peer over NVLink: eight lanes per
+              // row write its 128 bytes, four rows per pass.
+              const int unit = lane & 7;
+              const int64_t col = n_chunk + unit * 8;
+#pragma unroll 1
+              for (int pass = 0; pass < 8; ++pass) {
+                const int r = pass * 4 + (lane >> 3);
+                const int64_t grow = warp_row0 + r;
+                if (grow >= p.M) break;
+                const uint4 v = *reinterpret_cast<const uint4*>(sb + r * (kEpiCols * 2) +
+                                                               ((unit ^ (r & 7)) << 4));
+                for (int i = 0; i < p.n_peers; ++i) {
+                  uint16_t* dst = p.peers[i] + grow * p.ldy + col;
+                  if (col + 8 <= p.N) {
+                    *reinterpret_cast<uint4*>(dst) = v;
+                  } else {
+                    const uint16_t* e = reinterpret_cast<const uint16_t*>(&v);
+                    for (int j = 0; j < 8 && col + j < p.N; ++j) dst[j] = e[j];
+                  }
+                }
+              }
+            }
           }
         } else if (row_ok) {
           if (p.y_vec_ok && n_base + 32 <= p.N) {
@@ -309,6 +336,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
     // Staging tiles stay valid (and y complete) until every TMA store has finished.
     if (lane == 0) bulk_wait_group_all();
     __syncwarp();
+    if (p.n_peers > 0) __threadfence_system();   // peer stores ordered before the kernel ends
   }
 
   __syncthreads();
@@ -338,7 +366,7 @@ bool use_pair_gemm(int64_t M, int64_t N, int sm_count) {
 cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int64_t lda,
                             const void* w, int64_t N, int64_t ldw, const void* bias, int epilogue,
                             void* y, int64_t ldy, unsigned int* err, int sm_count,
-                            cudaStream_t stream) {
+                            cudaStream_t stream, void* const* peers, int n_peers) {
   const int64_t m_tiles = (M + kPairM - 1) / kPairM;
   const int64_t n_tiles = (N + kPairN - 1) / kPairN;
   const int64_t num_tiles = m_tiles * n_tiles;
@@ -357,6 +385,9 @@ cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int6
   p.n_tiles = static_cast<int>(n_tiles);
   p.num_tiles = static_cast<int>(num_tiles);
   p.err = err;
+  if (n_peers < 0 || n_peers > kMaxPeers || (n_peers > 0 && !peers)) return cudaErrorInvalidValue;
+  p.n_peers = n_peers;
+  for (int i = 0; i < n_peers; ++i) p.peers[i] = static_cast<uint16_t*>(peers[i]);
 
   CUtensorMap ta, tb, ty;
   if (!make_tmap_kmajor(&ta, a, M, K, lda, kBK2, kHalfM)) return cudaErrorInvalidValue;
@@ -364,6 +395,7 @@ cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int6
   // TMA-store epilogue when y's rows are 16-byte aligned (else direct stores).
   p.y_tma = p.y_vec_ok && make_tmap_kmajor(&ty, y, M, N, ldy, kEpiCols, 32) ? 1 : 0;
   if (!p.y_tma) ty = ta;     // not read by the kernel
+  if (n_peers > 0 && !p.y_tma) return cudaErrorInvalidValue;   // peer stores ride the TMA path
 
   auto kern = dtype == GW_DTYPE_BF16 ? gemm_tc2_kernel<GW_DTYPE_BF16> : gemm_tc2_kernel<GW_DTYPE_F16>;
   cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), kSmemBytes2);

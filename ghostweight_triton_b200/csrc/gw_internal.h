@@ -39,6 +39,10 @@ cudaError_t launch_gather_rows_t(const void* src, int dtype, int64_t rows_src, i
                                  cudaStream_t stream);
 cudaError_t launch_fill_bias(void* y, int dtype, int64_t M, int64_t N, int64_t ldy,
                              const void* bias, int epilogue, cudaStream_t stream);
+// Copies y [rows, cols] (leading dimension ld, 16-bit, 16-byte aligned rows)
+// into each peer buffer at the same offsets.
+cudaError_t launch_copy_to_peers(const void* y, int64_t rows, int64_t cols, int64_t ld,
+                                 void* const* peers, int n_peers, int sm_count, cudaStream_t stream);
 cudaError_t launch_validate_indices(const int64_t* idx, int64_t n, int64_t K, int32_t* bad,
                                     cudaStream_t stream);
 
@@ -58,10 +62,14 @@ cudaError_t launch_gemm_tc(int a_mode, const void* x, int dtype, int64_t M, int6
 // gw_gemm_tc2.cu: CTA-pair (cta_group::2) tcgen05 GEMM, dense A [M, K] by TMA,
 // 256 x 256 tiles per pair. Chained to the previous kernel by programmatic
 // dependent launch.
+// With n_peers > 0 (at most kMaxPeers; requires y, ldy and every peer buffer
+// 16-byte aligned) each finished tile is also stored at the same offset into
+// each peer buffer (other GPUs' memory mapped into this process).
+constexpr int kMaxPeers = 7;
 cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int64_t lda,
                             const void* w, int64_t N, int64_t ldw, const void* bias, int epilogue,
                             void* y, int64_t ldy, unsigned int* err, int sm_count,
-                            cudaStream_t stream);
+                            cudaStream_t stream, void* const* peers = nullptr, int n_peers = 0);
 // Whether the CTA-pair kernel serves a dense-A GEMM of this shape.
 bool use_pair_gemm(int64_t M, int64_t N, int sm_count);
 

@@ -10,8 +10,12 @@ W[r*n : (r+1)*n, :] and bias slice; x is replicated. Each rank:
      would give (a column is dead in W iff it is dead in every shard);
   2. packs its shard's alive columns once (K2);
   3. runs the tcgen05 gather-GEMM on its rows (K3) -> y_r [M, n];
-  4. if the next op needs full rows, all-gathers y (NCCL over NVLink) into
-     [world, M, n] and re-lays it out to [M, N].
+  4. if the next op needs full rows, either all-gathers y (NCCL over NVLink)
+     into [world, M, n] and re-lays it out to [M, N] (gather_output=True), or
+     (gather_output="peers") lets the GEMM itself store every finished tile
+     into all ranks' full [M, N] outputs over NVLink (CUDA IPC mappings of the
+     peers' buffers, gw_gather_gemm_peers), followed by one small collective
+     that orders every rank's readers after every rank's GEMM.
 
 The reference has no multi-GPU code; this is the sharded configuration of the
 same hot path. Uneven splits pad the last shard with zero rows.
@@ -44,6 +48,88 @@ def union_mask(mask: torch.Tensor, group=None) -> torch.Tensor:
     return mask
 
 
+class PeerOutputs:
+    """Full-size [rows, cols] output buffers shared by the ranks of a group.
+
+    Each rank allocates `n_buf` buffers with cudaMalloc (outside torch's
+    caching allocator, so that CUDA IPC handles cover exactly one buffer),
+    exports their IPC handles, and opens every peer's; rank r then holds the
+    device addresses of all ranks' buffer i. Mappings are closed and buffers
+    freed by close() (collective: every rank closes its peer mappings, then a
+    barrier, then each frees its own).
+    """
+
+    def __init__(self, rows: int, cols: int, dtype: torch.dtype, group=None, n_buf: int = 2):
+        from cuda.bindings import runtime as rt
+
+        self._rt = rt
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.rows, self.cols, self.dtype = rows, cols, dtype
+        self.device = torch.cuda.current_device()
+        self._check(rt.cudaSetDevice(self.device))
+        nbytes = rows * cols * torch.empty((), dtype=dtype).element_size()
+        self._own: list[int] = []
+        self._peers: list[list[int]] = []        # [buf][rank] -> address (own at index rank)
+        handles = []
+        for _ in range(n_buf):
+            ptr = self._check(rt.cudaMalloc(nbytes))
+            self._own.append(int(ptr))
+            h = self._check(rt.cudaIpcGetMemHandle(ptr))
+            handles.append(bytes(h.reserved))
+        gathered: list = [None] * self.world
+        dist.all_gather_object(gathered, handles, group=group)
+        for i in range(n_buf):
+            addrs = []
+            for r in range(self.world):
+                if r == self.rank:
+                    addrs.append(self._own[i])
+                    continue
+                h = rt.cudaIpcMemHandle_t()
+                h.reserved = gathered[r][i]
+                addrs.append(int(self._check(
+                    rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess))))
+            self._peers.append(addrs)
+        self._views = [self._wrap(ptr, nbytes) for ptr in self._own]
+
+    @staticmethod
+    def _check(res):
+        err = res[0] if isinstance(res, tuple) else res
+        if int(err) != 0:
+            raise RuntimeError(f"CUDA runtime error {err}")
+        return res[1] if isinstance(res, tuple) and len(res) > 1 else None
+
+    def _wrap(self, ptr: int, nbytes: int) -> torch.Tensor:
+        class _Mem:
+            __cuda_array_interface__ = {"shape": (nbytes // 2,), "typestr": "<i2",
+                                        "data": (ptr, False), "strides": None,
+                                        "version": 2}
+        t = torch.as_tensor(_Mem(), device=torch.device("cuda", self.device))
+        assert t.data_ptr() == ptr and t.numel() == nbytes // 2
+        return t.view(self.dtype).view(self.rows, self.cols)
+
+    def local(self, i: int) -> torch.Tensor:
+        return self._views[i]
+
+    def peer_addresses(self, i: int, byte_offset: int = 0) -> list[int]:
+        """Addresses of the other ranks' buffer i (rank order, own rank left out)."""
+        return [a + byte_offset for r, a in enumerate(self._peers[i]) if r != self.rank]
+
+    def close(self) -> None:
+        rt = self._rt
+        for addrs in self._peers:
+            for r, a in enumerate(addrs):
+                if r != self.rank:
+                    rt.cudaIpcCloseMemHandle(a)
+        self._peers = []
+        dist.barrier(group=self.group)
+        for ptr in self._own:
+            rt.cudaFree(ptr)
+        self._own = []
+        self._views = []
+
+
 def gather_columns_from_ranks(y_local: torch.Tensor, n_total: int, group=None,
                               out: torch.Tensor | None = None) -> torch.Tensor:
     """All-gather row-major [M, n] shards into [M, n_total] (shard r -> columns r*n ..)."""
@@ -64,7 +150,7 @@ class ColumnParallelGhostLinear(nn.Module):
     """GhostLinear whose output features are split across the ranks of `group`."""
 
     def __init__(self, in_features: int, out_features: int, bias: bool = True,
-                 threshold: float = 0.0, gather_output: bool = True, group=None,
+                 threshold: float = 0.0, gather_output: bool | str = True, group=None,
                  device=None, dtype=None):
         super().__init__()
         self.group = group
@@ -80,6 +166,9 @@ class ColumnParallelGhostLinear(nn.Module):
         self.bias = nn.Parameter(torch.zeros(self.n_local, **factory)) if bias else None
         self.alive: torch.Tensor | None = None
         self.w_packed: torch.Tensor | None = None
+        self._peer_out: PeerOutputs | None = None
+        self._peer_step = 0
+        self._flag: torch.Tensor | None = None
 
     @property
     def k_alive(self) -> int:
@@ -138,8 +227,52 @@ class ColumnParallelGhostLinear(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         lead = x.shape[:-1]
+        # Peer stores need 16-byte aligned rows and block offsets (multiples of 8
+        # elements) on every rank -- the shard width decides it uniformly, so all
+        # ranks take the same path and issue the same collectives.
+        if (self.gather_output == "peers" and self.world > 1 and self.out_features % 8 == 0
+                and self.n_local % 8 == 0):
+            return self._forward_peers(x).reshape(*lead, self.out_features)
         y = self.local_forward(x)
         if not self.gather_output:
             return y.reshape(*lead, self.n_local)
         full = gather_columns_from_ranks(y, self.out_features, self.group)
         return full.reshape(*lead, self.out_features)
+
+    def _forward_peers(self, x: torch.Tensor) -> torch.Tensor:
+        """Full [M, N] output with the all-gather fused into the GEMM (peer stores).
+
+        The result is a view of one of two shared buffers used in turn: it stays
+        valid until the call after the next one. Every rank must call with the
+        same M.
+        """
+        from ghostweight_triton_b200 import _native
+
+        assert self.alive is not None, "call freeze_weight_mask() first"
+        x2 = x.reshape(-1, self.in_features).contiguous()
+        M = x2.shape[0]
+        po = self._peer_out
+        if po is None or po.rows < M:
+            if po is not None:
+                po.close()
+            po = self._peer_out = PeerOutputs(M, self.out_features, x2.dtype, self.group)
+            self._flag = torch.zeros(1, dtype=torch.int32, device=x2.device)
+        i = self._peer_step % 2
+        self._peer_step += 1
+        full = po.local(i)[:M]
+        n_real = self.row_stop - self.row_start
+        esize = full.element_size()
+        bias = self.bias[:n_real] if self.bias is not None else None
+        _native.gather_gemm_peers(x2, self.w_packed[:n_real], self.alive,
+                                  full[:, self.row_start:self.row_stop],
+                                  po.peer_addresses(i, self.row_start * esize), bias=bias)
+        # Orders every rank's readers of `full` after every rank's GEMM (and its
+        # peer stores): each rank joins only after its own GEMM on this stream.
+        dist.all_reduce(self._flag, group=self.group)
+        return full
+
+    def close(self) -> None:
+        """Release the shared output buffers (collective when gather_output="peers")."""
+        if self._peer_out is not None:
+            self._peer_out.close()
+            self._peer_out = None

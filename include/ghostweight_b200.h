@@ -212,6 +212,32 @@ GW_API int gw_gather_gemm(const void* x, int dtype, int64_t M, int64_t K, int64_
                           int strategy, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * gw_gather_gemm (pregather strategy, fp16/bf16) whose output also lands in
+ * other GPUs' memory: the M x N block written to y (leading dimension ldy) is
+ * written, at the same offsets, into each peer_y[i] -- device addresses valid
+ * in this process (e.g. opened CUDA IPC handles of the other ranks' output
+ * buffers), same leading dimension. This is the all-gather of a
+ * column-parallel layer fused into the GEMM: each rank passes its block of the
+ * full [M, N_total] output (y = full + column offset) and the same block of
+ * every peer's full output. Where the shape runs on the CTA-pair kernel the
+ * peer stores are issued from its epilogue tile by tile (over NVLink, plain
+ * stores, no multicast); otherwise a copy kernel follows the GEMM.
+ * Requires y, ldy and every peer_y 16-byte aligned, at most GW_MAX_PEERS peers,
+ * and a workspace as for gw_gather_gemm. No synchronisation between GPUs is
+ * done here: the caller orders the peers' readers after every rank's call
+ * (e.g. a collective on each stream) and must not let a peer overwrite a
+ * buffer that is still being read.
+ * Replaces the NCCL all-gather after the column-parallel GEMM
+ * (ghostweight_triton_b200/sharded.py); no counterpart in the reference.
+ */
+#define GW_MAX_PEERS 7
+GW_API int gw_gather_gemm_peers(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
+                                const void* w_packed, int64_t N, int64_t ldw, const int64_t* idx,
+                                int64_t n_alive, const void* bias, int epilogue, void* y,
+                                int64_t ldy, void* const* peer_y, int n_peers, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
+/*
  * Dense GEMM over an already-compacted activation (the two-step path of
  * gather.py:1-14: gather_compact followed by a matmul):
  *   y[m, n] = act( sum_{j < K} a[m, j] * w_packed[n, j] + bias[n] )

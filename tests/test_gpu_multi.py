@@ -56,12 +56,24 @@ def _rank_main(rank: int, world: int, port: int, q) -> None:
             y = layer(x)
             ref = F.linear(x.float(), w.float(), b.float())
             err = (y.float() - ref).abs().max().item()
-            results[str(dtype)] = (err, layer.k_alive, tuple(y.shape))
+            # The all-gather fused into the GEMM (peer stores over NVLink): three
+            # calls cycle through both shared buffers; each result equals NCCL's.
+            layer.gather_output = "peers"
+            errs = []
+            for step in range(3):
+                xs = x if step != 1 else x * 0.5
+                yp = layer(xs).clone()
+                refp = ref if step != 1 else F.linear(xs.float(), w.float(), b.float())
+                errs.append((yp.float() - refp).abs().max().item())
+            layer.close()
+            results[str(dtype)] = (max(err, *errs), layer.k_alive, tuple(y.shape))
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, results, None))
     except Exception as e:  # reported to the parent, which fails the test
-        q.put((rank, None, repr(e)))
+        import traceback
+
+        q.put((rank, None, repr(e) + "\n" + traceback.format_exc()))
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
