@@ -539,8 +539,21 @@ def run_mlp_sharded(args, world, rank, local):
     t_peers = timed(step_peers, args.steps, world) if world > 1 else t_nccl
     layer.close()
     t_full = min(t_nccl, t_peers)
+    # Roofline of the step: the slower of the tensor work per GPU and the bytes
+    # each GPU must receive over NVLink ((world-1)/world of y), at the measured
+    # peer-copy bandwidth of 770 GB/s per direction.
+    per = t_full / args.steps
+    t_flop = useful / world / (float(peaks["bf16_tflops"]) * 1e12)
+    link_bytes = (world - 1) / world * M * N * 2
+    t_link = link_bytes / 770e9
+    roof = {"bound": "nvlink" if t_link > t_flop else "tensor",
+            "achieved": round((link_bytes / per / 1e9) if t_link > t_flop else (useful / world / per / 1e12), 2),
+            "peak": 770.0 if t_link > t_flop else float(peaks["bf16_tflops"]),
+            "unit": "GB/s" if t_link > t_flop else "TFLOP/s",
+            "frac": round(max(t_link, t_flop) / per, 4), "traffic": None,
+            "peak_source": ("measured peer copy, 770 GB/s per direction" if t_link > t_flop
+                            else f"{peak_src} bf16_tflops")}
     if rank == 0:
-        per = t_full / args.steps
         line = {
             "metric": METRIC, "value": round(useful / per / 1e12, 3), "unit": "TFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -554,10 +567,11 @@ def run_mlp_sharded(args, world, rank, local):
             "nccl_allgather_ms": round(t_nccl / args.steps * 1e3, 4),
             "gemm_only_tflops": round(useful / (t_gemm / args.steps) / 1e12, 3),
             "gemm_only_ms": round(t_gemm / args.steps * 1e3, 4),
-            "roofline": {"bound": "tensor", "achieved": round(useful / world / (t_gemm / args.steps) / 1e12, 2),
-                         "peak": float(peaks["bf16_tflops"]), "unit": "TFLOP/s",
-                         "frac": round(useful / world / (t_gemm / args.steps) / 1e12 / float(peaks["bf16_tflops"]), 4),
-                         "peak_source": peak_src, "traffic": None},
+            "roofline": roof,
+            "gemm_roofline": {"bound": "tensor", "achieved": round(useful / world / (t_gemm / args.steps) / 1e12, 2),
+                              "peak": float(peaks["bf16_tflops"]), "unit": "TFLOP/s",
+                              "frac": round(useful / world / (t_gemm / args.steps) / 1e12 / float(peaks["bf16_tflops"]), 4),
+                              "peak_source": peak_src},
             "gpu_launches": 2 * args.steps,
         }
         print(json.dumps(line), flush=True)
