@@ -339,6 +339,14 @@ def sweep(device, peaks) -> list[dict]:
                 tg = graph_time(ours, 20, 1)
                 tdg = graph_time(dense, 20, 1)
                 useful = 2.0 * M * N * kp
+                runs = {}
+                if pattern.startswith("block"):
+                    # 64-column runs: the GEMM reads x in place (no gather launch).
+                    direct = lambda: ghost_linear(L["x"], L["wp"], L["idx"], out=L["y"], strategy="runs")
+                    tr = event_time(lambda i: direct(), iters=20)
+                    trg = graph_time(direct, 20, 1)
+                    runs = {"runs_us": round(tr * 1e6, 2), "graph_runs_us": round(trg * 1e6, 2),
+                            "graph_runs_speedup_vs_dense": round(tdg / trg, 3)}
                 rows.append({"M": M, "pattern": pattern, "sparsity": sp, "K_alive": kp,
                              "us": round(t * 1e6, 2), "useful_tflops": round(useful / t / 1e12, 1),
                              "dense_equiv_tflops": round(2.0 * M * N * K / t / 1e12, 1),
@@ -346,7 +354,7 @@ def sweep(device, peaks) -> list[dict]:
                              "cublas_dense_us": round(td * 1e6, 2),
                              "speedup_vs_dense": round(td / t, 3), "ideal": round(K / kp, 3),
                              "graph_us": round(tg * 1e6, 2), "graph_cublas_dense_us": round(tdg * 1e6, 2),
-                             "graph_speedup_vs_dense": round(tdg / tg, 3)})
+                             "graph_speedup_vs_dense": round(tdg / tg, 3), **runs})
                 del L
     torch.cuda.empty_cache()
     return rows
@@ -599,7 +607,8 @@ def run_mlp_sharded(args, world, rank, local):
             "ms_per_step": round(per * 1e3, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic, seeded",
             "config": {"workload": "sharded MLP projection x[8192,8192] W[28672,8192] bf16, 70% dead 128-col blocks",
-                       "K_alive": kp, "parallelism": f"column-parallel N over {world} GPUs, full output on every rank"},
+                       "K_alive": kp, "parallelism": f"column-parallel N over {world} GPUs, full output on every rank",
+                       "strategy": layer.strategy},
             "gather": ("GEMM epilogue stores every tile into all ranks' outputs over NVLink (CUDA IPC)"
                        if world > 1 and t_peers <= t_nccl else "NCCL all-gather + re-layout"),
             "peer_fused_ms": round(t_peers / args.steps * 1e3, 4) if world > 1 else None,
@@ -611,7 +620,7 @@ def run_mlp_sharded(args, world, rank, local):
                               "peak": float(peaks["bf16_tflops"]), "unit": "TFLOP/s",
                               "frac": round(useful / world / (t_gemm / args.steps) / 1e12 / float(peaks["bf16_tflops"]), 4),
                               "peak_source": peak_src},
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": (1 if layer.strategy == "runs" else 2) * args.steps,
         }
         print(json.dumps(line), flush=True)
 

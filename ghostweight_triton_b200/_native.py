@@ -31,7 +31,7 @@ GW_ERR_WORKSPACE = 5
 GW_ERR_CUDA = 6
 GW_ERR_DEVICE = 7
 GW_ERR_UNSUPPORTED = 8
-GEMM_STRATEGIES = {"auto": 0, "fused": 1, "pregather": 2, "overlap": 3}
+GEMM_STRATEGIES = {"auto": 0, "fused": 1, "pregather": 2, "overlap": 3, "runs": 4}
 DEVICE_ERR_WAIT_TIMEOUT = 1
 DEVICE_ERR_BAD_INDEX = 2
 
@@ -53,9 +53,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gw_gather_gemm": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _i,
                             _vp, _i64, _i, _vp, _sz, _vp]),
     "gw_gather_gemm_peers": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _i,
-                                  _vp, _i64, _vp, _i, _vp, _sz, _vp]),
+                                  _vp, _i64, _vp, _i, _i, _vp, _sz, _vp]),
     "gw_packed_gemm": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i, _vp, _i64, _vp]),
     "gw_validate_indices": (_i, [_vp, _i64, _i64, _vp, _vp]),
+    "gw_index_runs": (_i, [_vp, _i64, _i64, _vp, _vp]),
 }
 
 _lib: ctypes.CDLL | None = None
@@ -276,7 +277,8 @@ def gather_gemm(x: torch.Tensor, w_packed: torch.Tensor, idx: torch.Tensor, y: t
     """y = act(x[:, idx] @ w_packed[:, :len(idx)]^T + bias) on the current stream.
 
     strategy "auto" uses the two-launch pregather path when `workspace` is large
-    enough, else the single fused kernel; "fused" / "pregather" force one.
+    enough, else the single fused kernel; "fused" / "pregather" force one;
+    "runs" loads x directly (idx must be 64-column runs: see index_runs).
     """
     _rowmajor(x, w_packed, y)
     assert idx.dtype == torch.int64 and idx.is_contiguous()
@@ -303,12 +305,14 @@ def gather_gemm(x: torch.Tensor, w_packed: torch.Tensor, idx: torch.Tensor, y: t
 
 def gather_gemm_peers(x: torch.Tensor, w_packed: torch.Tensor, idx: torch.Tensor, y: torch.Tensor,
                       peer_addresses: list[int], bias: torch.Tensor | None = None,
-                      activation: str | None = None, workspace: torch.Tensor | None = None) -> None:
-    """gather_gemm (pregather) whose output block y also goes to each peer address.
+                      activation: str | None = None, workspace: torch.Tensor | None = None,
+                      strategy: str = "pregather") -> None:
+    """gather_gemm whose output block y also goes to each peer address.
 
     y is this rank's block of a full output (a column slice view, row stride
     ldy); peer_addresses are device addresses of the same block in the other
-    ranks' full outputs (same row stride), valid in this process.
+    ranks' full outputs (same row stride), valid in this process. strategy is
+    "pregather" (gather, then the GEMM) or "runs" (no gather; see index_runs).
     """
     _rowmajor(x, w_packed)
     assert y.ndim == 2 and y.stride(1) == 1
@@ -316,7 +320,7 @@ def gather_gemm_peers(x: torch.Tensor, w_packed: torch.Tensor, idx: torch.Tensor
     M, K = x.shape
     N = y.shape[1]
     n = idx.numel()
-    if workspace is None:
+    if workspace is None and strategy != "runs":
         nbytes = gather_gemm_workspace_bytes(M, n, x.dtype)
         workspace = gemm_workspace(x.device, nbytes) if nbytes else None
     ws_ptr, ws_bytes = (None, 0) if workspace is None else (workspace.data_ptr(), workspace.numel() * workspace.element_size())
@@ -325,7 +329,8 @@ def gather_gemm_peers(x: torch.Tensor, w_packed: torch.Tensor, idx: torch.Tensor
         st = load().gw_gather_gemm_peers(
             _ptr(x), dtype_code(x.dtype), M, K, max(x.stride(0), K), _ptr(w_packed), N,
             max(w_packed.stride(0), n), _ptr(idx), n, _ptr(bias), epilogue_code(activation),
-            _ptr(y), y.stride(0), peers, len(peer_addresses), ws_ptr, ws_bytes, _stream(x.device))
+            _ptr(y), y.stride(0), peers, len(peer_addresses), GEMM_STRATEGIES[strategy], ws_ptr,
+            ws_bytes, _stream(x.device))
     _check(st, "gw_gather_gemm_peers")
 
 
@@ -349,6 +354,16 @@ def validate_indices(idx: torch.Tensor, K: int) -> int:
     with _on_device(idx.device):
         st = load().gw_validate_indices(_ptr(idx), idx.numel(), int(K), _ptr(bad), _stream(idx.device))
     _check(st, "gw_validate_indices")
+    return int(bad.item())
+
+
+def index_runs(idx: torch.Tensor, K: int) -> int:
+    """Entries of idx that break the 64-column-run structure of strategy "runs"
+    (0: the list qualifies; synchronises)."""
+    bad = torch.empty(1, dtype=torch.int32, device=idx.device)
+    with _on_device(idx.device):
+        st = load().gw_index_runs(_ptr(idx), idx.numel(), int(K), _ptr(bad), _stream(idx.device))
+    _check(st, "gw_index_runs")
     return int(bad.item())
 
 

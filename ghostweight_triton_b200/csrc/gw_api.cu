@@ -277,21 +277,25 @@ namespace {
 // the SMs (decode-sized M), else the single-CTA persistent kernel.
 // With peers, the output is also written into each peer buffer: by the pair
 // kernel's epilogue, tile by tile, or by a copy kernel after the other kernels.
+// With a_cols, a is x [M, a_width] and K the count of alive columns, which form
+// 64-column runs starting at a_cols[64 j] (GW_GEMM_RUNS).
 cudaError_t launch_dense_gemm(const void* a, int dtype, int64_t M, int64_t K, int64_t lda,
                               const void* w, int64_t N, int64_t ldw, const void* bias, int epilogue,
                               void* y, int64_t ldy, const gw::DeviceInfo* d, cudaStream_t s,
-                              void* const* peers = nullptr, int n_peers = 0) {
+                              void* const* peers = nullptr, int n_peers = 0,
+                              const int64_t* a_cols = nullptr, int64_t a_width = 0) {
   if (gw::use_pair_gemm(M, N, d->sm_count))
     return gw::launch_gemm_tc2(a, dtype, M, K, lda, w, N, ldw, bias, epilogue, y, ldy,
-                               d->err_word, d->sm_count, s, peers, n_peers);
+                               d->err_word, d->sm_count, s, peers, n_peers, a_cols, a_width);
   cudaError_t e;
   const gw::SplitKPlan sk = gw::plan_splitk(M, N, K, d->sm_count);
   if (sk.split >= 2)
     e = gw::launch_gemm_splitk(sk, a, dtype, M, K, lda, w, N, ldw, bias, epilogue, y, ldy,
-                               d->err_word, s);
+                               d->err_word, s, a_cols, a_width);
   else
-    e = gw::launch_gemm_tc(0, a, dtype, M, K, lda, w, N, ldw, nullptr, K, bias, epilogue, y, ldy,
-                           d->err_word, d->sm_count, s);
+    e = gw::launch_gemm_tc(0, a, dtype, M, a_cols ? a_width : K, lda, w, N, ldw, nullptr, K, bias,
+                           epilogue, y, ldy, d->err_word, d->sm_count, s, nullptr, 0, nullptr,
+                           a_cols);
   if (e != cudaSuccess || n_peers == 0) return e;
   return gw::launch_copy_to_peers(y, M, N, ldy, peers, n_peers, d->sm_count, s);
 }
@@ -310,7 +314,7 @@ int gw_gather_gemm(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
   if (!valid_dtype(dtype)) return GW_ERR_DTYPE;
   if (!valid_epi(epilogue)) return GW_ERR_UNSUPPORTED;
   if (strategy != GW_GEMM_AUTO && strategy != GW_GEMM_FUSED && strategy != GW_GEMM_PREGATHER &&
-      strategy != GW_GEMM_OVERLAP)
+      strategy != GW_GEMM_OVERLAP && strategy != GW_GEMM_RUNS)
     return GW_ERR_UNSUPPORTED;
   if (!matrix_ok(M, K, ldx) || n_alive < 0 || !matrix_ok(N, n_alive, ldw) ||
       !matrix_ok(M, N, ldy))
@@ -336,6 +340,13 @@ int gw_gather_gemm(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
   }
   if (!aligned16(w_packed) || (ldw % 8) != 0) return GW_ERR_ALIGN;
   if (n_alive > 0x7FFFFFFFll - 64) return GW_ERR_SHAPE;
+  if (strategy == GW_GEMM_RUNS) {
+    if ((n_alive % 64) != 0) return GW_ERR_UNSUPPORTED;
+    if (!aligned16(x) || (ldx % 8) != 0) return GW_ERR_ALIGN;
+    e = launch_dense_gemm(x, dtype, M, n_alive, ldx, w_packed, N, ldw, bias, epilogue, y, ldy, d,
+                          s, nullptr, 0, idx, K);
+    return e == cudaSuccess ? GW_OK : cuda_fail(e);
+  }
   const size_t need = gw_gather_gemm_workspace_bytes(M, n_alive, dtype);
   const bool ws_ok = workspace != nullptr && workspace_bytes >= need;
   int strat = strategy;
@@ -367,11 +378,13 @@ int gw_gather_gemm(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
 int gw_gather_gemm_peers(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
                          const void* w_packed, int64_t N, int64_t ldw, const int64_t* idx,
                          int64_t n_alive, const void* bias, int epilogue, void* y, int64_t ldy,
-                         void* const* peer_y, int n_peers, void* workspace, size_t workspace_bytes,
-                         void* stream) {
+                         void* const* peer_y, int n_peers, int strategy, void* workspace,
+                         size_t workspace_bytes, void* stream) {
   if (dtype != GW_DTYPE_F16 && dtype != GW_DTYPE_BF16) return GW_ERR_DTYPE;
   if (!valid_epi(epilogue)) return GW_ERR_UNSUPPORTED;
   if (n_peers < 0 || n_peers > GW_MAX_PEERS) return GW_ERR_UNSUPPORTED;
+  if (strategy != GW_GEMM_AUTO && strategy != GW_GEMM_PREGATHER && strategy != GW_GEMM_RUNS)
+    return GW_ERR_UNSUPPORTED;
   if (!matrix_ok(M, K, ldx) || n_alive < 0 || !matrix_ok(N, n_alive, ldw) ||
       !matrix_ok(M, N, ldy))
     return GW_ERR_SHAPE;
@@ -395,6 +408,13 @@ int gw_gather_gemm_peers(const void* x, int dtype, int64_t M, int64_t K, int64_t
   if (!x || !w_packed || !idx) return GW_ERR_NULL;
   if (!aligned16(w_packed) || (ldw % 8) != 0) return GW_ERR_ALIGN;
   if (n_alive > 0x7FFFFFFFll - 64) return GW_ERR_SHAPE;
+  if (strategy == GW_GEMM_RUNS) {
+    if ((n_alive % 64) != 0) return GW_ERR_UNSUPPORTED;
+    if (!aligned16(x) || (ldx % 8) != 0) return GW_ERR_ALIGN;
+    e = launch_dense_gemm(x, dtype, M, n_alive, ldx, w_packed, N, ldw, bias, epilogue, y, ldy, d,
+                          s, peer_y, n_peers, idx, K);
+    return e == cudaSuccess ? GW_OK : cuda_fail(e);
+  }
   if (!workspace) return GW_ERR_NULL;
   if (workspace_bytes < gw_gather_gemm_workspace_bytes(M, n_alive, dtype)) return GW_ERR_WORKSPACE;
   if (!aligned16(workspace)) return GW_ERR_ALIGN;
@@ -442,6 +462,16 @@ int gw_validate_indices(const int64_t* idx, int64_t n, int64_t K, int32_t* bad_c
   if (st != GW_OK) return st;
   cudaError_t e = gw::launch_validate_indices(idx, n, K, bad_count,
                                               static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? GW_OK : cuda_fail(e);
+}
+
+int gw_index_runs(const int64_t* idx, int64_t n, int64_t K, int32_t* bad_count, void* stream) {
+  if (n < 0 || K < 0) return GW_ERR_SHAPE;
+  if (!bad_count || (n > 0 && !idx)) return GW_ERR_NULL;
+  const gw::DeviceInfo* d = nullptr;
+  int st = current_device(&d);
+  if (st != GW_OK) return st;
+  cudaError_t e = gw::launch_index_runs(idx, n, K, bad_count, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? GW_OK : cuda_fail(e);
 }
 

@@ -39,6 +39,23 @@ __device__ __forceinline__ void raise_error(unsigned int* err, unsigned int bits
   if (err) atomicOr(err, bits);
 }
 
+// First x column of k-block j when the alive columns form 64-column runs:
+// cols[64 j]. Producers load it one stage ahead (run_start_load) so that the
+// load's latency hides behind the wait for a free stage, then validate it
+// (run_start_check): a TMA box may only start at a column whose byte offset is
+// a multiple of 16 (8 columns of 16 bits), so a start outside [0, width) or not
+// a multiple of 8 raises GW_DERR_BAD_INDEX and column 0 is loaded instead.
+__device__ __forceinline__ int64_t run_start_load(const int64_t* cols, int j) {
+  return __ldg(cols + static_cast<int64_t>(j) * 64);
+}
+__device__ __forceinline__ int run_start_check(int64_t c, int64_t width, unsigned int* err) {
+  if (c < 0 || c >= width || (c & 7) != 0) {
+    raise_error(err, GW_DERR_BAD_INDEX);
+    return 0;
+  }
+  return static_cast<int>(c);
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -159,6 +159,23 @@ __global__ void validate_indices_kernel(const int64_t* __restrict__ idx, int64_t
   if ((threadIdx.x & 31) == 0 && local) atomicAdd(bad, local);
 }
 
+// Entries that break the 64-column-run structure: idx[64 j + r] must equal
+// idx[64 j] + r, idx[64 j] must be a multiple of 8, every entry must lie in
+// [0, K) and the list must end on a whole run.
+__global__ void index_runs_kernel(const int64_t* __restrict__ idx, int64_t n, int64_t K,
+                                  int32_t* bad) {
+  int local = 0;
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < n;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = t & 63;
+    const int64_t start = idx[t - r];
+    const int64_t c = idx[t];
+    local += (c < 0 || c >= K || c != start + r || (start & 7) != 0 || t - r + 64 > n) ? 1 : 0;
+  }
+  local = __reduce_add_sync(0xFFFFFFFFu, local);
+  if ((threadIdx.x & 31) == 0 && local) atomicAdd(bad, local);
+}
+
 inline unsigned clamp_grid(int64_t v, int64_t hi) {
   if (v < 1) v = 1;
   if (v > hi) v = hi;
@@ -308,6 +325,15 @@ cudaError_t launch_validate_indices(const int64_t* idx, int64_t n, int64_t K, in
   if (e != cudaSuccess || n == 0) return e;
   const unsigned grid = clamp_grid((n + 255) / 256, 1024);
   validate_indices_kernel<<<grid, 256, 0, stream>>>(idx, n, K, bad);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_index_runs(const int64_t* idx, int64_t n, int64_t K, int32_t* bad,
+                              cudaStream_t stream) {
+  cudaError_t e = cudaMemsetAsync(bad, 0, sizeof(int32_t), stream);
+  if (e != cudaSuccess || n == 0) return e;
+  const unsigned grid = clamp_grid((n + 255) / 256, 1024);
+  index_runs_kernel<<<grid, 256, 0, stream>>>(idx, n, K, bad);
   return cudaGetLastError();
 }
 

@@ -69,6 +69,8 @@ struct SkParams {
   int split;                 // cluster size S
   int a_tx_bytes;            // bytes of one x' box (its rows: min(M rounded up to 8, 128))
   unsigned int* err;
+  const int64_t* a_cols;     // alive columns in 64-column runs: A is x, k-block kb at a_cols[64 kb]
+  int64_t a_width;           // columns of x (with a_cols)
 };
 
 __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t cluster_addr) {
@@ -202,14 +204,18 @@ gemm_splitk_kernel(const __grid_constant__ CUtensorMap tmap_b,
       asm volatile("griddepcontrol.wait;" ::: "memory");   // x' may come from the previous kernel
       int issued = 0;
       bool ok = true;
+      int64_t nxt = p.a_cols ? run_start_load(p.a_cols, kb0) : 0;   // next k-block's run start
       for (int kb = kb0; kb < kb1; ++kb, ++issued) {
         const int s = issued % C::kStages;
         const uint32_t ph = (issued / C::kStages) & 1u;
+        const int64_t cur = nxt;
+        if (p.a_cols && kb + 1 < kb1) nxt = run_start_load(p.a_cols, kb + 1);
         if (!mbar_wait(empty(s), ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
         const uint32_t a_s = sbase + s * C::kStageBytes;
         mbar_arrive_expect_tx(full(s), C::kBBytes + p.a_tx_bytes);
         tma_load_2d(a_s + C::kABytes, &tmap_b, kb * kSkBK, n_blk * BN, full(s));
-        tma_load_2d(a_s, &tmap_a, kb * kSkBK, m_blk * kSkBM, full(s));
+        const int ax = p.a_cols ? run_start_check(cur, p.a_width, p.err) : kb * kSkBK;
+        tma_load_2d(a_s, &tmap_a, ax, m_blk * kSkBM, full(s));
       }
       if (!ok) {
         // Loads still in flight complete before the ring is reused or the CTA exits.
@@ -411,7 +417,8 @@ SplitKPlan plan_splitk(int64_t M, int64_t N, int64_t K, int sm_count) {
 cudaError_t launch_gemm_splitk(const SplitKPlan& plan, const void* a, int dtype, int64_t M,
                                int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,
                                const void* bias, int epilogue, void* y, int64_t ldy,
-                               unsigned int* err, cudaStream_t stream) {
+                               unsigned int* err, cudaStream_t stream, const int64_t* a_cols,
+                               int64_t a_width) {
   if (plan.split < 2 || plan.split > 8 || plan.tiles <= 0 || plan.tiles > 65535)
     return cudaErrorInvalidValue;
   SkParams p{};
@@ -426,7 +433,10 @@ cudaError_t launch_gemm_splitk(const SplitKPlan& plan, const void* a, int dtype,
   p.m_tiles = static_cast<int>((M + kSkBM - 1) / kSkBM);
   p.split = plan.split;
   p.err = err;
+  p.a_cols = a_cols;
+  p.a_width = a_width;
   if (p.num_kb < plan.split) return cudaErrorInvalidValue;
+  if (a_cols && (K % kSkBK) != 0) return cudaErrorInvalidValue;
   // With fewer than 128 rows the x' box covers only the rows that exist; the
   // MMA still reads 128 rows of shared memory, and the rows past the box hold
   // stale data that reaches only output rows that are never stored.
@@ -434,7 +444,8 @@ cudaError_t launch_gemm_splitk(const SplitKPlan& plan, const void* a, int dtype,
   p.a_tx_bytes = a_rows * kSkBK * 2;
 
   CUtensorMap ta, tb;
-  if (!make_tmap_kmajor(&ta, a, M, K, lda, kSkBK, a_rows)) return cudaErrorInvalidValue;
+  if (!make_tmap_kmajor(&ta, a, M, a_cols ? a_width : K, lda, kSkBK, a_rows))
+    return cudaErrorInvalidValue;
   if (!make_tmap_kmajor(&tb, w, N, K, ldw, kSkBK, plan.bn)) return cudaErrorInvalidValue;
   const bool bf = dtype == GW_DTYPE_BF16;
   switch (plan.bn) {

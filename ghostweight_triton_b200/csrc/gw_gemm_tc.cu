@@ -103,6 +103,7 @@ struct TcParams {
   uint16_t* xg;                 // kAOverlap: scratch x' [M, ldg]
   int64_t ldg;
   unsigned int* kb_ready;       // kAOverlap: per-k-block count of gathered 128-row units
+  const int64_t* a_cols;        // kATma: k-block kb of A starts at x column a_cols[64 kb] (or null)
 };
 
 template <int BN, int DT, int AMODE>
@@ -169,12 +170,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
       uint32_t it = 0;
       int ready_kb = 0;   // kAOverlap: k-blocks of x' known to be complete
       bool ok = true;
+      const int64_t* a_cols = AMODE == kATma ? p.a_cols : nullptr;
+      int64_t nxt = a_cols ? run_start_load(a_cols, 0) : 0;   // next k-block's run start
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
         const int m_blk = tile % p.m_tiles;
         const int n_blk = tile / p.m_tiles;
         for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
           const int s = it % C::kStages;
           const uint32_t ph = (it / C::kStages) & 1u;
+          const int64_t cur = nxt;
+          if (a_cols) nxt = run_start_load(a_cols, kb + 1 == p.num_kb ? 0 : kb + 1);
           if (AMODE == kAOverlap && ready_kb <= kb) {
             while (ready_kb <= kb) {
               if (!wait_counter_geq(p.kb_ready + ready_kb, static_cast<uint32_t>(p.m_tiles),
@@ -193,7 +198,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
           } else {
             mbar_arrive_expect_tx(full_b(s), C::kBBytes + C::kABytes);
             tma_load_2d(b_s, &tmap_b, kb * kBK, n_blk * BN, full_b(s));
-            tma_load_2d(a_s, &tmap_a, kb * kBK, m_blk * kBM, full_b(s));
+            const int ax = a_cols ? run_start_check(cur, p.K, p.err) : kb * kBK;
+            tma_load_2d(a_s, &tmap_a, ax, m_blk * kBM, full_b(s));
           }
         }
       }
@@ -486,7 +492,7 @@ cudaError_t launch_gemm_tc(int a_mode, const void* x, int dtype, int64_t M, int6
                            const int64_t* idx, int64_t n_alive, const void* bias, int epilogue,
                            void* y, int64_t ldy, unsigned int* err, int sm_count,
                            cudaStream_t stream, void* scratch_xg, int64_t ldg,
-                           unsigned int* kb_ready) {
+                           unsigned int* kb_ready, const int64_t* a_cols) {
   // Tile width 256 (measured best on B200 where there are several waves:
   // wider tiles reuse A more per byte moved), 128 for narrow N. When 256-wide
   // tiles leave SMs idle in a single wave and 192-wide ones still fit in one
@@ -532,13 +538,16 @@ cudaError_t launch_gemm_tc(int a_mode, const void* x, int dtype, int64_t M, int6
   p.xg = static_cast<uint16_t*>(scratch_xg);
   p.ldg = ldg;
   p.kb_ready = kb_ready;
+  p.a_cols = a_mode == kATma ? a_cols : nullptr;
+  if (p.a_cols && (n_alive % kBK) != 0) return cudaErrorInvalidValue;
 
   CUtensorMap tb, ta;
   if (!make_tmap_kmajor(&tb, w, N, n_alive, ldw, kBK, BN)) return cudaErrorInvalidValue;
   if (a_mode == kASmemGather) {
     ta = tb;   // unused by the shared-memory gather variant
   } else if (a_mode == kATma) {
-    if (!make_tmap_kmajor(&ta, x, M, n_alive, ldx, kBK, kBM)) return cudaErrorInvalidValue;
+    // A is the compacted x' [M, n_alive], or x [M, K] itself with a_cols.
+    if (!make_tmap_kmajor(&ta, x, M, a_cols ? K : n_alive, ldx, kBK, kBM)) return cudaErrorInvalidValue;
   } else {
     if (!scratch_xg || !kb_ready || (ldg % 8) != 0) return cudaErrorInvalidValue;
     if (!make_tmap_kmajor(&ta, scratch_xg, M, n_alive, ldg, kBK, kBM)) return cudaErrorInvalidValue;

@@ -79,6 +79,10 @@ struct Tc2Params {
   // these buffers of other GPUs (same ldy; device addresses valid here).
   int n_peers;
   uint16_t* peers[kMaxPeers];
+  // Alive columns in 64-column runs: A is x itself and k atom kb starts at
+  // column a_cols[64 kb] (null: A is the compacted x', atom kb at 64 kb).
+  const int64_t* a_cols;
+  int64_t a_width;          // columns of x (with a_cols)
 };
 
 template <int DT>
@@ -143,6 +147,12 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
       asm volatile("griddepcontrol.wait;" ::: "memory");   // A may come from the previous kernel
       uint32_t it = 0;
       bool ok = true;
+      // a_cols: run starts of the stage after the current one, loaded ahead.
+      int64_t nxt0 = 0, nxt1 = 0;
+      if (p.a_cols) {
+        nxt0 = run_start_load(p.a_cols, 0);
+        if (p.num_kb > 1) nxt1 = run_start_load(p.a_cols, 1);
+      }
       for (int tile = pair; ok && tile < p.num_tiles; tile += num_pairs) {
         const int m_blk = tile % p.m_tiles;
         const int n_blk = tile / p.m_tiles;
@@ -151,6 +161,12 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
         for (int ks = 0; ks < p.num_ks; ++ks, ++it) {
           const int s = it % kStages2;
           const uint32_t ph = (it / kStages2) & 1u;
+          const int64_t cur0 = nxt0, cur1 = nxt1;
+          if (p.a_cols) {
+            const int nk = (ks + 1 == p.num_ks ? 0 : ks + 1) * kAtoms2;
+            nxt0 = run_start_load(p.a_cols, nk);
+            if (nk + 1 < p.num_kb) nxt1 = run_start_load(p.a_cols, nk + 1);
+          }
           if (!mbar_wait_cluster(empty(s), ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
           const uint32_t a_s = sbase + s * kStageBytes2;
           const uint32_t b_s = a_s + kABytes2;
@@ -160,7 +176,8 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
           if (rank == 0) mbar_arrive_expect_tx(full(s), 2u * 2u * atoms * kAtomBytes2);
           for (int a = 0; a < atoms; ++a) {
             const int kx = (ks * kAtoms2 + a) * kBK2;
-            tma_load_2d_pair(a_s + a * kAtomBytes2, &tmap_a, kx, a_row, leader_full);
+            const int ax = p.a_cols ? run_start_check(a == 0 ? cur0 : cur1, p.a_width, p.err) : kx;
+            tma_load_2d_pair(a_s + a * kAtomBytes2, &tmap_a, ax, a_row, leader_full);
             tma_load_2d_pair(b_s + a * kAtomBytes2, &tmap_b, kx, b_row, leader_full);
           }
         }
@@ -366,7 +383,8 @@ bool use_pair_gemm(int64_t M, int64_t N, int sm_count) {
 cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int64_t lda,
                             const void* w, int64_t N, int64_t ldw, const void* bias, int epilogue,
                             void* y, int64_t ldy, unsigned int* err, int sm_count,
-                            cudaStream_t stream, void* const* peers, int n_peers) {
+                            cudaStream_t stream, void* const* peers, int n_peers,
+                            const int64_t* a_cols, int64_t a_width) {
   const int64_t m_tiles = (M + kPairM - 1) / kPairM;
   const int64_t n_tiles = (N + kPairN - 1) / kPairN;
   const int64_t num_tiles = m_tiles * n_tiles;
@@ -389,8 +407,12 @@ cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int6
   p.n_peers = n_peers;
   for (int i = 0; i < n_peers; ++i) p.peers[i] = static_cast<uint16_t*>(peers[i]);
 
+  p.a_cols = a_cols;
+  p.a_width = a_width;
   CUtensorMap ta, tb, ty;
-  if (!make_tmap_kmajor(&ta, a, M, K, lda, kBK2, kHalfM)) return cudaErrorInvalidValue;
+  // With a_cols, A is x [M, a_width] (K = the alive count, a multiple of 64).
+  if (a_cols && (K % kBK2) != 0) return cudaErrorInvalidValue;
+  if (!make_tmap_kmajor(&ta, a, M, a_cols ? a_width : K, lda, kBK2, kHalfM)) return cudaErrorInvalidValue;
   if (!make_tmap_kmajor(&tb, w, N, K, ldw, kBK2, kHalfN)) return cudaErrorInvalidValue;
   // TMA-store epilogue when y's rows are 16-byte aligned (else direct stores).
   p.y_tma = p.y_vec_ok && make_tmap_kmajor(&ty, y, M, N, ldy, kEpiCols, 32) ? 1 : 0;

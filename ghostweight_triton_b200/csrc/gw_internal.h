@@ -45,6 +45,8 @@ cudaError_t launch_copy_to_peers(const void* y, int64_t rows, int64_t cols, int6
                                  void* const* peers, int n_peers, int sm_count, cudaStream_t stream);
 cudaError_t launch_validate_indices(const int64_t* idx, int64_t n, int64_t K, int32_t* bad,
                                     cudaStream_t stream);
+cudaError_t launch_index_runs(const int64_t* idx, int64_t n, int64_t K, int32_t* bad,
+                              cudaStream_t stream);
 
 // gw_gemm_tc.cu: tcgen05 gather-GEMM / packed GEMM (fp16, bf16).
 // a_mode: 0 -> A is a dense [M, n_alive] matrix loaded by TMA (idx unused)
@@ -52,12 +54,14 @@ cudaError_t launch_validate_indices(const int64_t* idx, int64_t n, int64_t K, in
 //         2 -> warps gather x[:, idx] into scratch_xg [M, ldg] inside the kernel
 //              (per-k-block counters kb_ready[num_kb], zeroed by the launcher),
 //              then TMA streams it; cooperative launch
+// a_mode 0 with a_cols: as launch_gemm_tc2's a_cols (A = x [M, K], k-block kb
+// loaded from column a_cols[64 kb], n_alive a multiple of 64).
 cudaError_t launch_gemm_tc(int a_mode, const void* x, int dtype, int64_t M, int64_t K,
                            int64_t ldx, const void* w, int64_t N, int64_t ldw,
                            const int64_t* idx, int64_t n_alive, const void* bias, int epilogue,
                            void* y, int64_t ldy, unsigned int* err, int sm_count,
                            cudaStream_t stream, void* scratch_xg = nullptr, int64_t ldg = 0,
-                           unsigned int* kb_ready = nullptr);
+                           unsigned int* kb_ready = nullptr, const int64_t* a_cols = nullptr);
 
 // gw_gemm_tc2.cu: CTA-pair (cta_group::2) tcgen05 GEMM, dense A [M, K] by TMA,
 // 256 x 256 tiles per pair. Chained to the previous kernel by programmatic
@@ -66,10 +70,14 @@ cudaError_t launch_gemm_tc(int a_mode, const void* x, int dtype, int64_t M, int6
 // 16-byte aligned) each finished tile is also stored at the same offset into
 // each peer buffer (other GPUs' memory mapped into this process).
 constexpr int kMaxPeers = 7;
+// With a_cols (alive columns in 64-column runs, each starting at a multiple of
+// 8; K = their count, a multiple of 64), A is x [M, a_width] itself and k atom
+// kb is loaded from column a_cols[64 kb]: no compacted copy of x is needed.
 cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int64_t lda,
                             const void* w, int64_t N, int64_t ldw, const void* bias, int epilogue,
                             void* y, int64_t ldy, unsigned int* err, int sm_count,
-                            cudaStream_t stream, void* const* peers = nullptr, int n_peers = 0);
+                            cudaStream_t stream, void* const* peers = nullptr, int n_peers = 0,
+                            const int64_t* a_cols = nullptr, int64_t a_width = 0);
 // Whether the CTA-pair kernel serves a dense-A GEMM of this shape.
 bool use_pair_gemm(int64_t M, int64_t N, int sm_count);
 
@@ -81,6 +89,7 @@ cudaError_t launch_gemm_f32(const float* x, int64_t M, int64_t K, int64_t ldx, c
 
 // gw_gemm_splitk.cu: split-K over a cluster of `split` CTAs reduced in DSMEM,
 // for dense-A GEMMs whose output has too few tiles to occupy the SMs.
+// a_cols / a_width: as launch_gemm_tc2's.
 struct SplitKPlan {
   int bn = 0;            // tile width (32 .. 256)
   int split = 1;         // cluster size; 1 = not worth it (use the persistent kernels)
@@ -90,7 +99,8 @@ SplitKPlan plan_splitk(int64_t M, int64_t N, int64_t K, int sm_count);
 cudaError_t launch_gemm_splitk(const SplitKPlan& plan, const void* a, int dtype, int64_t M,
                                int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,
                                const void* bias, int epilogue, void* y, int64_t ldy,
-                               unsigned int* err, cudaStream_t stream);
+                               unsigned int* err, cudaStream_t stream,
+                               const int64_t* a_cols = nullptr, int64_t a_width = 0);
 
 // Driver entry point for cuTensorMapEncodeTiled (resolved once, no libcuda link).
 void* tensor_map_encoder();

@@ -46,7 +46,8 @@ def ghostweight_matmul(
     BLOCK_M, BLOCK_N, BLOCK_K : accepted for signature compatibility; ignored.
     bias          : optional [N], added in the fp32 epilogue (extension).
     activation    : None, "gelu" or "gelu_tanh", applied after the bias (extension).
-    strategy      : "auto" | "pregather" | "fused" (extension, see module docstring).
+    strategy      : "auto" | "pregather" | "fused" | "overlap" | "runs" (extension, see
+                    module docstring; "runs" needs an alive list of 64-column runs).
 
     Returns
     -------
@@ -73,12 +74,20 @@ def ghostweight_matmul(
 
 def _gemm(x, w_packed, idx, y, bias, activation, strategy):
     ws = None
-    if strategy != "fused" and x.dtype != torch.float32:
+    if strategy == "runs" and (x.data_ptr() % 16 or x.stride(0) % 8):
+        strategy = "auto"          # direct TMA of x needs 16-byte aligned rows
+    if strategy not in ("fused", "runs") and x.dtype != torch.float32:
         nbytes = _native.gather_gemm_workspace_bytes(x.shape[0], idx.numel(), x.dtype)
         if nbytes:
             ws = _native.gemm_workspace(x.device, nbytes)
     _native.gather_gemm(x, w_packed, idx, y, bias=bias, activation=activation,
                         strategy=strategy, workspace=ws)
+
+
+def index_runs(alive_indices: torch.Tensor, K: int) -> int:
+    """Entries of the alive list that keep it from being 64-column runs (0: strategy
+    "runs" applies). One device pass and one host synchronisation."""
+    return _native.index_runs(alive_indices, K)
 
 
 def ghost_linear(

@@ -11,7 +11,10 @@ What changes underneath:
 * dynamic mode runs the fused mask+compaction kernel K1 instead of
   dead_neuron_mask + torch.nonzero + cast (module.py:103-104); reading the
   alive count is the one host synchronisation, as nonzero's is in the reference;
-* the bias add (module.py:116-117) is fused into the GEMM epilogue.
+* the bias add (module.py:116-117) is fused into the GEMM epilogue;
+* a frozen alive list made of 64-column runs (a mask that kills whole blocks of
+  input columns) is detected once, and the GEMM then loads those blocks of x
+  directly (strategy "runs": no gather launch, no scratch).
 
 Additions beyond the reference surface: ``freeze_weight_mask()`` freezes the
 mask from the per-input-column |W| reduction (the weight-side dead-column
@@ -27,7 +30,7 @@ import torch.nn.functional as F
 
 from ghostweight_triton_b200.kernels.gather import pack_weight
 from ghostweight_triton_b200.kernels.mask import dead_neuron_mask_compact, alive_indices as _alive
-from ghostweight_triton_b200.kernels.matmul import ghost_linear
+from ghostweight_triton_b200.kernels.matmul import ghost_linear, index_runs
 
 _ACTIVATIONS = (None, "gelu", "gelu_tanh")
 
@@ -89,6 +92,8 @@ class GhostLinear(nn.Module):
         # (key, packed weight) for the frozen index list; rebuilt when the
         # weight, its dtype/device or the index list changes.
         self._packed: tuple[tuple, torch.Tensor] | None = None
+        # (key, whether the frozen list is made of 64-column runs), same key rule.
+        self._runs: tuple[tuple, bool] | None = None
 
     # ------------------------------------------------------------------ construction
     @classmethod
@@ -152,6 +157,13 @@ class GhostLinear(nn.Module):
         self._packed = (key, packed)
         return packed
 
+    def _alive_runs(self, alive: torch.Tensor) -> bool:
+        """Whether the frozen list is made of 64-column runs (checked once per list)."""
+        key = (alive.data_ptr(), alive.numel(), alive._version, alive.device)
+        if self._runs is None or self._runs[0] != key:
+            self._runs = (key, index_runs(alive, self.in_features) == 0)
+        return self._runs[1]
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         """x : [..., in_features] -> [..., out_features] (arbitrary batch dims)."""
         orig_shape = x.shape
@@ -178,11 +190,15 @@ class GhostLinear(nn.Module):
             if self.activation is not None:
                 out = F.gelu(out, approximate="tanh" if self.activation == "gelu_tanh" else "none")
         else:
+            strategy = "auto"
             if frozen:
                 w_packed = self._weight_packed(alive, x_2d.dtype)
+                if x_2d.dtype != torch.float32 and self._alive_runs(alive):
+                    strategy = "runs"
             else:
                 w_packed = pack_weight(self.weight.detach(), alive, dtype=x_2d.dtype)
-            out = ghost_linear(x_2d, w_packed, alive, bias=bias, activation=self.activation)
+            out = ghost_linear(x_2d, w_packed, alive, bias=bias, activation=self.activation,
+                               strategy=strategy)
         return out.reshape(*orig_shape[:-1], self.out_features)
 
     # ------------------------------------------------------------------ masks
@@ -206,6 +222,7 @@ class GhostLinear(nn.Module):
         self._frozen_indices = idx.to(torch.int64)
         self._mask_frozen = True
         self._packed = None
+        self._runs = None
         k_alive = int(self._frozen_indices.numel())
         self._last_sparsity = float(1.0 - k_alive / self.in_features)
 
@@ -214,6 +231,7 @@ class GhostLinear(nn.Module):
         self._mask_frozen = False
         self._frozen_indices = None
         self._packed = None
+        self._runs = None
 
     @property
     def current_sparsity(self) -> float:

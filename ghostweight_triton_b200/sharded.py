@@ -9,7 +9,8 @@ W[r*n : (r+1)*n, :] and bias slice; x is replicated. Each rank:
      every rank uses the same alive list -- exactly the list the full weight
      would give (a column is dead in W iff it is dead in every shard);
   2. packs its shard's alive columns once (K2);
-  3. runs the tcgen05 gather-GEMM on its rows (K3) -> y_r [M, n];
+  3. runs the tcgen05 gather-GEMM on its rows (K3) -> y_r [M, n] (strategy
+     "runs", no gather, when the alive list is made of 64-column runs);
   4. if the next op needs full rows, either all-gathers y (NCCL over NVLink)
      into [world, M, n] and re-lays it out to [M, N] (gather_output=True), or
      (gather_output="peers") lets the GEMM itself store every finished tile
@@ -30,7 +31,7 @@ import torch.nn as nn
 
 from ghostweight_triton_b200.kernels.gather import pack_weight
 from ghostweight_triton_b200.kernels.mask import dead_neuron_mask_compact
-from ghostweight_triton_b200.kernels.matmul import ghost_linear
+from ghostweight_triton_b200.kernels.matmul import ghost_linear, index_runs
 
 
 def shard_rows(n_total: int, world: int, rank: int) -> tuple[int, int, int]:
@@ -166,6 +167,7 @@ class ColumnParallelGhostLinear(nn.Module):
         self.bias = nn.Parameter(torch.zeros(self.n_local, **factory)) if bias else None
         self.alive: torch.Tensor | None = None
         self.w_packed: torch.Tensor | None = None
+        self.strategy = "auto"       # "runs" when the alive list is 64-column runs
         self._peer_out: PeerOutputs | None = None
         self._peer_step = 0
         self._flag: torch.Tensor | None = None
@@ -217,13 +219,18 @@ class ColumnParallelGhostLinear(nn.Module):
             union_mask(mask, self.group)
             self.alive = torch.nonzero(mask, as_tuple=False).squeeze(-1).to(torch.int64)
             self.w_packed = pack_weight(self.weight.detach(), self.alive)
+            # Same list on every rank, so every rank picks the same strategy.
+            runs = (self.weight.dtype != torch.float32 and self.alive.numel() > 0
+                    and index_runs(self.alive, self.in_features) == 0)
+            self.strategy = "runs" if runs else "auto"
 
     # ------------------------------------------------------------------ forward
     def local_forward(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """This rank's output columns y[:, start:start+n_local] (padded rows included)."""
         assert self.alive is not None, "call freeze_weight_mask() first"
         x2 = x.reshape(-1, self.in_features)
-        return ghost_linear(x2, self.w_packed, self.alive, bias=self.bias, out=out)
+        return ghost_linear(x2, self.w_packed, self.alive, bias=self.bias, out=out,
+                            strategy=self.strategy)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         lead = x.shape[:-1]
@@ -263,9 +270,11 @@ class ColumnParallelGhostLinear(nn.Module):
         n_real = self.row_stop - self.row_start
         esize = full.element_size()
         bias = self.bias[:n_real] if self.bias is not None else None
+        runs = self.strategy == "runs" and x2.data_ptr() % 16 == 0 and x2.stride(0) % 8 == 0
         _native.gather_gemm_peers(x2, self.w_packed[:n_real], self.alive,
                                   full[:, self.row_start:self.row_stop],
-                                  po.peer_addresses(i, self.row_start * esize), bias=bias)
+                                  po.peer_addresses(i, self.row_start * esize), bias=bias,
+                                  strategy="runs" if runs else "pregather")
         # Orders every rank's readers of `full` after every rank's GEMM (and its
         # peer stores): each rank joins only after its own GEMM on this stream.
         dist.all_reduce(self._flag, group=self.group)

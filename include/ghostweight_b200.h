@@ -194,15 +194,25 @@ GW_API int gw_gather_rows_t(const void* src, int dtype, int64_t rows, int64_t co
  *   GW_GEMM_OVERLAP   one cooperative kernel: its gather warps write x[:, idx] to
  *                     the workspace k-block by k-block while the TMA/MMA warps
  *                     already consume the finished k-blocks.
+ *   GW_GEMM_RUNS      for alive lists made of 64-column runs (a mask that kills
+ *                     whole 64- or 128-column blocks): idx[64 j + r] = idx[64 j] + r
+ *                     for r < 64, idx[64 j] a multiple of 8, n_alive a multiple
+ *                     of 64. One GEMM launch, no gather and no workspace: each
+ *                     64-column block of x is loaded straight from x by TMA.
+ *                     Requires x 16-byte aligned and ldx % 8 == 0; n_alive % 64
+ *                     != 0 returns GW_ERR_UNSUPPORTED. The kernel checks only the
+ *                     run starts (a bad one sets GW_DERR_BAD_INDEX and yields a
+ *                     wrong result); gw_index_runs checks the whole list once.
  * workspace: device scratch of at least gw_gather_gemm_workspace_bytes(M, n_alive,
- * dtype) bytes, 16-byte aligned (may be NULL for GW_GEMM_FUSED / fp32). Its
- * contents on entry do not matter; concurrent calls must not share it.
+ * dtype) bytes, 16-byte aligned (may be NULL for GW_GEMM_FUSED, GW_GEMM_RUNS and
+ * fp32). Its contents on entry do not matter; concurrent calls must not share it.
  */
 typedef enum {
   GW_GEMM_AUTO = 0,
   GW_GEMM_FUSED = 1,
   GW_GEMM_PREGATHER = 2,
-  GW_GEMM_OVERLAP = 3
+  GW_GEMM_OVERLAP = 3,
+  GW_GEMM_RUNS = 4
 } gw_gemm_strategy;
 
 GW_API size_t gw_gather_gemm_workspace_bytes(int64_t M, int64_t n_alive, int dtype);
@@ -222,8 +232,11 @@ GW_API int gw_gather_gemm(const void* x, int dtype, int64_t M, int64_t K, int64_
  * every peer's full output. Where the shape runs on the CTA-pair kernel the
  * peer stores are issued from its epilogue tile by tile (over NVLink, plain
  * stores, no multicast); otherwise a copy kernel follows the GEMM.
- * Requires y, ldy and every peer_y 16-byte aligned, at most GW_MAX_PEERS peers,
- * and a workspace as for gw_gather_gemm. No synchronisation between GPUs is
+ * Requires y, ldy and every peer_y 16-byte aligned and at most GW_MAX_PEERS
+ * peers. strategy: GW_GEMM_AUTO or GW_GEMM_PREGATHER (gather into the
+ * workspace, sized as for gw_gather_gemm, then the GEMM) or GW_GEMM_RUNS (no
+ * gather, no workspace; the conditions of gw_gather_gemm apply); others return
+ * GW_ERR_UNSUPPORTED. No synchronisation between GPUs is
  * done here: the caller orders the peers' readers after every rank's call
  * (e.g. a collective on each stream) and must not let a peer overwrite a
  * buffer that is still being read.
@@ -234,8 +247,8 @@ GW_API int gw_gather_gemm(const void* x, int dtype, int64_t M, int64_t K, int64_
 GW_API int gw_gather_gemm_peers(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
                                 const void* w_packed, int64_t N, int64_t ldw, const int64_t* idx,
                                 int64_t n_alive, const void* bias, int epilogue, void* y,
-                                int64_t ldy, void* const* peer_y, int n_peers, void* workspace,
-                                size_t workspace_bytes, void* stream);
+                                int64_t ldy, void* const* peer_y, int n_peers, int strategy,
+                                void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Dense GEMM over an already-compacted activation (the two-step path of
@@ -255,6 +268,17 @@ GW_API int gw_packed_gemm(const void* a, int dtype, int64_t M, int64_t K, int64_
  */
 GW_API int gw_validate_indices(const int64_t* idx, int64_t n, int64_t K, int32_t* bad_count,
                                void* stream);
+
+/*
+ * Counts the entries of idx[0, n) that break the structure GW_GEMM_RUNS needs
+ * into *bad_count (int32, device, overwritten): idx[64 j + r] == idx[64 j] + r,
+ * idx[64 j] % 8 == 0, every entry in [0, K), n a multiple of 64 (entries of a
+ * trailing partial run count). 0 means gw_gather_gemm may use GW_GEMM_RUNS with
+ * this list. No counterpart in the reference, whose gather-GEMM always reads
+ * x through idx (kernels/matmul.py:55-63).
+ */
+GW_API int gw_index_runs(const int64_t* idx, int64_t n, int64_t K, int32_t* bad_count,
+                         void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -97,6 +97,25 @@ def gather_rows(w: np.ndarray, idx: np.ndarray) -> np.ndarray:
     return np.ascontiguousarray(w[np.asarray(idx, dtype=np.int64), :])
 
 
+def index_runs(idx: np.ndarray, K: int) -> int:
+    """Entries of idx that keep x[:, idx] from being whole 64-column slices of x.
+
+    The reference always gathers x through idx (ghostweight_triton/kernels/
+    matmul.py:55-63); when every 64-entry group idx[64 j : 64 j + 64] is the
+    consecutive run idx[64 j] + (0 .. 63) starting at a multiple of 8, that
+    gather is a set of contiguous slices. Counted as bad: entries outside
+    [0, K), entries off their run, every entry of a run with a misaligned start,
+    and entries of a trailing partial run.
+    """
+    idx = np.asarray(idx, dtype=np.int64)
+    n = len(idx)
+    t = np.arange(n)
+    r = t & 63
+    start = idx[t - r] if n else idx
+    bad = (idx < 0) | (idx >= K) | (idx != start + r) | ((start & 7) != 0) | (t - r + 64 > n)
+    return int(bad.sum())
+
+
 def pack_weight(weight_nk: np.ndarray, idx: np.ndarray, pad_to: int | None = None) -> np.ndarray:
     """[N, pad_to] with weight[:, idx] in the first len(idx) columns, zeros after."""
     idx = np.asarray(idx, dtype=np.int64)

@@ -67,6 +67,23 @@ def _rank_main(rank: int, world: int, port: int, q) -> None:
                 errs.append((yp.float() - refp).abs().max().item())
             layer.close()
             results[str(dtype)] = (max(err, *errs), layer.k_alive, tuple(y.shape))
+        # Whole 128-column blocks dead: the alive list is 64-column runs, so both
+        # output paths run the GEMM on x in place (strategy "runs", no gather).
+        M, N, K = 1024, 2048, 2048
+        g = torch.Generator(device=device).manual_seed(11)
+        w = (torch.randn(N, K, device=device, generator=g) / K ** 0.5).half()
+        b = torch.randn(N, device=device, generator=g).half()
+        x = torch.randn(M, K, device=device, generator=g).half()
+        blocks = torch.randperm(K // 128, device=device, generator=g)[: K // 256]
+        w[:, (blocks[:, None] * 128 + torch.arange(128, device=device)).reshape(-1)] = 0
+        layer = ColumnParallelGhostLinear.from_full_weight(w, b, device=device)
+        ref = F.linear(x.float(), w.float(), b.float())
+        errs = [(layer(x).float() - ref).abs().max().item()]
+        layer.gather_output = "peers"
+        for _ in range(2):
+            errs.append((layer(x).float() - ref).abs().max().item())
+        layer.close()
+        results["runs"] = (max(errs), layer.k_alive, layer.strategy)
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, results, None))
@@ -100,8 +117,10 @@ def test_column_parallel_two_ranks_nccl():
                 p.terminate()
                 p.join(timeout=10)
     for rank, res in got.items():
-        for dt, (err, k_alive, shape) in res.items():
+        for dt in ("torch.bfloat16", "torch.float16"):
+            err = res[dt][0]
             tol = 0.1 if "bfloat16" in dt else 0.02
             assert err < tol, f"rank {rank} {dt}: max err {err}"
         assert res["torch.bfloat16"][1] == 1024 and res["torch.bfloat16"][2] == (2048, 4096)
         assert res["torch.float16"][1] == 384 and res["torch.float16"][2] == (300, 1000)
+        assert res["runs"][0] < 0.02 and res["runs"][1:] == (1024, "runs"), res["runs"]

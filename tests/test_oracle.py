@@ -133,3 +133,25 @@ def test_ghost_linear_equals_dense_when_dead_columns_zero():
     y_sparse = O.ghost_linear(x, w, alive, dtype="f32")
     y_dense = O.ghost_linear(x, w, np.arange(64), dtype="f32")
     assert np.allclose(y_sparse, y_dense, atol=1e-5, rtol=1e-5)
+
+
+def test_index_runs_structure():
+    """Lists of whole 64-column runs (starts multiple of 8) have no violations, and
+    their gather equals the concatenated 64-column slices of x."""
+    K = 1024
+    for block in (64, 128):
+        idx = alive_from_dead(K, dead_columns(K, 0.5, 3, "block", block))
+        assert O.index_runs(idx, K) == 0
+        x = rand_matrix((5, K), 4, "f16")
+        slices = np.concatenate([x[:, s:s + 64] for s in idx[::64]], axis=1)
+        assert np.array_equal(O.gather_columns(x, idx), slices)
+    assert O.index_runs(np.arange(8, 8 + 128), K) == 0           # start 8: 16-byte aligned
+    assert O.index_runs(np.arange(4, 4 + 64), K) == 64            # start 4: whole run misaligned
+    assert O.index_runs(np.arange(0, 96), K) == 32                # trailing partial run
+    broken = np.arange(0, 128)
+    broken[70] = 500
+    assert O.index_runs(broken, K) == 1
+    assert O.index_runs(np.arange(K - 32, K + 32), K) == 32       # 32 entries past K
+    assert O.index_runs(np.array([], dtype=np.int64), K) == 0
+    random_idx = alive_from_dead(K, dead_columns(K, 0.5, 3, "random"))
+    assert O.index_runs(random_idx, K) > 0
