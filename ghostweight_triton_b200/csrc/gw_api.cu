@@ -2,6 +2,7 @@
 // Declarations (with the reference interface each entry point replaces) are in
 // include/ghostweight_b200.h.
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -271,10 +272,20 @@ size_t gemm_ws_header(int64_t n_alive) {
 }  // namespace
 
 namespace {
+// GW_DECODE_GEMM=0 turns the decode-shaped kernel off (A/B measurements).
+bool decode_gemm_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("GW_DECODE_GEMM");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 // Dense-A GEMM y = act(a @ w^T + bias) on the kernel that suits the shape:
 // the CTA-pair kernel when there are enough 256 x 256 tiles for every SM
-// pair, cluster split-K when the output has too few tiles to occupy half of
-// the SMs (decode-sized M), else the single-CTA persistent kernel.
+// pair; for at most 32 rows the decode kernel (features on the MMA's M side,
+// split-K in a cluster); cluster split-K when the output has too few tiles to
+// occupy half of the SMs; else the single-CTA persistent kernel.
 // With peers, the output is also written into each peer buffer: by the pair
 // kernel's epilogue, tile by tile, or by a copy kernel after the other kernels.
 // With a_cols, a is x [M, a_width] and K the count of alive columns, which form
@@ -288,8 +299,13 @@ cudaError_t launch_dense_gemm(const void* a, int dtype, int64_t M, int64_t K, in
     return gw::launch_gemm_tc2(a, dtype, M, K, lda, w, N, ldw, bias, epilogue, y, ldy,
                                d->err_word, d->sm_count, s, peers, n_peers, a_cols, a_width);
   cudaError_t e;
-  const gw::SplitKPlan sk = gw::plan_splitk(M, N, K, d->sm_count);
-  if (sk.split >= 2)
+  const gw::DecodePlan dp = decode_gemm_enabled() ? gw::plan_decode(M, N, K, d->sm_count)
+                                                  : gw::DecodePlan{};
+  const gw::SplitKPlan sk = dp.split >= 2 ? gw::SplitKPlan{} : gw::plan_splitk(M, N, K, d->sm_count);
+  if (dp.split >= 2)
+    e = gw::launch_gemm_decode(dp, a, dtype, M, K, lda, w, N, ldw, bias, epilogue, y, ldy,
+                               d->err_word, s, a_cols, a_width);
+  else if (sk.split >= 2)
     e = gw::launch_gemm_splitk(sk, a, dtype, M, K, lda, w, N, ldw, bias, epilogue, y, ldy,
                                d->err_word, s, a_cols, a_width);
   else
@@ -364,7 +380,7 @@ int gw_gather_gemm(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
   void* xg = static_cast<char*>(workspace) + gemm_ws_header(n_alive);
   if (strat == GW_GEMM_PREGATHER) {
     e = gw::launch_gather_columns(x, dtype, M, ldx, K, idx, n_alive, xg, ldp, n_alive,
-                                  d->err_word, d->sm_count, s);
+                                  d->err_word, d->sm_count, s, true);
     if (e != cudaSuccess) return cuda_fail(e);
     e = launch_dense_gemm(xg, dtype, M, n_alive, ldp, w_packed, N, ldw, bias, epilogue, y, ldy,
                           d, s);
@@ -421,7 +437,7 @@ int gw_gather_gemm_peers(const void* x, int dtype, int64_t M, int64_t K, int64_t
   const int64_t ldp = gemm_ld_pad(n_alive);
   void* xg = static_cast<char*>(workspace) + gemm_ws_header(n_alive);
   e = gw::launch_gather_columns(x, dtype, M, ldx, K, idx, n_alive, xg, ldp, n_alive,
-                                d->err_word, d->sm_count, s);
+                                d->err_word, d->sm_count, s, true);
   if (e != cudaSuccess) return cuda_fail(e);
   e = launch_dense_gemm(xg, dtype, M, n_alive, ldp, w_packed, N, ldw, bias, epilogue, y, ldy, d, s,
                         peer_y, n_peers);

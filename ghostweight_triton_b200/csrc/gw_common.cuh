@@ -126,6 +126,12 @@ __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
 
+// Brings a 2-D tile of the tensor into L2 (no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const void* tmap, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];"
+               :: "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y) : "memory");
+}
+
 // 2-D tile load global -> shared, completion signalled on `bar` as tx bytes.
 // x is the innermost (contiguous) coordinate in elements; callers keep
 // x * sizeof(elem) a multiple of 16 bytes.
@@ -269,6 +275,18 @@ __device__ __forceinline__ void tc_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[3
       : "memory");
 }
 
+// Each lane reads 16 consecutive 32-bit TMEM columns of its own lane (row).
+__device__ __forceinline__ void tc_ld_32x32b_x16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
 // Shared-memory matrix descriptor for a K-major operand tile stored in the
 // 128-byte-swizzled canonical layout: rows of 128 B (64 16-bit elements),
 // 16-byte chunk c of row r stored at chunk position c ^ (r % 8), groups of 8
@@ -313,6 +331,40 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
                ::: "memory");
+}
+// The two halves of cluster_sync, for barriers whose wait can come much later
+// than the arrive (every thread of the CTA executes each, in order).
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrive without ordering this thread's earlier memory operations (a release
+// arrive waits for them, remote stores included).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+
+// Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from
+// this CTA's shared memory into another CTA's (cluster-window address of the
+// destination and of its mbarrier), counted as transaction bytes on that
+// mbarrier. The source must stay untouched until the data has landed.
+__device__ __forceinline__ void bulk_copy_to_cta(uint32_t cluster_dst, uint32_t src, uint32_t bytes,
+                                                 uint32_t cluster_bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      :: "r"(cluster_dst), "r"(src), "r"(bytes), "r"(cluster_bar) : "memory");
+}
+
+// 16-byte store into another CTA's shared memory (cluster-window addresses of
+// the destination and of its mbarrier), counted as 16 transaction bytes on
+// that mbarrier when it lands.
+__device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, float a, float b, float c,
+                                            float d, uint32_t cluster_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"
+      :: "r"(cluster_addr), "f"(a), "f"(b), "f"(c), "f"(d), "r"(cluster_bar) : "memory");
 }
 
 // Arrive on an mbarrier of another CTA of the cluster (cluster-window address).

@@ -31,13 +31,16 @@ template <typename raw>
 __global__ void __launch_bounds__(kGThreads)
 gather_columns_kernel(const raw* __restrict__ src, int64_t rows, int64_t ld_src, int64_t cols_src,
                       const int64_t* __restrict__ idx, int64_t n_idx, raw* __restrict__ dst,
-                      int64_t ld_dst, int64_t pad_to, unsigned int* err) {
+                      int64_t ld_dst, int64_t pad_to, unsigned int* err, int early_dependents) {
   // Launched as a programmatic dependent of the previous kernel of the stream
-  // (which may have produced src or idx): wait for it to complete. Then let a
-  // dependent kernel (the GEMM that consumes dst) start its prologue early;
-  // it still waits for this grid to finish before reading dst.
+  // (which may have produced src or idx): wait for it to complete. When dst is
+  // the x' of the GEMM launched next (early_dependents), let that GEMM start
+  // its prologue early; it waits for this grid to finish before reading x'.
+  // Otherwise (a packed weight, a caller's buffer) the next kernel starts
+  // only when this grid has finished: a GEMM may read its weight operand
+  // before its own wait.
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (early_dependents) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int64_t c0 = static_cast<int64_t>(blockIdx.x) * kColChunk;
@@ -187,7 +190,7 @@ inline unsigned clamp_grid(int64_t v, int64_t hi) {
 cudaError_t launch_gather_columns(const void* src, int dtype, int64_t rows, int64_t ld_src,
                                   int64_t cols_src, const int64_t* idx, int64_t n_idx, void* dst,
                                   int64_t ld_dst, int64_t pad_to, unsigned int* err,
-                                  int sm_count, cudaStream_t stream) {
+                                  int sm_count, cudaStream_t stream, bool early_dependents) {
   if (rows == 0 || pad_to == 0) return cudaSuccess;
   const int64_t col_blocks = (pad_to + kColChunk - 1) / kColChunk;
   const int64_t target = static_cast<int64_t>(sm_count > 0 ? sm_count : 148) * 8;
@@ -198,11 +201,11 @@ cudaError_t launch_gather_columns(const void* src, int dtype, int64_t rows, int6
   if (dtype == GW_DTYPE_F32) {
     return launch_pdl(gather_columns_kernel<uint32_t>, grid, dim3(kGThreads), stream,
                       static_cast<const uint32_t*>(src), rows, ld_src, cols_src, idx, n_idx,
-                      static_cast<uint32_t*>(dst), ld_dst, pad_to, err);
+                      static_cast<uint32_t*>(dst), ld_dst, pad_to, err, early_dependents ? 1 : 0);
   }
   return launch_pdl(gather_columns_kernel<uint16_t>, grid, dim3(kGThreads), stream,
                     static_cast<const uint16_t*>(src), rows, ld_src, cols_src, idx, n_idx,
-                    static_cast<uint16_t*>(dst), ld_dst, pad_to, err);
+                    static_cast<uint16_t*>(dst), ld_dst, pad_to, err, early_dependents ? 1 : 0);
 }
 
 namespace {

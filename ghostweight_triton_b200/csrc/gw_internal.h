@@ -25,10 +25,14 @@ cudaError_t launch_mask_compact(const void* x, int dtype, int64_t rows, int64_t 
                                 void* workspace, int sm_count, cudaStream_t stream);
 
 // gw_gather.cu
+// early_dependents: dst is the x' of the GEMM launched right after, which may
+// start its prologue before this grid finishes (it waits before reading x').
+// Leave it false for anything a later kernel may read before its own wait
+// (packed weights, the caller's buffers).
 cudaError_t launch_gather_columns(const void* src, int dtype, int64_t rows, int64_t ld_src,
                                   int64_t cols_src, const int64_t* idx, int64_t n_idx, void* dst,
                                   int64_t ld_dst, int64_t pad_to, unsigned int* err,
-                                  int sm_count, cudaStream_t stream);
+                                  int sm_count, cudaStream_t stream, bool early_dependents = false);
 cudaError_t launch_gather_rows(const void* src, int dtype, int64_t rows_src, int64_t cols,
                                int64_t ld_src, const int64_t* idx, int64_t n_idx, void* dst,
                                int64_t ld_dst, unsigned int* err, int sm_count,
@@ -97,6 +101,21 @@ struct SplitKPlan {
 };
 SplitKPlan plan_splitk(int64_t M, int64_t N, int64_t K, int sm_count);
 cudaError_t launch_gemm_splitk(const SplitKPlan& plan, const void* a, int dtype, int64_t M,
+                               int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,
+                               const void* bias, int epilogue, void* y, int64_t ldy,
+                               unsigned int* err, cudaStream_t stream,
+                               const int64_t* a_cols = nullptr, int64_t a_width = 0);
+
+// gw_gemm_decode.cu: at most 32 rows of A; the MMA runs over 128-feature
+// blocks of W' (M = 128) and all rows of A padded to mp (N = 16 or 32),
+// split-K over a cluster of `split` CTAs reduced in DSMEM, two CTAs per SM.
+struct DecodePlan {
+  int mp = 0;            // padded rows of A: 16 or 32
+  int split = 1;         // cluster size; 1 = no plan
+  int64_t blocks = 0;    // 128-feature blocks of W'
+};
+DecodePlan plan_decode(int64_t M, int64_t N, int64_t K, int sm_count);
+cudaError_t launch_gemm_decode(const DecodePlan& plan, const void* a, int dtype, int64_t M,
                                int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,
                                const void* bias, int epilogue, void* y, int64_t ldy,
                                unsigned int* err, cudaStream_t stream,

@@ -206,6 +206,15 @@ GW_API int gw_gather_rows_t(const void* src, int dtype, int64_t rows, int64_t co
  * workspace: device scratch of at least gw_gather_gemm_workspace_bytes(M, n_alive,
  * dtype) bytes, 16-byte aligned (may be NULL for GW_GEMM_FUSED, GW_GEMM_RUNS and
  * fp32). Its contents on entry do not matter; concurrent calls must not share it.
+ *
+ * Weights are read early: the GEMMs are launched as programmatic dependents
+ * of the previous kernel on the stream, and for M <= 64 the kernel requests
+ * its first tiles of w_packed before waiting for that kernel. w_packed must
+ * therefore not be the output of the immediately preceding GEMM call of this
+ * library on the stream (such kernels let their successor start early). Any
+ * other producer is safe: this library's packing and gather entry points, and
+ * kernels launched without programmatic completion triggers, finish before
+ * the GEMM starts.
  */
 typedef enum {
   GW_GEMM_AUTO = 0,

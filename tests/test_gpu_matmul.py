@@ -215,6 +215,27 @@ def test_chained_layers_pdl():
     torch.testing.assert_close(h, ref.half(), **tols(torch.float16))
 
 
+@pytest.mark.parametrize("M", [16, 64])
+def test_chained_decode_pack_then_runs_gemm(M):
+    """Each layer packs its weight and runs the GEMM straight after it (runs strategy: no
+    gather in between), reading the previous layer's output in place. The decode kernel
+    requests weight tiles before waiting for the previous kernel, so the pack must be
+    complete when the GEMM starts; its input must still wait for the previous GEMM."""
+    K = 4096
+    g = torch.Generator(device="cuda").manual_seed(M)
+    x = torch.randn(M, K, device="cuda", dtype=torch.float16, generator=g)
+    h, ref = x, x.float()
+    for layer in range(6):
+        w = (torch.randn(K, K, device="cuda", generator=g) / 45.0).half()
+        blocks = torch.sort(torch.randperm(K // 64, device="cuda", generator=g)[: K // 128]).values
+        idx = (blocks[:, None] * 64 + torch.arange(64, device="cuda")).reshape(-1)
+        out = torch.empty(M, K, device="cuda", dtype=torch.float16)
+        _native.gather_gemm(h, pack_weight(w, idx), idx, out, strategy="runs")
+        h = out
+        ref = (ref.half().float()[:, idx] @ w.float()[:, idx].t())
+    torch.testing.assert_close(h, ref.half(), **tols(torch.float16))
+
+
 # ----------------------------------------------------------------- cluster split-K (decode-sized M)
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
 @pytest.mark.parametrize("M,K,N,kp,bias,act", [
@@ -248,6 +269,38 @@ def test_cluster_split_k_vs_fp32(dt, M, K, N, kp, bias, act):
         ref = F.gelu(ref, approximate="tanh")
     torch.testing.assert_close(ys[0], ref.to(torch_dt), **tols(torch_dt))
     assert torch.equal(ys[0], ys[1]) and torch.equal(ys[1], ys[2])
+
+
+# ----------------------------------------------------------------- decode kernel (M <= 32)
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("M,K,N,kp,bias,act", [
+    (8, 1024, 1000, 200, True, "gelu"),         # MP 16; ragged last feature block and k-block
+    (17, 2048, 136, 1100, False, None),         # MP 32; two feature blocks, the second ragged
+    (32, 4096, 4096, 2048, True, "gelu_tanh"),  # MP 32, every padded row valid
+    (16, 3072, 768, 1536, True, None),          # six feature blocks: clusters of 16
+    (2, 8192, 3072, 8192, False, None),         # long k range per CTA
+    (48, 4096, 4096, 2048, True, None),         # 33..64 rows: cluster split-K instead
+])
+def test_decode_kernel_vs_fp32(dt, M, K, N, kp, bias, act):
+    torch_dt = DT[dt]
+    g = torch.Generator(device="cuda").manual_seed(M * 13 + kp)
+    x = torch.randn(M, K, device="cuda", dtype=torch_dt, generator=g)
+    w = (torch.randn(N, K, device="cuda", generator=g) / kp ** 0.5).to(torch_dt)
+    b = torch.randn(N, device="cuda", generator=g).to(torch_dt) if bias else None
+    idx = torch.sort(torch.randperm(K, device="cuda", generator=g)[:kp]).values
+    wp = pack_weight(w, idx)
+    ys = []
+    for _ in range(2):                          # fixed reduction order: bitwise reproducible
+        y = torch.full((M, N), float("nan"), device="cuda", dtype=torch_dt)
+        ghost_linear(x, wp, idx, bias=b, activation=act, out=y)
+        ys.append(y)
+    ref = F.linear(x.float()[:, idx], w.float()[:, idx], None if b is None else b.float())
+    if act == "gelu":
+        ref = F.gelu(ref)
+    elif act == "gelu_tanh":
+        ref = F.gelu(ref, approximate="tanh")
+    torch.testing.assert_close(ys[0], ref.to(torch_dt), **tols(torch_dt))
+    assert torch.equal(ys[0], ys[1])
 
 
 @pytest.mark.parametrize("M,N,K", [(16, 4096, 2048), (128, 4096, 1024), (7, 768, 3072), (300, 1000, 640)])

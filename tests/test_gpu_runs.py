@@ -129,9 +129,10 @@ def test_runs_falls_back_for_unaligned_x():
     torch.testing.assert_close(y, ref, **tols(torch.float16))
 
 
+@pytest.mark.parametrize("M", [384, 16])
 @pytest.mark.parametrize("pattern,expect", [("block", True), ("random", False)])
-def test_ghostlinear_frozen_picks_runs(pattern, expect):
-    K, N, M = 2048, 1536, 384
+def test_ghostlinear_frozen_picks_runs(pattern, expect, M):
+    K, N = 2048, 1536
     layer = GhostLinear(K, N, device="cuda", dtype=torch.bfloat16)
     with torch.no_grad():
         layer.weight.normal_(0, K ** -0.5)
