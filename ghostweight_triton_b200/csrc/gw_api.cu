@@ -363,6 +363,17 @@ int gw_gather_gemm(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
                           s, nullptr, 0, idx, K);
     return e == cudaSuccess ? GW_OK : cuda_fail(e);
   }
+  if ((strategy == GW_GEMM_AUTO || strategy == GW_GEMM_FUSED) && M <= 4 && decode_gemm_enabled()) {
+    // At most 4 rows (single-sequence decoding): the decode kernel gathers
+    // x[:, idx] itself, one launch instead of two. With more rows its
+    // per-element gather loads cost more than the separate gather launch.
+    const gw::DecodePlan dp = gw::plan_decode(M, N, n_alive, d->sm_count);
+    if (dp.split >= 2) {
+      e = gw::launch_gemm_decode_gather(dp, x, dtype, M, K, ldx, idx, n_alive, w_packed, N, ldw,
+                                        bias, epilogue, y, ldy, d->err_word, s);
+      return e == cudaSuccess ? GW_OK : cuda_fail(e);
+    }
+  }
   const size_t need = gw_gather_gemm_workspace_bytes(M, n_alive, dtype);
   const bool ws_ok = workspace != nullptr && workspace_bytes >= need;
   int strat = strategy;

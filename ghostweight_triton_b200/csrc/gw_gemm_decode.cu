@@ -31,7 +31,9 @@
 //
 // Roles (192 threads): warp 0 TMA producer, warp 1 TMEM allocator + MMA
 // issuer, warps 2..5 TMEM drain and send (warp w reads lane quadrant w % 4);
-// all six warps share the reduction. Every mbarrier wait is bounded
+// all six warps share the reduction. In gather mode (x and the alive list
+// instead of a compacted x'), warps 2..5 first gather x[:, idx] into the
+// stages' a tiles while TMA streams W': one launch per layer, no x' in memory. Every mbarrier wait is bounded
 // (gw_common.cuh). No TMA multicast.
 #include <cstdlib>
 #include <mutex>
@@ -85,7 +87,58 @@ struct DcParams {
   unsigned int* err;
   const int64_t* a_cols;     // alive columns in 64-column runs: a is x, k-block kb at a_cols[64 kb]
   int64_t a_width;           // columns of x (with a_cols)
+  // Gather mode (gx != null): a = x[:, gidx] is gathered into shared memory by
+  // the drain warps (idle until the main loop ends) instead of loaded by TMA.
+  const uint16_t* gx;
+  int64_t ldx;
+  int64_t x_cols;            // K of x: gathered indices outside [0, x_cols) read as zero
+  const int64_t* gidx;
+  int64_t n_alive;
 };
+
+// Gather mode: one warp fills the a tile (MP rows x 64 columns, 128-byte
+// swizzled rows) of k-block kb. Lane l takes the alive columns 64 kb + 2 l and
+// + 1 (indices loaded once) for every row, so a warp's loads of one row cover
+// 64 consecutive alive columns (a few hundred bytes of x) and its 4-byte
+// shared-memory stores one whole 128-byte row. Columns past n_alive are zero
+// (W' is zero there, and 0 * garbage could be NaN); rows past M are left as
+// they are (they reach only accumulator columns that are never stored).
+template <int MP>
+__device__ __forceinline__ void dc_gather_tile(const DcParams& p, uint32_t xs, int kb, int lane) {
+  const int64_t c0 = static_cast<int64_t>(kb) * kDcK + 2 * lane;
+  int64_t col[2];
+  bool bad = false;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    col[j] = -1;
+    if (c0 + j < p.n_alive) {
+      const int64_t c = __ldg(p.gidx + c0 + j);
+      if (c < 0 || c >= p.x_cols) bad = true;
+      else col[j] = c;
+    }
+  }
+  if (bad) raise_error(p.err, GW_DERR_BAD_INDEX);
+  const int chunk = lane >> 2;                 // 16-byte chunk of the row
+  const uint32_t within = static_cast<uint32_t>((lane & 3) * 4);
+  uint32_t v[MP];
+#pragma unroll
+  for (int r = 0; r < MP; ++r) {
+    v[r] = 0u;
+    if (r < p.M) {
+      const uint16_t* xr = p.gx + static_cast<int64_t>(r) * p.ldx;
+      const uint32_t lo = col[0] >= 0 ? static_cast<uint32_t>(__ldg(xr + col[0])) : 0u;
+      const uint32_t hi = col[1] >= 0 ? static_cast<uint32_t>(__ldg(xr + col[1])) : 0u;
+      v[r] = lo | (hi << 16);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < MP; ++r) {
+    if (r < p.M) {
+      const uint32_t addr = xs + static_cast<uint32_t>(r * 128 + ((chunk ^ (r & 7)) << 4)) + within;
+      asm volatile("st.shared.b32 [%0], %1;" :: "r"(addr), "r"(v[r]) : "memory");
+    }
+  }
+}
 
 // CTA `rank` owns features [rank * F, (rank + 1) * F) of the block, F = 128 / S.
 // Once every slot of its receive buffer has landed it sums the S slots in rank
@@ -165,7 +218,7 @@ gemm_decode_kernel(const __grid_constant__ CUtensorMap tmap_w,
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(full(s), 1);
+      mbar_init(full(s), p.gx ? 2 : 1);    // gather mode: the producer's and the gathering warp's arrivals
       mbar_init(empty(s), 1);
     }
     mbar_init(tfull, 1);
@@ -225,8 +278,10 @@ gemm_decode_kernel(const __grid_constant__ CUtensorMap tmap_w,
           mbar_arrive_expect_tx(full(s), kDcWBytes + p.x_tx_bytes);
           tma_load_2d(w_s, &tmap_w, kb * kDcK, n_blk * kDcN, full(s));
         }
-        const int ax = p.a_cols ? run_start_check(cur, p.a_width, p.err) : kb * kDcK;
-        tma_load_2d(w_s + kDcWBytes, &tmap_a, ax, 0, full(s));
+        if (!p.gx) {
+          const int ax = p.a_cols ? run_start_check(cur, p.a_width, p.err) : kb * kDcK;
+          tma_load_2d(w_s + kDcWBytes, &tmap_a, ax, 0, full(s));
+        }
       }
       if (!ok) {
         // Loads still in flight complete before the CTA exits.
@@ -263,6 +318,24 @@ gemm_decode_kernel(const __grid_constant__ CUtensorMap tmap_w,
     }
     __syncwarp();
   } else {
+    if (p.gx) {
+      // ---------------------------------------------------------- gather a
+      // Warp w fills the a tiles of stages w - 2, w + 2, ... (x and the alive
+      // list may come from the previous kernel of the stream).
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      const int nk = kb1 - kb0;
+      for (int i = warp - 2; i < nk; i += 4) {
+        const int s = i % C::kStages;
+        const uint32_t ph = (i / C::kStages) & 1u;
+        int ok = 1;
+        if (lane == 0) ok = mbar_wait(empty(s), ph ^ 1u, abort_flag, p.err) ? 1 : 0;
+        if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) break;
+        dc_gather_tile<MP>(p, sbase + s * C::kStageBytes + kDcWBytes, kb0 + i, lane);
+        fence_proxy_async_smem();        // the tile is read by the tensor core
+        __syncwarp();
+        if (lane == 0) mbar_arrive(full(s));
+      }
+    }
     // ------------------------------------------------------------ TMEM drain
     // Warp w reads TMEM lanes 32 (w % 4) .. +31 = output features of the block;
     // column m of the accumulator is row m of y.
@@ -448,14 +521,34 @@ DecodePlan plan_decode(int64_t M, int64_t N, int64_t K, int sm_count) {
   return best;
 }
 
-cudaError_t launch_gemm_decode(const DecodePlan& plan, const void* a, int dtype, int64_t M,
-                               int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,
-                               const void* bias, int epilogue, void* y, int64_t ldy,
-                               unsigned int* err, cudaStream_t stream, const int64_t* a_cols,
-                               int64_t a_width) {
-  if (plan.split < 2 || plan.split > 16 || plan.blocks <= 0 || plan.blocks > 65535 ||
-      M <= 0 || M > plan.mp)
+namespace {
+cudaError_t launch_decode_params(const DecodePlan& plan, DcParams& p, int dtype, const void* a,
+                                 int64_t lda, const void* w, int64_t ldw, int64_t K,
+                                 cudaStream_t stream) {
+  // The box of a covers only the rows that exist (rounded up to 8); the MMA
+  // reads MP rows of shared memory, and the rows past the box hold stale data
+  // that reaches only accumulator columns m >= M, which are never stored.
+  const int a_rows = static_cast<int>((p.M + 7) / 8 * 8);
+  p.x_tx_bytes = p.gx ? 0 : a_rows * kDcK * 2;
+  CUtensorMap ta, tw;
+  if (!make_tmap_kmajor(&tw, w, p.N, K, ldw, kDcK, kDcN)) return cudaErrorInvalidValue;
+  if (p.gx) {
+    ta = tw;                          // unused: a is gathered in the kernel
+  } else if (!make_tmap_kmajor(&ta, a, p.M, p.a_cols ? p.a_width : K, lda, kDcK, a_rows)) {
     return cudaErrorInvalidValue;
+  }
+  const bool bf = dtype == GW_DTYPE_BF16;
+  switch (plan.mp) {
+    case 16: return bf ? launch_dc<16, GW_DTYPE_BF16>(tw, ta, p, plan.blocks, stream)
+                       : launch_dc<16, GW_DTYPE_F16>(tw, ta, p, plan.blocks, stream);
+    case 32: return bf ? launch_dc<32, GW_DTYPE_BF16>(tw, ta, p, plan.blocks, stream)
+                       : launch_dc<32, GW_DTYPE_F16>(tw, ta, p, plan.blocks, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+DcParams decode_params(const DecodePlan& plan, int64_t M, int64_t K, int64_t N, const void* bias,
+                       int epilogue, void* y, int64_t ldy, unsigned int* err) {
   DcParams p{};
   p.M = M;
   p.N = N;
@@ -467,28 +560,42 @@ cudaError_t launch_gemm_decode(const DecodePlan& plan, const void* a, int dtype,
   p.num_kb = static_cast<int>((K + kDcK - 1) / kDcK);
   p.split = plan.split;
   p.err = err;
-  p.a_cols = a_cols;
-  p.a_width = a_width;
+  return p;
+}
+}  // namespace
+
+cudaError_t launch_gemm_decode_gather(const DecodePlan& plan, const void* x, int dtype, int64_t M,
+                                      int64_t K, int64_t ldx, const int64_t* idx, int64_t n_alive,
+                                      const void* w, int64_t N, int64_t ldw, const void* bias,
+                                      int epilogue, void* y, int64_t ldy, unsigned int* err,
+                                      cudaStream_t stream) {
+  if (plan.split < 2 || plan.split > 16 || plan.blocks <= 0 || plan.blocks > 65535 ||
+      M <= 0 || M > plan.mp || n_alive <= 0)
+    return cudaErrorInvalidValue;
+  DcParams p = decode_params(plan, M, n_alive, N, bias, epilogue, y, ldy, err);
+  if (p.num_kb < plan.split) return cudaErrorInvalidValue;
+  p.gx = static_cast<const uint16_t*>(x);
+  p.ldx = ldx;
+  p.x_cols = K;
+  p.gidx = idx;
+  p.n_alive = n_alive;
+  return launch_decode_params(plan, p, dtype, nullptr, 0, w, ldw, n_alive, stream);
+}
+
+cudaError_t launch_gemm_decode(const DecodePlan& plan, const void* a, int dtype, int64_t M,
+                               int64_t K, int64_t lda, const void* w, int64_t N, int64_t ldw,
+                               const void* bias, int epilogue, void* y, int64_t ldy,
+                               unsigned int* err, cudaStream_t stream, const int64_t* a_cols,
+                               int64_t a_width) {
+  if (plan.split < 2 || plan.split > 16 || plan.blocks <= 0 || plan.blocks > 65535 ||
+      M <= 0 || M > plan.mp)
+    return cudaErrorInvalidValue;
+  DcParams p = decode_params(plan, M, K, N, bias, epilogue, y, ldy, err);
   if (p.num_kb < plan.split) return cudaErrorInvalidValue;
   if (a_cols && (K % kDcK) != 0) return cudaErrorInvalidValue;
-  // The box of a covers only the rows that exist (rounded up to 8); the MMA
-  // reads MP rows of shared memory, and the rows past the box hold stale data
-  // that reaches only accumulator columns m >= M, which are never stored.
-  const int a_rows = static_cast<int>((M + 7) / 8 * 8);
-  p.x_tx_bytes = a_rows * kDcK * 2;
-
-  CUtensorMap ta, tw;
-  if (!make_tmap_kmajor(&ta, a, M, a_cols ? a_width : K, lda, kDcK, a_rows))
-    return cudaErrorInvalidValue;
-  if (!make_tmap_kmajor(&tw, w, N, K, ldw, kDcK, kDcN)) return cudaErrorInvalidValue;
-  const bool bf = dtype == GW_DTYPE_BF16;
-  switch (plan.mp) {
-    case 16: return bf ? launch_dc<16, GW_DTYPE_BF16>(tw, ta, p, plan.blocks, stream)
-                       : launch_dc<16, GW_DTYPE_F16>(tw, ta, p, plan.blocks, stream);
-    case 32: return bf ? launch_dc<32, GW_DTYPE_BF16>(tw, ta, p, plan.blocks, stream)
-                       : launch_dc<32, GW_DTYPE_F16>(tw, ta, p, plan.blocks, stream);
-    default: return cudaErrorInvalidValue;
-  }
+  p.a_cols = a_cols;
+  p.a_width = a_width;
+  return launch_decode_params(plan, p, dtype, a, lda, w, ldw, K, stream);
 }
 
 }  // namespace gw

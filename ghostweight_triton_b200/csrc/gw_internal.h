@@ -120,6 +120,13 @@ cudaError_t launch_gemm_decode(const DecodePlan& plan, const void* a, int dtype,
                                const void* bias, int epilogue, void* y, int64_t ldy,
                                unsigned int* err, cudaStream_t stream,
                                const int64_t* a_cols = nullptr, int64_t a_width = 0);
+// Same, with A = x[:, idx] gathered inside the kernel (x [M, K], leading
+// dimension ldx; no alignment requirement on x): one launch, no x' in memory.
+cudaError_t launch_gemm_decode_gather(const DecodePlan& plan, const void* x, int dtype, int64_t M,
+                                      int64_t K, int64_t ldx, const int64_t* idx, int64_t n_alive,
+                                      const void* w, int64_t N, int64_t ldw, const void* bias,
+                                      int epilogue, void* y, int64_t ldy, unsigned int* err,
+                                      cudaStream_t stream);
 
 // Driver entry point for cuTensorMapEncodeTiled (resolved once, no libcuda link).
 void* tensor_map_encoder();

@@ -187,8 +187,11 @@ GW_API int gw_gather_rows_t(const void* src, int dtype, int64_t rows, int64_t co
  * reference disables TF32 for fp32 (matmul.py:127-130).
  *
  * strategy (fp16/bf16 only):
- *   GW_GEMM_AUTO      GW_GEMM_PREGATHER when a large-enough workspace is given, else fused;
- *   GW_GEMM_FUSED     one kernel: producer warps gather x[:, idx] into shared memory;
+ *   GW_GEMM_AUTO      for M <= 4 the decode kernel with the gather inside (one
+ *                     launch, no workspace); otherwise GW_GEMM_PREGATHER when a
+ *                     large-enough workspace is given, else fused;
+ *   GW_GEMM_FUSED     one kernel: warps gather x[:, idx] into shared memory (for
+ *                     M <= 4 the decode kernel's gather, as with AUTO);
  *   GW_GEMM_PREGATHER two launches: x[:, idx] -> workspace (dense [M, K'_pad]),
  *                     then the GEMM with both operands loaded by TMA;
  *   GW_GEMM_OVERLAP   one cooperative kernel: its gather warps write x[:, idx] to

@@ -303,6 +303,29 @@ def test_decode_kernel_vs_fp32(dt, M, K, N, kp, bias, act):
     assert torch.equal(ys[0], ys[1])
 
 
+@pytest.mark.parametrize("strategy", ["auto", "pregather"])
+def test_decode_gather_unaligned_x_unsorted_repeats(strategy):
+    """The decode kernel's in-kernel gather (auto) reads x through any leading dimension
+    and any index order, repeats included; the two-launch path (pregather) agrees."""
+    M, K, N = 3, 1001, 700
+    g = torch.Generator(device="cuda").manual_seed(21)
+    base = torch.randn(M, K + 3, device="cuda", dtype=torch.float16, generator=g)
+    x = base[:, 1:K + 1]                        # row stride 1004, first element 2 bytes in
+    w = (torch.randn(N, K, device="cuda", generator=g) / 20).half()
+    idx = torch.randint(0, K, (517,), device="cuda", generator=g)
+    b = torch.randn(N, device="cuda", generator=g).half()
+    wp = pack_weight(w, idx)
+    y = torch.empty(M, N, device="cuda", dtype=torch.float16)
+    if strategy == "auto":
+        _native.gather_gemm(x, wp, idx, y, bias=b, activation="gelu_tanh", strategy="auto")
+    else:
+        ws = _native.gemm_workspace(x.device, _native.gather_gemm_workspace_bytes(M, idx.numel(), x.dtype))
+        _native.gather_gemm(x.contiguous(), wp, idx, y, bias=b, activation="gelu_tanh",
+                            strategy="pregather", workspace=ws)
+    ref = F.gelu(x.float()[:, idx] @ w.float()[:, idx].t() + b.float(), approximate="tanh")
+    torch.testing.assert_close(y, ref.half(), **tols(torch.float16))
+
+
 @pytest.mark.parametrize("M,N,K", [(16, 4096, 2048), (128, 4096, 1024), (7, 768, 3072), (300, 1000, 640)])
 def test_packed_gemm_decode_shapes(M, N, K):
     g = torch.Generator(device="cuda").manual_seed(N + K)
