@@ -625,6 +625,138 @@ def run_mlp_sharded(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------- decoding (small M)
+DECODE_LAYERS = 16
+
+
+def run_decode(args, world, rank, local):
+    """Decoding through a stack of 4096 x 4096 fp16 layers, a few rows at a time.
+
+    16 layers, each W [4096, 4096] ~ N(0, 1/sqrt(K)) with 50% of its input
+    columns zeroed (seeded uniform), K' = 2048, packed once (16 x 16.8 MB of
+    packed weights > 126 MB L2, so every step streams its weight from HBM).
+    Step = one layer's gather-GEMM on x [M, 4096] through the product path
+    (ghost_linear, frozen alive list): for M = 16 the gather launch and the
+    decode GEMM, for M = 1 the decode GEMM gathering x itself. The 16 layer
+    calls are captured in one CUDA graph and replayed (launch-bound sizes).
+    """
+    import torch.nn.functional as F
+
+    from ghostweight_triton_b200 import GhostLinear, _native
+    from ghostweight_triton_b200.kernels.matmul import ghost_linear
+
+    device = torch.device("cuda", torch.cuda.current_device())
+    peaks, peak_src = load_peaks()
+    K = N = 4096
+    g = torch.Generator(device=device).manual_seed(11 + rank)
+    layers = []
+    for i in range(DECODE_LAYERS):
+        dead = torch.from_numpy(dead_columns(K, 0.5, 100 + i, "random")).to(device)
+        lin = GhostLinear(K, N, bias=False, threshold=0.0, device=device, dtype=torch.float16)
+        with torch.no_grad():
+            lin.weight.normal_(0.0, K ** -0.5, generator=g)
+            lin.weight[:, dead] = 0
+        lin.freeze_weight_mask()
+        layers.append(lin)
+    kp = int(layers[0]._frozen_indices.numel())
+    packed = [lin._weight_packed(lin._frozen_indices, torch.float16) for lin in layers]
+
+    def layer_time(M: int, fn_for):
+        xs = [torch.randn(M, K, device=device, generator=g).half() for _ in range(DECODE_LAYERS)]
+        ys = [torch.empty(M, N, device=device, dtype=torch.float16) for _ in range(DECODE_LAYERS)]
+        fns = [fn_for(i, xs[i], ys[i]) for i in range(DECODE_LAYERS)]
+
+        def all_layers():
+            for f in fns:
+                f()
+        reps = max(10, min(args.steps, 50))
+        return graph_time(all_layers, reps, world) / DECODE_LAYERS, xs, ys
+
+    res = {}
+    for M in (16, 1):
+        t, xs, ys = layer_time(M, lambda i, x, y: (lambda: ghost_linear(
+            x, packed[i], layers[i]._frozen_indices, out=y)))
+        err = float((ys[0].float() - F.linear(xs[0].float(), layers[0].weight.detach().float())).abs().max().item())
+        dense_w = [lin.weight.detach() for lin in layers]
+        td, _, _ = layer_time(M, lambda i, x, y: (lambda: torch.mm(x, dense_w[i].t(), out=y)))
+        res[M] = (t, td, err)
+    # The decode GEMM alone on a pre-gathered x' (its roofline: W' from HBM).
+    xg = [torch.randn(16, kp, device=device, generator=g).half() for _ in range(DECODE_LAYERS)]
+    yg = [torch.empty(16, N, device=device, dtype=torch.float16) for _ in range(DECODE_LAYERS)]
+
+    def gemm_all():
+        for i in range(DECODE_LAYERS):
+            _native.packed_gemm(xg[i], packed[i], yg[i])
+    reps = max(10, min(args.steps, 50))
+    t_gemm = graph_time(gemm_all, reps, world) / DECODE_LAYERS
+    w_bytes = N * kp * 2
+    alg_bytes = w_bytes + 16 * kp * 2 + 16 * N * 2
+    # End to end through GhostLinear.forward: x from pinned host memory, y back.
+    hx = [torch.randn(16, K).half().pin_memory() for _ in range(DECODE_LAYERS)]
+    hy = torch.empty(16, N, dtype=torch.float16).pin_memory()
+
+    def e2e_step(i):
+        with torch.no_grad():
+            hy.copy_(layers[i % DECODE_LAYERS](hx[i % DECODE_LAYERS].to(device, non_blocking=True)),
+                     non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    te = timed(e2e_step, args.steps, world) / args.steps
+    if rank == 0:
+        t16, td16, err16 = res[16]
+        t1, td1, err1 = res[1]
+        cpu = cpu_decode_sample(kp)
+        line = {
+            "metric": "decode gather-GEMM time per layer (M=16 rows, 4096x4096 fp16, 50% dead)",
+            "value": round(t16 * 1e6, 3), "unit": "us", "n_gpus": world, "steps": reps,
+            "warmup": args.warmup, "ms_per_step": round(t16 * 1e3, 5), "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+            "data": "synthetic: x ~ N(0,1), W ~ N(0,1/sqrt(K)), 50% input columns zeroed (seeded uniform)",
+            "config": {"workload": "decode: 16 rotating 4096x4096 fp16 layers (K'=2048), M=16 rows per step",
+                       "M": 16, "N": N, "K": K, "K_alive": kp,
+                       "l2": "16 layers x 16.8 MB packed weights = 268 MB > 126 MB L2",
+                       "timing": "CUDA graph of 16 layer calls, replayed"},
+            "cublas_dense_us": round(td16 * 1e6, 3), "speedup_vs_dense": round(td16 / t16, 3),
+            "ideal_speedup": round(K / kp, 3), "max_abs_err_vs_fp32": err16,
+            "m1": {"us": round(t1 * 1e6, 3), "cublas_dense_us": round(td1 * 1e6, 3),
+                   "speedup_vs_dense": round(td1 / t1, 3), "max_abs_err_vs_fp32": err1,
+                   "path": "one launch: the decode GEMM gathers x[:, alive] itself"},
+            "roofline": {"bound": "hbm", "achieved": round(alg_bytes / t_gemm / 1e9, 1),
+                         "peak": float(peaks["hbm_gbs"]), "unit": "GB/s",
+                         "frac": round(alg_bytes / t_gemm / 1e9 / float(peaks["hbm_gbs"]), 4),
+                         "traffic": 16871424.0, "peak_source": f"{peak_src} hbm_gbs",
+                         "kernel": "gemm_decode_kernel<16> on x' (csrc/gw_gemm_decode.cu), graph replay",
+                         "us": round(t_gemm * 1e6, 3)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(te * 1e6, 3), "unit": "us", "h2d_bytes_per_step": 16 * K * 2,
+                    "d2h_bytes_per_step": 16 * N * 2, "path": "GhostLinear.forward, pinned host x and y"},
+            "gpu_launches": 2 * reps * DECODE_LAYERS,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def cpu_decode_sample(kp: int) -> dict:
+    """The oracle's restatement of the reference path for one 16-row layer call."""
+    sys.path.insert(0, str(REPO))
+    from oracle import gw_oracle as O
+
+    rng = np.random.default_rng(5)
+    K = N = 4096
+    x = rng.standard_normal((16, K)).astype(np.float16)
+    w = (rng.standard_normal((K, N)) / 64).astype(np.float16)
+    idx = np.sort(rng.permutation(K)[:kp]).astype(np.int64)
+    O.ghostweight_matmul(x, w, idx)
+    ts = []
+    for _ in range(20):
+        t0 = time.perf_counter()
+        O.ghostweight_matmul(x, w, idx)
+        ts.append(time.perf_counter() - t0)
+    return {"value": round(float(np.median(ts)) * 1e6, 1), "unit": "us", "cores": os.cpu_count(),
+            "kind": "port", "sample": "one 16-row 4096x4096 layer call (K'=2048) through "
+                                      "oracle.ghostweight_matmul, median of 20"}
+
+
 # ---------------------------------------------------------------------------- config 1: fp32 GhostLinear
 def run_fp32_linear(args, world, rank, local):
     """Single GhostLinear fp32 through the reference's default (dynamic) path.
@@ -887,7 +1019,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["gemm", "mlp-sharded", "ghostlinear-fp32", "gpt2", "distilbert"],
+    ap.add_argument("--workload", choices=["gemm", "mlp-sharded", "ghostlinear-fp32", "gpt2", "distilbert",
+                                           "decode"],
                     default="gemm")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -906,6 +1039,8 @@ def main():
             run_mlp_sharded(args, world, rank, local)
         elif args.workload == "ghostlinear-fp32":
             run_fp32_linear(args, world, rank, local)
+        elif args.workload == "decode":
+            run_decode(args, world, rank, local)
         else:
             run_model(args, world, rank, local, args.workload)
     finally:
