@@ -57,6 +57,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gw_packed_gemm": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i, _vp, _i64, _vp]),
     "gw_validate_indices": (_i, [_vp, _i64, _i64, _vp, _vp]),
     "gw_index_runs": (_i, [_vp, _i64, _i64, _vp, _vp]),
+    "gw_gather_columns_dev": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _i64, _i64, _vp]),
+    "gw_gather_rows_t_dev": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _i64, _i64, _vp]),
+    "gw_gather_gemm_dev": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _vp, _i,
+                                _vp, _i64, _vp, _sz, _vp]),
 }
 
 _lib: ctypes.CDLL | None = None
@@ -301,6 +305,56 @@ def gather_gemm(x: torch.Tensor, w_packed: torch.Tensor, idx: torch.Tensor, y: t
             torch.cuda.set_device(cur)
     if st:
         _check(st, "gw_gather_gemm")
+
+
+def gather_columns_dev(src: torch.Tensor, idx: torch.Tensor, n_dev: torch.Tensor, dst: torch.Tensor,
+                       pad_to: int) -> None:
+    """dst[r, j] = src[r, idx[j]] for j < n (n = n_dev[0] on the device, at most len(idx)); zero
+    columns [n, round_up(max(n, 1), 64)). No synchronisation."""
+    _rowmajor(src, dst)
+    assert idx.dtype == torch.int64 and n_dev.dtype == torch.int32
+    rows, cols = src.shape
+    with _on_device(src.device):
+        st = load().gw_gather_columns_dev(
+            _ptr(src), dtype_code(src.dtype), rows, cols, max(src.stride(0), cols), _ptr(idx),
+            idx.numel(), _ptr(n_dev), _ptr(dst), max(dst.stride(0), pad_to), int(pad_to),
+            _stream(src.device))
+    _check(st, "gw_gather_columns_dev")
+
+
+def gather_rows_t_dev(src: torch.Tensor, idx: torch.Tensor, n_dev: torch.Tensor, dst: torch.Tensor,
+                      pad_to: int) -> None:
+    """dst[n, j] = src[idx[j], n] for j < n_dev[0]; zero up to the next 64-column boundary."""
+    _rowmajor(src, dst)
+    assert idx.dtype == torch.int64 and n_dev.dtype == torch.int32
+    rows, cols = src.shape
+    with _on_device(src.device):
+        st = load().gw_gather_rows_t_dev(
+            _ptr(src), dtype_code(src.dtype), rows, cols, max(src.stride(0), cols), _ptr(idx),
+            idx.numel(), _ptr(n_dev), _ptr(dst), max(dst.stride(0), pad_to), int(pad_to),
+            _stream(src.device))
+    _check(st, "gw_gather_rows_t_dev")
+
+
+def gather_gemm_dev(x: torch.Tensor, w_packed: torch.Tensor, idx: torch.Tensor, n_dev: torch.Tensor,
+                    y: torch.Tensor, bias: torch.Tensor | None = None, activation: str | None = None,
+                    workspace: torch.Tensor | None = None) -> None:
+    """gather_gemm with K' = n_dev[0] read on the device (len(idx) is its upper bound)."""
+    _rowmajor(x, w_packed, y)
+    assert idx.dtype == torch.int64 and n_dev.dtype == torch.int32
+    M, K = x.shape
+    N = w_packed.shape[0]
+    n = idx.numel()
+    if workspace is None and x.dtype != torch.float32:
+        nbytes = gather_gemm_workspace_bytes(M, n, x.dtype)
+        workspace = gemm_workspace(x.device, nbytes) if nbytes else None
+    ws_ptr, ws_bytes = (None, 0) if workspace is None else (workspace.data_ptr(), workspace.numel() * workspace.element_size())
+    with _on_device(x.device):
+        st = load().gw_gather_gemm_dev(
+            _ptr(x), dtype_code(x.dtype), M, K, max(x.stride(0), K), _ptr(w_packed), N,
+            w_packed.stride(0), _ptr(idx), n, _ptr(n_dev), _ptr(bias), epilogue_code(activation),
+            _ptr(y), max(y.stride(0), N), ws_ptr, ws_bytes, _stream(x.device))
+    _check(st, "gw_gather_gemm_dev")
 
 
 def gather_gemm_peers(x: torch.Tensor, w_packed: torch.Tensor, idx: torch.Tensor, y: torch.Tensor,

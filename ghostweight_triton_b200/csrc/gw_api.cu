@@ -228,6 +228,24 @@ int gw_gather_columns(const void* src, int dtype, int64_t rows, int64_t cols, in
   return e == cudaSuccess ? GW_OK : cuda_fail(e);
 }
 
+int gw_gather_columns_dev(const void* src, int dtype, int64_t rows, int64_t cols, int64_t ld_src,
+                          const int64_t* idx, int64_t n_idx_max, const int32_t* n_idx_dev,
+                          void* dst, int64_t ld_dst, int64_t pad_to, void* stream) {
+  if (!valid_dtype(dtype)) return GW_ERR_DTYPE;
+  if (!matrix_ok(rows, cols, ld_src) || n_idx_max < 0 || n_idx_max > 0x7FFFFFFFll ||
+      pad_to < n_idx_max || !matrix_ok(rows, pad_to, ld_dst))
+    return GW_ERR_SHAPE;
+  const gw::DeviceInfo* d = nullptr;
+  int st = current_device(&d);
+  if (st != GW_OK) return st;
+  if (rows == 0 || pad_to == 0) return GW_OK;
+  if (!dst || !n_idx_dev || (n_idx_max > 0 && (!src || !idx))) return GW_ERR_NULL;
+  cudaError_t e = gw::launch_gather_columns(src, dtype, rows, ld_src, cols, idx, n_idx_max, dst,
+                                            ld_dst, pad_to, d->err_word, d->sm_count,
+                                            static_cast<cudaStream_t>(stream), false, n_idx_dev);
+  return e == cudaSuccess ? GW_OK : cuda_fail(e);
+}
+
 int gw_gather_rows(const void* src, int dtype, int64_t rows, int64_t cols, int64_t ld_src,
                    const int64_t* idx, int64_t n_idx, void* dst, int64_t ld_dst, void* stream) {
   if (!valid_dtype(dtype)) return GW_ERR_DTYPE;
@@ -270,6 +288,24 @@ size_t gemm_ws_header(int64_t n_alive) {
   return (kb * sizeof(unsigned int) + 255) / 256 * 256;
 }
 }  // namespace
+
+int gw_gather_rows_t_dev(const void* src, int dtype, int64_t rows, int64_t cols, int64_t ld_src,
+                         const int64_t* idx, int64_t n_idx_max, const int32_t* n_idx_dev,
+                         void* dst, int64_t ld_dst, int64_t pad_to, void* stream) {
+  if (!valid_dtype(dtype)) return GW_ERR_DTYPE;
+  if (!matrix_ok(rows, cols, ld_src) || n_idx_max < 0 || n_idx_max > 0x7FFFFFFFll ||
+      pad_to < n_idx_max || !matrix_ok(cols, pad_to, ld_dst))
+    return GW_ERR_SHAPE;
+  const gw::DeviceInfo* d = nullptr;
+  int st = current_device(&d);
+  if (st != GW_OK) return st;
+  if (cols == 0 || pad_to == 0) return GW_OK;
+  if (!dst || !n_idx_dev || (n_idx_max > 0 && (!src || !idx))) return GW_ERR_NULL;
+  cudaError_t e = gw::launch_gather_rows_t(src, dtype, rows, cols, ld_src, idx, n_idx_max, dst,
+                                           ld_dst, pad_to, d->err_word,
+                                           static_cast<cudaStream_t>(stream), n_idx_dev);
+  return e == cudaSuccess ? GW_OK : cuda_fail(e);
+}
 
 namespace {
 // GW_DECODE_GEMM=0 turns the decode-shaped kernel off (A/B measurements).
@@ -399,6 +435,58 @@ int gw_gather_gemm(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
     e = gw::launch_gemm_tc(2, x, dtype, M, K, ldx, w_packed, N, ldw, idx, n_alive, bias,
                            epilogue, y, ldy, d->err_word, d->sm_count, s, xg, ldp, counters);
   }
+  return e == cudaSuccess ? GW_OK : cuda_fail(e);
+}
+
+int gw_gather_gemm_dev(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
+                       const void* w_packed, int64_t N, int64_t ldw, const int64_t* idx,
+                       int64_t n_alive_max, const int32_t* n_alive_dev, const void* bias,
+                       int epilogue, void* y, int64_t ldy, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  if (!valid_dtype(dtype)) return GW_ERR_DTYPE;
+  if (!valid_epi(epilogue)) return GW_ERR_UNSUPPORTED;
+  if (!matrix_ok(M, K, ldx) || n_alive_max < 0 || n_alive_max > K ||
+      !matrix_ok(N, n_alive_max, ldw) || !matrix_ok(M, N, ldy))
+    return GW_ERR_SHAPE;
+  const gw::DeviceInfo* d = nullptr;
+  int st = current_device(&d);
+  if (st != GW_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (M == 0 || N == 0) return GW_OK;
+  if (!y) return GW_ERR_NULL;
+  cudaError_t e;
+  if (n_alive_max == 0) {
+    e = gw::launch_fill_bias(y, dtype, M, N, ldy, bias, epilogue, s);
+    return e == cudaSuccess ? GW_OK : cuda_fail(e);
+  }
+  if (!x || !w_packed || !idx || !n_alive_dev) return GW_ERR_NULL;
+  if (dtype == GW_DTYPE_F32) {
+    e = gw::launch_gemm_f32(static_cast<const float*>(x), M, K, ldx,
+                            static_cast<const float*>(w_packed), N, ldw, idx, n_alive_max,
+                            static_cast<const float*>(bias), epilogue, static_cast<float*>(y),
+                            ldy, d->err_word, s, n_alive_dev);
+    return e == cudaSuccess ? GW_OK : cuda_fail(e);
+  }
+  const int64_t ldp = gemm_ld_pad(n_alive_max);
+  if (!aligned16(w_packed) || (ldw % 8) != 0) return GW_ERR_ALIGN;
+  if (ldw < ldp) return GW_ERR_SHAPE;           // W' is zero up to the 64-column boundary
+  if (n_alive_max > 0x7FFFFFFFll - 64) return GW_ERR_SHAPE;
+  if (!workspace) return GW_ERR_NULL;
+  if (workspace_bytes < gw_gather_gemm_workspace_bytes(M, n_alive_max, dtype)) return GW_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return GW_ERR_ALIGN;
+  void* xg = static_cast<char*>(workspace) + gemm_ws_header(n_alive_max);
+  e = gw::launch_gather_columns(x, dtype, M, ldx, K, idx, n_alive_max, xg, ldp, ldp, d->err_word,
+                                d->sm_count, s, true, n_alive_dev);
+  if (e != cudaSuccess) return cuda_fail(e);
+  // The count is known only on the device: the persistent kernels, whose
+  // launch does not depend on it, read it (decode and split-K plans do).
+  if (gw::use_pair_gemm(M, N, d->sm_count))
+    e = gw::launch_gemm_tc2(xg, dtype, M, ldp, ldp, w_packed, N, ldw, bias, epilogue, y, ldy,
+                            d->err_word, d->sm_count, s, nullptr, 0, nullptr, 0, n_alive_dev);
+  else
+    e = gw::launch_gemm_tc(0, xg, dtype, M, ldp, ldp, w_packed, N, ldw, nullptr, ldp, bias,
+                           epilogue, y, ldy, d->err_word, d->sm_count, s, nullptr, 0, nullptr,
+                           nullptr, n_alive_dev);
   return e == cudaSuccess ? GW_OK : cuda_fail(e);
 }
 

@@ -56,6 +56,15 @@ __device__ __forceinline__ int run_start_check(int64_t c, int64_t width, unsigne
   return static_cast<int>(c);
 }
 
+// k-blocks of a GEMM whose alive count lives on the device (written by an
+// earlier kernel; read after griddepcontrol.wait): ceil(count / 64), at least
+// one (a zero-filled k-block when the count is 0), at most the launch's bound.
+__device__ __forceinline__ int device_num_kb(const int32_t* k_dev, int max_kb) {
+  const int n = *reinterpret_cast<const volatile int32_t*>(k_dev);
+  const int kb = (max(n, 0) + 63) / 64;
+  return min(max(kb, 1), max_kb);
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -31,7 +31,8 @@ template <typename raw>
 __global__ void __launch_bounds__(kGThreads)
 gather_columns_kernel(const raw* __restrict__ src, int64_t rows, int64_t ld_src, int64_t cols_src,
                       const int64_t* __restrict__ idx, int64_t n_idx, raw* __restrict__ dst,
-                      int64_t ld_dst, int64_t pad_to, unsigned int* err, int early_dependents) {
+                      int64_t ld_dst, int64_t pad_to, unsigned int* err, int early_dependents,
+                      const int32_t* __restrict__ n_dev) {
   // Launched as a programmatic dependent of the previous kernel of the stream
   // (which may have produced src or idx): wait for it to complete. When dst is
   // the x' of the GEMM launched next (early_dependents), let that GEMM start
@@ -44,6 +45,16 @@ gather_columns_kernel(const raw* __restrict__ src, int64_t rows, int64_t ld_src,
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int64_t c0 = static_cast<int64_t>(blockIdx.x) * kColChunk;
+  if (n_dev) {
+    // The count lives on the device (written by the mask kernel): n_idx and
+    // pad_to are upper bounds. Columns [n, round_up(max(n, 1), 64)) are zero,
+    // the ones past that are left alone (a GEMM reading this count never
+    // reaches them).
+    const int64_t n = min(static_cast<int64_t>(max(*n_dev, 0)), n_idx);
+    n_idx = n;
+    pad_to = min(pad_to, (max(n, int64_t{1}) + 63) / 64 * 64);
+    if (c0 >= pad_to) return;
+  }
 
   int64_t scol[kColsPerLane];
   bool live[kColsPerLane];
@@ -105,12 +116,21 @@ template <typename raw>
 __global__ void __launch_bounds__(kGThreads)
 gather_rows_t_kernel(const raw* __restrict__ src, int64_t rows_src, int64_t cols, int64_t ld_src,
                      const int64_t* __restrict__ idx, int64_t n_idx, raw* __restrict__ dst,
-                     int64_t ld_dst, int64_t pad_to, unsigned int* err) {
+                     int64_t ld_dst, int64_t pad_to, unsigned int* err,
+                     const int32_t* __restrict__ n_dev) {
   __shared__ raw tile[kTTile][kTTile + 1];
   const int tx = threadIdx.x & 63;   // 0..63
   const int ty = threadIdx.x >> 6;   // 0..3
   const int64_t j0 = static_cast<int64_t>(blockIdx.x) * kTTile;   // output column block (alive)
   const int64_t n0 = static_cast<int64_t>(blockIdx.y) * kTTile;   // output row block (features)
+  if (n_dev) {
+    // Count on the device: as in gather_columns_kernel (whole CTAs past the
+    // zero-filled range return before the barrier).
+    const int64_t n = min(static_cast<int64_t>(max(*n_dev, 0)), n_idx);
+    n_idx = n;
+    pad_to = min(pad_to, (max(n, int64_t{1}) + 63) / 64 * 64);
+    if (j0 >= pad_to) return;
+  }
   bool bad = false;
 #pragma unroll 4
   for (int i = 0; i < kTTile / 4; ++i) {
@@ -190,7 +210,8 @@ inline unsigned clamp_grid(int64_t v, int64_t hi) {
 cudaError_t launch_gather_columns(const void* src, int dtype, int64_t rows, int64_t ld_src,
                                   int64_t cols_src, const int64_t* idx, int64_t n_idx, void* dst,
                                   int64_t ld_dst, int64_t pad_to, unsigned int* err,
-                                  int sm_count, cudaStream_t stream, bool early_dependents) {
+                                  int sm_count, cudaStream_t stream, bool early_dependents,
+                                  const int32_t* n_dev) {
   if (rows == 0 || pad_to == 0) return cudaSuccess;
   const int64_t col_blocks = (pad_to + kColChunk - 1) / kColChunk;
   const int64_t target = static_cast<int64_t>(sm_count > 0 ? sm_count : 148) * 8;
@@ -201,11 +222,13 @@ cudaError_t launch_gather_columns(const void* src, int dtype, int64_t rows, int6
   if (dtype == GW_DTYPE_F32) {
     return launch_pdl(gather_columns_kernel<uint32_t>, grid, dim3(kGThreads), stream,
                       static_cast<const uint32_t*>(src), rows, ld_src, cols_src, idx, n_idx,
-                      static_cast<uint32_t*>(dst), ld_dst, pad_to, err, early_dependents ? 1 : 0);
+                      static_cast<uint32_t*>(dst), ld_dst, pad_to, err, early_dependents ? 1 : 0,
+                      n_dev);
   }
   return launch_pdl(gather_columns_kernel<uint16_t>, grid, dim3(kGThreads), stream,
                     static_cast<const uint16_t*>(src), rows, ld_src, cols_src, idx, n_idx,
-                    static_cast<uint16_t*>(dst), ld_dst, pad_to, err, early_dependents ? 1 : 0);
+                    static_cast<uint16_t*>(dst), ld_dst, pad_to, err, early_dependents ? 1 : 0,
+                    n_dev);
 }
 
 namespace {
@@ -283,7 +306,7 @@ cudaError_t launch_gather_rows(const void* src, int dtype, int64_t rows_src, int
 cudaError_t launch_gather_rows_t(const void* src, int dtype, int64_t rows_src, int64_t cols,
                                  int64_t ld_src, const int64_t* idx, int64_t n_idx, void* dst,
                                  int64_t ld_dst, int64_t pad_to, unsigned int* err,
-                                 cudaStream_t stream) {
+                                 cudaStream_t stream, const int32_t* n_dev) {
   if (cols == 0 || pad_to == 0) return cudaSuccess;
   const int64_t gx = (pad_to + kTTile - 1) / kTTile;
   const int64_t gy = (cols + kTTile - 1) / kTTile;
@@ -292,11 +315,11 @@ cudaError_t launch_gather_rows_t(const void* src, int dtype, int64_t rows_src, i
   if (dtype == GW_DTYPE_F32) {
     gather_rows_t_kernel<uint32_t><<<grid, kGThreads, 0, stream>>>(
         static_cast<const uint32_t*>(src), rows_src, cols, ld_src, idx, n_idx,
-        static_cast<uint32_t*>(dst), ld_dst, pad_to, err);
+        static_cast<uint32_t*>(dst), ld_dst, pad_to, err, n_dev);
   } else {
     gather_rows_t_kernel<uint16_t><<<grid, kGThreads, 0, stream>>>(
         static_cast<const uint16_t*>(src), rows_src, cols, ld_src, idx, n_idx,
-        static_cast<uint16_t*>(dst), ld_dst, pad_to, err);
+        static_cast<uint16_t*>(dst), ld_dst, pad_to, err, n_dev);
   }
   return cudaGetLastError();
 }

@@ -26,7 +26,9 @@ gemm_f32_kernel(const float* __restrict__ x, int64_t M, int64_t K, int64_t ldx,
                 const float* __restrict__ w, int64_t N, int64_t ldw,
                 const int64_t* __restrict__ idx, int64_t n_alive,
                 const float* __restrict__ bias, int epi, float* __restrict__ y, int64_t ldy,
-                unsigned int* err) {
+                unsigned int* err, const int32_t* __restrict__ n_dev) {
+  // n_dev: the alive count on the device (n_alive is then an upper bound).
+  if (n_dev) n_alive = min(n_alive, static_cast<int64_t>(max(*n_dev, 0)));
   // +4 floats per k-row: conflict-free loader stores, rows stay 16-byte aligned.
   __shared__ __align__(16) float As[2][kSBK][kSBM + 4];
   __shared__ __align__(16) float Bs[2][kSBK][kSBN + 4];
@@ -128,14 +130,14 @@ gemm_f32_kernel(const float* __restrict__ x, int64_t M, int64_t K, int64_t ldx,
 cudaError_t launch_gemm_f32(const float* x, int64_t M, int64_t K, int64_t ldx, const float* w,
                             int64_t N, int64_t ldw, const int64_t* idx, int64_t n_alive,
                             const float* bias, int epilogue, float* y, int64_t ldy,
-                            unsigned int* err, cudaStream_t stream) {
+                            unsigned int* err, cudaStream_t stream, const int32_t* n_dev) {
   if (M == 0 || N == 0) return cudaSuccess;
   const int64_t gx = (N + kSBN - 1) / kSBN;
   const int64_t gy = (M + kSBM - 1) / kSBM;
   if (gx > 0x7FFFFFFFll || gy > 65535) return cudaErrorInvalidValue;
   dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
   gemm_f32_kernel<<<grid, kSThreads, 0, stream>>>(x, M, K, ldx, w, N, ldw, idx, n_alive, bias,
-                                                  epilogue, y, ldy, err);
+                                                  epilogue, y, ldy, err, n_dev);
   return cudaGetLastError();
 }
 

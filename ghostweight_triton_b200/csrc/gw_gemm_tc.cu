@@ -104,6 +104,7 @@ struct TcParams {
   int64_t ldg;
   unsigned int* kb_ready;       // kAOverlap: per-k-block count of gathered 128-row units
   const int64_t* a_cols;        // kATma: k-block kb of A starts at x column a_cols[64 kb] (or null)
+  const int32_t* k_dev;         // kATma: K' on the device (num_kb an upper bound; see device_num_kb)
 };
 
 template <int BN, int DT, int AMODE>
@@ -167,6 +168,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
       // stream (the pregather launch): with programmatic dependent launch this
       // CTA got here early, so wait for that grid before reading it.
       if (AMODE == kATma) asm volatile("griddepcontrol.wait;" ::: "memory");
+      const int num_kb = (AMODE == kATma && p.k_dev) ? device_num_kb(p.k_dev, p.num_kb) : p.num_kb;
       uint32_t it = 0;
       int ready_kb = 0;   // kAOverlap: k-blocks of x' known to be complete
       bool ok = true;
@@ -175,11 +177,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
         const int m_blk = tile % p.m_tiles;
         const int n_blk = tile / p.m_tiles;
-        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
           const int s = it % C::kStages;
           const uint32_t ph = (it / C::kStages) & 1u;
           const int64_t cur = nxt;
-          if (a_cols) nxt = run_start_load(a_cols, kb + 1 == p.num_kb ? 0 : kb + 1);
+          if (a_cols) nxt = run_start_load(a_cols, kb + 1 == num_kb ? 0 : kb + 1);
           if (AMODE == kAOverlap && ready_kb <= kb) {
             while (ready_kb <= kb) {
               if (!wait_counter_geq(p.kb_ready + ready_kb, static_cast<uint32_t>(p.m_tiles),
@@ -214,6 +216,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f16(DT == GW_DTYPE_BF16 ? 1u : 0u, kBM, BN);
+      int num_kb = p.num_kb;
+      if (AMODE == kATma && p.k_dev) {  // K' written by an earlier kernel: read it after the wait
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        num_kb = device_num_kb(p.k_dev, p.num_kb);
+      }
       uint32_t it = 0, lt = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++lt) {
@@ -222,7 +229,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
         if (!mbar_wait(tempty(b), aph ^ 1u, abort_flag, p.err)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + b * BN;
-        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
           const int s = it % C::kStages;
           const uint32_t ph = (it / C::kStages) & 1u;
           if (!mbar_wait(full_b(s), ph, abort_flag, p.err)) { ok = false; break; }
@@ -492,7 +499,7 @@ cudaError_t launch_gemm_tc(int a_mode, const void* x, int dtype, int64_t M, int6
                            const int64_t* idx, int64_t n_alive, const void* bias, int epilogue,
                            void* y, int64_t ldy, unsigned int* err, int sm_count,
                            cudaStream_t stream, void* scratch_xg, int64_t ldg,
-                           unsigned int* kb_ready, const int64_t* a_cols) {
+                           unsigned int* kb_ready, const int64_t* a_cols, const int32_t* k_dev) {
   // Tile width 256 (measured best on B200 where there are several waves:
   // wider tiles reuse A more per byte moved), 128 for narrow N. When 256-wide
   // tiles leave SMs idle in a single wave and 192-wide ones still fit in one
@@ -539,6 +546,7 @@ cudaError_t launch_gemm_tc(int a_mode, const void* x, int dtype, int64_t M, int6
   p.ldg = ldg;
   p.kb_ready = kb_ready;
   p.a_cols = a_mode == kATma ? a_cols : nullptr;
+  p.k_dev = a_mode == kATma ? k_dev : nullptr;
   if (p.a_cols && (n_alive % kBK) != 0) return cudaErrorInvalidValue;
 
   CUtensorMap tb, ta;

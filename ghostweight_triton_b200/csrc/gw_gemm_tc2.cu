@@ -83,6 +83,8 @@ struct Tc2Params {
   // column a_cols[64 kb] (null: A is the compacted x', atom kb at 64 kb).
   const int64_t* a_cols;
   int64_t a_width;          // columns of x (with a_cols)
+  // K' on the device (num_kb is then an upper bound; see device_num_kb).
+  const int32_t* k_dev;
 };
 
 template <int DT>
@@ -145,34 +147,36 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
     // ------------------------------------------------------------ TMA producer (both CTAs)
     if (lane == 0) {
       asm volatile("griddepcontrol.wait;" ::: "memory");   // A may come from the previous kernel
+      const int num_kb = p.k_dev ? device_num_kb(p.k_dev, p.num_kb) : p.num_kb;
+      const int num_ks = (num_kb + kAtoms2 - 1) / kAtoms2;
       uint32_t it = 0;
       bool ok = true;
       // a_cols: run starts of the stage after the current one, loaded ahead.
       int64_t nxt0 = 0, nxt1 = 0;
       if (p.a_cols) {
         nxt0 = run_start_load(p.a_cols, 0);
-        if (p.num_kb > 1) nxt1 = run_start_load(p.a_cols, 1);
+        if (num_kb > 1) nxt1 = run_start_load(p.a_cols, 1);
       }
       for (int tile = pair; ok && tile < p.num_tiles; tile += num_pairs) {
         const int m_blk = tile % p.m_tiles;
         const int n_blk = tile / p.m_tiles;
         const int a_row = m_blk * kPairM + static_cast<int>(rank) * kHalfM;
         const int b_row = n_blk * kPairN + static_cast<int>(rank) * kHalfN;
-        for (int ks = 0; ks < p.num_ks; ++ks, ++it) {
+        for (int ks = 0; ks < num_ks; ++ks, ++it) {
           const int s = it % kStages2;
           const uint32_t ph = (it / kStages2) & 1u;
           const int64_t cur0 = nxt0, cur1 = nxt1;
           if (p.a_cols) {
-            const int nk = (ks + 1 == p.num_ks ? 0 : ks + 1) * kAtoms2;
+            const int nk = (ks + 1 == num_ks ? 0 : ks + 1) * kAtoms2;
             nxt0 = run_start_load(p.a_cols, nk);
-            if (nk + 1 < p.num_kb) nxt1 = run_start_load(p.a_cols, nk + 1);
+            if (nk + 1 < num_kb) nxt1 = run_start_load(p.a_cols, nk + 1);
           }
           if (!mbar_wait_cluster(empty(s), ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
           const uint32_t a_s = sbase + s * kStageBytes2;
           const uint32_t b_s = a_s + kABytes2;
           const uint32_t leader_full = mapa_shared(full(s), 0);
           // The last stage of an odd number of atoms carries one atom.
-          const int atoms = min(kAtoms2, p.num_kb - ks * kAtoms2);
+          const int atoms = min(kAtoms2, num_kb - ks * kAtoms2);
           if (rank == 0) mbar_arrive_expect_tx(full(s), 2u * 2u * atoms * kAtomBytes2);
           for (int a = 0; a < atoms; ++a) {
             const int kx = (ks * kAtoms2 + a) * kBK2;
@@ -192,6 +196,12 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
     // ------------------------------------------------------------ MMA issuer (leader only)
     if (lane == 0 && rank == 0) {
       constexpr uint32_t idesc = idesc_f16(DT == GW_DTYPE_BF16 ? 1u : 0u, kPairM, kPairN);
+      int num_kb = p.num_kb;
+      if (p.k_dev) {                   // K' written by an earlier kernel: read it after the wait
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        num_kb = device_num_kb(p.k_dev, p.num_kb);
+      }
+      const int num_ks = (num_kb + kAtoms2 - 1) / kAtoms2;
       uint32_t it = 0, lt = 0;
       bool ok = true;
       for (int tile = pair; ok && tile < p.num_tiles; tile += num_pairs, ++lt) {
@@ -200,7 +210,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
         if (!mbar_wait_cluster(tempty(b), aph ^ 1u, abort_flag, p.err)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + b * kPairN;
-        for (int ks = 0; ks < p.num_ks; ++ks, ++it) {
+        for (int ks = 0; ks < num_ks; ++ks, ++it) {
           const int s = it % kStages2;
           const uint32_t ph = (it / kStages2) & 1u;
           if (!mbar_wait_cluster(full(s), ph, abort_flag, p.err)) { ok = false; break; }
@@ -208,7 +218,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
           const uint32_t a_s = sbase + s * kStageBytes2;
           const uint64_t a_desc = smem_desc_kmajor_sw128(a_s);
           const uint64_t b_desc = smem_desc_kmajor_sw128(a_s + kABytes2);
-          const bool two = ks * kAtoms2 + 1 < p.num_kb;
+          const bool two = ks * kAtoms2 + 1 < num_kb;
           // Atom a starts kAtomBytes2 further on (>> 4 in the descriptor); each
           // 16-wide k step advances 32 bytes inside the swizzle atom.
 #pragma unroll
@@ -384,7 +394,7 @@ cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int6
                             const void* w, int64_t N, int64_t ldw, const void* bias, int epilogue,
                             void* y, int64_t ldy, unsigned int* err, int sm_count,
                             cudaStream_t stream, void* const* peers, int n_peers,
-                            const int64_t* a_cols, int64_t a_width) {
+                            const int64_t* a_cols, int64_t a_width, const int32_t* k_dev) {
   const int64_t m_tiles = (M + kPairM - 1) / kPairM;
   const int64_t n_tiles = (N + kPairN - 1) / kPairN;
   const int64_t num_tiles = m_tiles * n_tiles;
@@ -409,6 +419,7 @@ cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int6
 
   p.a_cols = a_cols;
   p.a_width = a_width;
+  p.k_dev = k_dev;
   CUtensorMap ta, tb, ty;
   // With a_cols, A is x [M, a_width] (K = the alive count, a multiple of 64).
   if (a_cols && (K % kBK2) != 0) return cudaErrorInvalidValue;

@@ -29,10 +29,13 @@ cudaError_t launch_mask_compact(const void* x, int dtype, int64_t rows, int64_t 
 // start its prologue before this grid finishes (it waits before reading x').
 // Leave it false for anything a later kernel may read before its own wait
 // (packed weights, the caller's buffers).
+// n_dev (optional): the index count on the device; n_idx and pad_to are then
+// upper bounds, and columns [n, round_up(max(n, 1), 64)) are written as zero.
 cudaError_t launch_gather_columns(const void* src, int dtype, int64_t rows, int64_t ld_src,
                                   int64_t cols_src, const int64_t* idx, int64_t n_idx, void* dst,
                                   int64_t ld_dst, int64_t pad_to, unsigned int* err,
-                                  int sm_count, cudaStream_t stream, bool early_dependents = false);
+                                  int sm_count, cudaStream_t stream, bool early_dependents = false,
+                                  const int32_t* n_dev = nullptr);
 cudaError_t launch_gather_rows(const void* src, int dtype, int64_t rows_src, int64_t cols,
                                int64_t ld_src, const int64_t* idx, int64_t n_idx, void* dst,
                                int64_t ld_dst, unsigned int* err, int sm_count,
@@ -40,7 +43,7 @@ cudaError_t launch_gather_rows(const void* src, int dtype, int64_t rows_src, int
 cudaError_t launch_gather_rows_t(const void* src, int dtype, int64_t rows_src, int64_t cols,
                                  int64_t ld_src, const int64_t* idx, int64_t n_idx, void* dst,
                                  int64_t ld_dst, int64_t pad_to, unsigned int* err,
-                                 cudaStream_t stream);
+                                 cudaStream_t stream, const int32_t* n_dev = nullptr);
 cudaError_t launch_fill_bias(void* y, int dtype, int64_t M, int64_t N, int64_t ldy,
                              const void* bias, int epilogue, cudaStream_t stream);
 // Copies y [rows, cols] (leading dimension ld, 16-bit, 16-byte aligned rows)
@@ -59,13 +62,15 @@ cudaError_t launch_index_runs(const int64_t* idx, int64_t n, int64_t K, int32_t*
 //              (per-k-block counters kb_ready[num_kb], zeroed by the launcher),
 //              then TMA streams it; cooperative launch
 // a_mode 0 with a_cols: as launch_gemm_tc2's a_cols (A = x [M, K], k-block kb
-// loaded from column a_cols[64 kb], n_alive a multiple of 64).
+// loaded from column a_cols[64 kb], n_alive a multiple of 64). a_mode 0 with
+// k_dev: as launch_gemm_tc2's k_dev (n_alive an upper bound).
 cudaError_t launch_gemm_tc(int a_mode, const void* x, int dtype, int64_t M, int64_t K,
                            int64_t ldx, const void* w, int64_t N, int64_t ldw,
                            const int64_t* idx, int64_t n_alive, const void* bias, int epilogue,
                            void* y, int64_t ldy, unsigned int* err, int sm_count,
                            cudaStream_t stream, void* scratch_xg = nullptr, int64_t ldg = 0,
-                           unsigned int* kb_ready = nullptr, const int64_t* a_cols = nullptr);
+                           unsigned int* kb_ready = nullptr, const int64_t* a_cols = nullptr,
+                           const int32_t* k_dev = nullptr);
 
 // gw_gemm_tc2.cu: CTA-pair (cta_group::2) tcgen05 GEMM, dense A [M, K] by TMA,
 // 256 x 256 tiles per pair. Chained to the previous kernel by programmatic
@@ -77,19 +82,24 @@ constexpr int kMaxPeers = 7;
 // With a_cols (alive columns in 64-column runs, each starting at a multiple of
 // 8; K = their count, a multiple of 64), A is x [M, a_width] itself and k atom
 // kb is loaded from column a_cols[64 kb]: no compacted copy of x is needed.
+// With k_dev, K is an upper bound and the kernel reads K' from the device (A
+// and W' must be zero in columns [K', round_up(max(K', 1), 64))).
 cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int64_t lda,
                             const void* w, int64_t N, int64_t ldw, const void* bias, int epilogue,
                             void* y, int64_t ldy, unsigned int* err, int sm_count,
                             cudaStream_t stream, void* const* peers = nullptr, int n_peers = 0,
-                            const int64_t* a_cols = nullptr, int64_t a_width = 0);
+                            const int64_t* a_cols = nullptr, int64_t a_width = 0,
+                            const int32_t* k_dev = nullptr);
 // Whether the CTA-pair kernel serves a dense-A GEMM of this shape.
 bool use_pair_gemm(int64_t M, int64_t N, int sm_count);
 
 // gw_gemm_simt.cu: exact-fp32 gather-GEMM.
+// n_dev (optional): the alive count on the device, n_alive its upper bound.
 cudaError_t launch_gemm_f32(const float* x, int64_t M, int64_t K, int64_t ldx, const float* w,
                             int64_t N, int64_t ldw, const int64_t* idx, int64_t n_alive,
                             const float* bias, int epilogue, float* y, int64_t ldy,
-                            unsigned int* err, cudaStream_t stream);
+                            unsigned int* err, cudaStream_t stream,
+                            const int32_t* n_dev = nullptr);
 
 // gw_gemm_splitk.cu: split-K over a cluster of `split` CTAs reduced in DSMEM,
 // for dense-A GEMMs whose output has too few tiles to occupy the SMs.

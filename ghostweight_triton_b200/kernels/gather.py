@@ -91,6 +91,33 @@ def pack_weight(weight: torch.Tensor, alive_indices: torch.Tensor,
     return buf[:, :k_alive]
 
 
+def pack_weight_dev(weight: torch.Tensor, alive_buffer: torch.Tensor, alive_count: torch.Tensor,
+                    dtype: torch.dtype | None = None) -> torch.Tensor:
+    """:func:`pack_weight` for an alive list whose length lives on the device.
+
+    ``alive_buffer`` holds the alive columns in its first ``alive_count[0]``
+    entries (int32 device scalar, as the mask kernel writes it); nothing is
+    synchronised. Returns the whole [N, round_up(K, 64)] buffer: columns
+    [K', round_up(max(K', 1), 64)) are zero, the ones past that are not
+    written (the device-count GEMM never reads them).
+    """
+    assert weight.ndim == 2 and weight.is_cuda
+    if dtype is not None and weight.dtype != dtype:
+        weight = weight.to(dtype)
+    idx = alive_buffer.contiguous().to(device=weight.device, dtype=torch.int64)
+    N, K = weight.shape
+    ld = max(_round_up(idx.numel(), PACK_ALIGN), PACK_ALIGN)
+    buf = torch.empty((N, ld), dtype=weight.dtype, device=weight.device)
+    if N > 0:
+        if weight.stride(1) == 1:
+            _native.gather_columns_dev(weight, idx, alive_count, buf, pad_to=ld)
+        elif weight.stride(0) == 1:
+            _native.gather_rows_t_dev(weight.t(), idx, alive_count, buf, pad_to=ld)
+        else:
+            _native.gather_columns_dev(weight.contiguous(), idx, alive_count, buf, pad_to=ld)
+    return buf
+
+
 def pack_weight_kn(weights_kn: torch.Tensor, alive_indices: torch.Tensor,
                    dtype: torch.dtype | None = None) -> torch.Tensor:
     """Same as :func:`pack_weight` for a reference-orientation weight [K, N]."""

@@ -110,6 +110,31 @@ def ghost_linear(
     return y
 
 
+def ghost_linear_dev(
+    x: torch.Tensor,
+    w_packed: torch.Tensor,
+    alive_buffer: torch.Tensor,
+    alive_count: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    activation: str | None = None,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """ghost_linear with K' = alive_count[0] read on the device (no host synchronisation).
+
+    w_packed is the [N, round_up(K, 64)] buffer of :func:`pack_weight_dev` for the
+    same alive list; alive_buffer's first K' entries are the alive columns.
+    """
+    assert x.ndim == 2 and x.is_cuda
+    x = x.contiguous()
+    M = x.shape[0]
+    N = w_packed.shape[0]
+    y = out if out is not None else torch.empty((M, N), dtype=x.dtype, device=x.device)
+    if M and N:
+        _native.gather_gemm_dev(x, w_packed, alive_buffer, alive_count, y, bias=bias,
+                                activation=activation)
+    return y
+
+
 def packed_linear(
     a: torch.Tensor,
     w_packed: torch.Tensor,

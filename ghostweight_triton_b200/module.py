@@ -9,8 +9,15 @@ What changes underneath:
   (frozen mode) or packed per call from the alive list (dynamic mode, reading
   only N*K' elements instead of transposing all N*K);
 * dynamic mode runs the fused mask+compaction kernel K1 instead of
-  dead_neuron_mask + torch.nonzero + cast (module.py:103-104); reading the
-  alive count is the one host synchronisation, as nonzero's is in the reference;
+  dead_neuron_mask + torch.nonzero + cast (module.py:103-104), and by default
+  (``sync_free = True``) never reads the alive count on the host: the packing,
+  the gather and the GEMM read it on the device, so a dynamic-mask forward
+  queues without a host synchronisation and can be captured in a CUDA graph.
+  The dense-fallback choice (module.py:111-112) then uses the previous
+  forward's sparsity once its count has reached the host (read without
+  waiting), and ``current_sparsity`` reads the count when it is accessed.
+  With ``sync_free = False`` the forward reads the count first, as the
+  reference does;
 * the bias add (module.py:116-117) is fused into the GEMM epilogue;
 * a frozen alive list made of 64-column runs (a mask that kills whole blocks of
   input columns) is detected once, and the GEMM then loads those blocks of x
@@ -28,11 +35,54 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from ghostweight_triton_b200.kernels.gather import pack_weight
+from ghostweight_triton_b200.kernels.gather import pack_weight, pack_weight_dev
 from ghostweight_triton_b200.kernels.mask import dead_neuron_mask_compact, alive_indices as _alive
-from ghostweight_triton_b200.kernels.matmul import ghost_linear, index_runs
+from ghostweight_triton_b200.kernels.matmul import ghost_linear, ghost_linear_dev, index_runs
 
 _ACTIVATIONS = (None, "gelu", "gelu_tanh")
+
+
+class _CountReadback:
+    """The last dynamic forward's alive count on its way to the host.
+
+    An asynchronous copy into pinned memory and an event: ``ready()`` returns
+    the count only if it has already landed (never waits), ``value()`` waits
+    for it. Not copied by deepcopy (events and pinned buffers stay per module).
+    """
+
+    def __init__(self):
+        self.host: torch.Tensor | None = None
+        self.event: torch.cuda.Event | None = None
+        self.dev: torch.Tensor | None = None
+
+    def __deepcopy__(self, memo):
+        return _CountReadback()
+
+    def record(self, count: torch.Tensor) -> None:
+        self.dev = count
+        if torch.cuda.is_current_stream_capturing():
+            self.event = None          # replays rewrite `count`; value() reads it then
+            return
+        if self.host is None:
+            self.host = torch.empty(1, dtype=torch.int32).pin_memory()
+            self.event = torch.cuda.Event()
+        elif self.event is None:
+            self.event = torch.cuda.Event()
+        self.host.copy_(count, non_blocking=True)
+        self.event.record()
+
+    def ready(self) -> int | None:
+        if self.event is None or self.host is None or torch.cuda.is_current_stream_capturing():
+            return None
+        return int(self.host[0]) if self.event.query() else None
+
+    def value(self) -> int | None:
+        if self.dev is None:
+            return None
+        if self.event is not None:
+            self.event.synchronize()
+            return int(self.host[0])
+        return int(self.dev.item())
 
 
 class GhostLinear(nn.Module):
@@ -94,6 +144,10 @@ class GhostLinear(nn.Module):
         self._packed: tuple[tuple, torch.Tensor] | None = None
         # (key, whether the frozen list is made of 64-column runs), same key rule.
         self._runs: tuple[tuple, bool] | None = None
+        # Dynamic mode without host synchronisation (see the module docstring).
+        self.sync_free: bool = True
+        self._readback = _CountReadback()
+        self._sparsity_pending = False
 
     # ------------------------------------------------------------------ construction
     @classmethod
@@ -171,6 +225,8 @@ class GhostLinear(nn.Module):
         assert x_2d.is_cuda, "GhostLinear runs on CUDA (sm_100) only"
 
         frozen = self._mask_frozen and self._frozen_indices is not None
+        if not frozen and self.sync_free:
+            return self._forward_sync_free(x_2d).reshape(*orig_shape[:-1], self.out_features)
         if frozen:
             alive = self._frozen_indices
             k_alive = alive.shape[0]
@@ -201,6 +257,25 @@ class GhostLinear(nn.Module):
                                strategy=strategy)
         return out.reshape(*orig_shape[:-1], self.out_features)
 
+    def _forward_sync_free(self, x_2d: torch.Tensor) -> torch.Tensor:
+        """Dynamic-mask forward whose alive count never leaves the device."""
+        _, buf, count = dead_neuron_mask_compact(x_2d, self.threshold, want_mask=False)
+        bias = self.bias
+        if bias is not None and bias.dtype != x_2d.dtype:
+            bias = bias.to(x_2d.dtype)
+        prev = self._readback.ready()           # the previous forward's count, if it has landed
+        dense = prev is not None and 1.0 - prev / self.in_features < self.min_sparsity_to_activate
+        if dense:
+            out = F.linear(x_2d, self.weight.to(x_2d.dtype), bias)
+            if self.activation is not None:
+                out = F.gelu(out, approximate="tanh" if self.activation == "gelu_tanh" else "none")
+        else:
+            w_packed = pack_weight_dev(self.weight.detach(), buf, count, dtype=x_2d.dtype)
+            out = ghost_linear_dev(x_2d, w_packed, buf, count, bias=bias, activation=self.activation)
+        self._readback.record(count)
+        self._sparsity_pending = True
+        return out
+
     # ------------------------------------------------------------------ masks
     def freeze_mask(self, calibration_input: torch.Tensor) -> None:
         """Freeze the dead-neuron mask from calibration activations; later calls reuse it."""
@@ -223,6 +298,7 @@ class GhostLinear(nn.Module):
         self._mask_frozen = True
         self._packed = None
         self._runs = None
+        self._sparsity_pending = False
         k_alive = int(self._frozen_indices.numel())
         self._last_sparsity = float(1.0 - k_alive / self.in_features)
 
@@ -235,7 +311,15 @@ class GhostLinear(nn.Module):
 
     @property
     def current_sparsity(self) -> float:
-        """Sparsity of the frozen mask, or of the most recent forward pass."""
+        """Sparsity of the frozen mask, or of the most recent forward pass (a
+        synchronisation-free forward's count is read here, on access)."""
+        if self._sparsity_pending and not (self._mask_frozen and self._frozen_indices is not None):
+            n = self._readback.value()
+            if n is not None:
+                self._last_sparsity = float(1.0 - n / self.in_features)
+            # A count recorded during CUDA-graph capture is rewritten by every
+            # replay: keep reading it.
+            self._sparsity_pending = self._readback.event is None and self._readback.dev is not None
         return self._last_sparsity
 
     @property

@@ -263,6 +263,41 @@ GW_API int gw_gather_gemm_peers(const void* x, int dtype, int64_t M, int64_t K, 
                                 void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Device-count variants, for the dynamic (per-forward) activation mask without
+ * a host synchronisation: the number of valid entries of idx is read from
+ * device memory (n_*_dev, an int32, e.g. gw_mask_compact's alive_count), so the
+ * mask, the packing, the gather and the GEMM are queued back to back. The
+ * reference reads that count on the host (torch.nonzero at
+ * ghostweight_triton/module.py:103-108). n_*_max is an upper bound (K); buffers
+ * are sized for it.
+ *
+ * gw_gather_columns_dev / gw_gather_rows_t_dev: as gw_gather_columns /
+ * gw_gather_rows_t with n = *n_idx_dev (clamped to [0, n_idx_max]); columns
+ * [n, round_up(max(n, 1), 64)) of dst are written as zero, columns past that
+ * (up to pad_to) are left as they are.
+ *
+ * gw_gather_gemm_dev: gw_gather_gemm (fp16/bf16: gather into the workspace,
+ * sized by gw_gather_gemm_workspace_bytes(M, n_alive_max, dtype), then the
+ * tcgen05 GEMM; fp32: the exact-fp32 kernel) with K' = *n_alive_dev. For
+ * fp16/bf16, w_packed must be zero in columns [K', round_up(max(K', 1), 64))
+ * (as gw_gather_columns_dev / gw_gather_rows_t_dev with pad_to = ldw leave it)
+ * and ldw >= round_up(n_alive_max, 64). K' = 0 gives act(bias).
+ */
+GW_API int gw_gather_columns_dev(const void* src, int dtype, int64_t rows, int64_t cols,
+                                 int64_t ld_src, const int64_t* idx, int64_t n_idx_max,
+                                 const int32_t* n_idx_dev, void* dst, int64_t ld_dst,
+                                 int64_t pad_to, void* stream);
+GW_API int gw_gather_rows_t_dev(const void* src, int dtype, int64_t rows, int64_t cols,
+                                int64_t ld_src, const int64_t* idx, int64_t n_idx_max,
+                                const int32_t* n_idx_dev, void* dst, int64_t ld_dst,
+                                int64_t pad_to, void* stream);
+GW_API int gw_gather_gemm_dev(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
+                              const void* w_packed, int64_t N, int64_t ldw, const int64_t* idx,
+                              int64_t n_alive_max, const int32_t* n_alive_dev, const void* bias,
+                              int epilogue, void* y, int64_t ldy, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
+/*
  * Dense GEMM over an already-compacted activation (the two-step path of
  * gather.py:1-14: gather_compact followed by a matmul):
  *   y[m, n] = act( sum_{j < K} a[m, j] * w_packed[n, j] + bias[n] )
