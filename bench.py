@@ -931,6 +931,19 @@ def run_model(args, world, rank, local, which: str):
     # The same forwards captured in CUDA graphs: no per-call host overhead.
     t_graph = graph_time(lambda: fwd(ghost, 0), steps, world)
     t_graph_dense = graph_time(lambda: fwd(dense, 0), steps, world)
+    # Extension: MLP blocks fused (the first projection computes only the second's
+    # alive features, written compacted; no gather before the second).
+    from ghostweight_triton_b200.fuse import fuse_mlp_chains
+
+    fused = copy.deepcopy(ghost)
+    n_fused = len(fuse_mlp_chains(fused))
+    for i in range(args.warmup):
+        fwd(fused, i)
+    t_graph_fused = graph_time(lambda: fwd(fused, 0), steps, world)
+    with torch.no_grad():
+        c = fwd(fused, 0).float()
+        rel_fused = float(((c - fwd(dense, 0).float()).norm() / fwd(dense, 0).float().norm()).item())
+    del fused
     # Linear-layer FLOPs of one forward over the alive columns (what the kernels compute).
     useful = 0.0
     for mod in ghost.modules():
@@ -963,6 +976,11 @@ def run_model(args, world, rank, local, which: str):
                            "dense_tokens_per_s": round(world * tokens / t_graph_dense, 1),
                            "speedup_vs_dense": round(t_graph_dense / t_graph, 3),
                            "ms_per_step": round(t_graph * 1e3, 4)},
+            "mlp_chains_fused": {"blocks": n_fused, "tokens_per_s": round(world * tokens / t_graph_fused, 1),
+                                 "speedup_vs_dense": round(t_graph_dense / t_graph_fused, 3),
+                                 "ms_per_step": round(t_graph_fused * 1e3, 4),
+                                 "rel_err_vs_dense_model": rel_fused,
+                                 "timing": "CUDA graph, as cuda_graph"},
             "linear_useful_tflops": round(useful / t / 1e12, 2),
             "rel_err_vs_dense_model": rel,
             "cpu_baseline": cpu,

@@ -1,10 +1,11 @@
-// K3, decode-sized variant: split-K over a thread-block cluster, reduced in
+// K3, small-M variant: split-K over a thread-block cluster, reduced in
 // distributed shared memory.
 //
 //   y[m, n] = act( sum_j a[m, j] * w[n, j] + bias[n] )      a = x' (dense, compacted)
 //
-// When the output has too few 128 x BN tiles to occupy the SMs (M of a few
-// rows to a few hundred: decoding, small batches), the persistent kernels
+// When the output has too few 128 x BN tiles to occupy the SMs (a few dozen
+// to a few hundred rows: small batches; at most 32 rows usually go to the
+// decode kernel, gw_gemm_decode.cu), the persistent kernels
 // leave most SMs idle and each busy SM streams a long k range alone. Here a
 // cluster of S CTAs (S = 2, 4 or 8) shares one output tile: CTA s of the
 // cluster accumulates k-blocks [s * nkb / S, (s + 1) * nkb / S) on its tensor

@@ -125,3 +125,24 @@ def test_sync_free_dense_fallback_follows_previous_forward():
     gl.sync_free = False
     torch.testing.assert_close(gl(sparse_x), F.linear(sparse_x, lin.weight, lin.bias), atol=1e-4, rtol=1e-4)
     assert gl.current_sparsity == pytest.approx(0.75)
+
+
+def test_device_count_edge_shapes():
+    """M = 0 / N = 0 return at once; an upper bound of 0 gives act(bias); counts above the
+    bound are clamped to it."""
+    x = torch.randn(5, 64, device="cuda", dtype=torch.float16)
+    w = torch.randn(24, 64, device="cuda", dtype=torch.float16) / 8
+    b = torch.randn(24, device="cuda", dtype=torch.float16)
+    cnt = torch.tensor([9], dtype=torch.int32, device="cuda")
+    empty = torch.empty(0, dtype=torch.int64, device="cuda")
+    wp = torch.zeros(24, 64, device="cuda", dtype=torch.float16)
+    y = torch.empty(5, 24, device="cuda", dtype=torch.float16)
+    _native.gather_gemm_dev(x, wp, empty, cnt, y, bias=b)
+    torch.testing.assert_close(y, b.expand(5, 24))
+    _native.gather_gemm_dev(x[:0], wp, empty, cnt, y[:0], bias=b)
+    idx = torch.arange(0, 64, 2, device="cuda")                     # 32 entries, count says 40
+    cnt.fill_(40)
+    wp = pack_weight_dev(w, idx, cnt)
+    _native.gather_gemm_dev(x, wp, idx, cnt, y, bias=b)
+    ref = (x.float()[:, idx] @ w.float()[:, idx].t() + b.float()).half()
+    torch.testing.assert_close(y, ref, **tols(torch.float16))

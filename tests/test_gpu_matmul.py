@@ -236,7 +236,7 @@ def test_chained_decode_pack_then_runs_gemm(M):
     torch.testing.assert_close(h, ref.half(), **tols(torch.float16))
 
 
-# ----------------------------------------------------------------- cluster split-K (decode-sized M)
+# ----------------------------------------------------------------- small M (cluster split-K and decode kernels)
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
 @pytest.mark.parametrize("M,K,N,kp,bias,act", [
     (16, 4096, 4096, 2048, False, None),        # 16 tiles of 256, clusters of 8
