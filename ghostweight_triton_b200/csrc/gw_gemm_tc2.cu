@@ -34,31 +34,41 @@ namespace gw {
 namespace {
 
 constexpr int kHalfM = 128;            // rows per CTA
-constexpr int kHalfN = 128;            // B rows per CTA
 constexpr int kPairM = 2 * kHalfM;
-constexpr int kPairN = 2 * kHalfN;
 constexpr int kBK2 = 64;
 constexpr int kThreads2 = 320;         // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
-constexpr int kEpiWarps2 = 8;          // two per TMEM lane quadrant, 128 columns each
+constexpr int kEpiWarps2 = 8;          // two per TMEM lane quadrant
 // A stage holds two 64-wide k atoms (128 of K) of A and of B: the single MMA
 // thread waits once and issues 8 MMAs per stage, so its per-stage overhead
 // (barrier wait, fence, commit) is paid once per 1024 tensor cycles.
 constexpr int kAtoms2 = 2;
 constexpr int kStageK2 = kAtoms2 * kBK2;
 constexpr int kStages2 = 3;
-constexpr int kAtomBytes2 = kHalfM * kBK2 * 2;       // one 128-row x 64-col atom (16 KB)
-static_assert(kHalfM == kHalfN, "A and B atoms have the same size");
-constexpr int kABytes2 = kAtoms2 * kAtomBytes2;
-constexpr int kBBytes2 = kAtoms2 * kAtomBytes2;
-constexpr int kStageBytes2 = kABytes2 + kBBytes2;
-constexpr int kTmemCols2 = 2 * kPairN;  // two 256-column accumulators
+constexpr int kAAtomBytes2 = kHalfM * kBK2 * 2;      // one 128-row x 64-col atom of A (16 KB)
+constexpr int kABytes2 = kAtoms2 * kAAtomBytes2;
+constexpr int kTmemCols2 = 512;         // two accumulators of up to 256 columns
 // Epilogue staging for TMA stores: per epilogue warp one 32-row x 64-column
 // 16-bit tile (4 KB, 128-byte swizzled rows).
 constexpr int kEpiCols = 64;
 constexpr int kEpiTileBytes = 32 * kEpiCols * 2;
 constexpr int kEpiBytes = kEpiWarps2 * kEpiTileBytes;
-constexpr int kSmemBytes2 = 1024 + kStages2 * kStageBytes2 + kEpiBytes + 256;
-static_assert(kSmemBytes2 <= 232448, "shared memory budget per CTA");
+
+// Pair tile width BN (256 or 192): each CTA holds BN / 2 rows of W' per atom;
+// the two epilogue warps of a lane quadrant take columns [0, 128) and
+// [128, BN) of the tile.
+template <int BN>
+struct Tc2Cfg {
+  static_assert(BN == 256 || BN == 192, "pair tile width");
+  static constexpr int kHalfN = BN / 2;
+  static constexpr int kBAtomBytes = kHalfN * kBK2 * 2;         // 16 or 12 KB
+  static constexpr int kBBytes = kAtoms2 * kBAtomBytes;
+  static constexpr int kStageBytes = kABytes2 + kBBytes;
+  static constexpr int kSmemBytes = 1024 + kStages2 * kStageBytes + kEpiBytes + 256;
+  static_assert(kBAtomBytes % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
+  static_assert(kSmemBytes <= 232448, "shared memory budget per CTA");
+  static constexpr int kCols0 = 128;                            // first warp of a quadrant
+  static constexpr int kCols1 = BN - 128;                       // second warp
+};
 
 struct Tc2Params {
   int64_t M;
@@ -87,11 +97,14 @@ struct Tc2Params {
   const int32_t* k_dev;
 };
 
-template <int DT>
+template <int BN, int DT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
 gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
                 const __grid_constant__ CUtensorMap tmap_a,
                 const __grid_constant__ CUtensorMap tmap_y, const Tc2Params p) {
+  using C = Tc2Cfg<BN>;
+  constexpr int kHalfN = C::kHalfN;
+  constexpr int kStageBytes2 = C::kStageBytes;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_s = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_s & 1023u)) & 1023u);
@@ -161,7 +174,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
         const int m_blk = tile % p.m_tiles;
         const int n_blk = tile / p.m_tiles;
         const int a_row = m_blk * kPairM + static_cast<int>(rank) * kHalfM;
-        const int b_row = n_blk * kPairN + static_cast<int>(rank) * kHalfN;
+        const int b_row = n_blk * BN + static_cast<int>(rank) * kHalfN;
         for (int ks = 0; ks < num_ks; ++ks, ++it) {
           const int s = it % kStages2;
           const uint32_t ph = (it / kStages2) & 1u;
@@ -177,12 +190,13 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
           const uint32_t leader_full = mapa_shared(full(s), 0);
           // The last stage of an odd number of atoms carries one atom.
           const int atoms = min(kAtoms2, num_kb - ks * kAtoms2);
-          if (rank == 0) mbar_arrive_expect_tx(full(s), 2u * 2u * atoms * kAtomBytes2);
+          if (rank == 0)
+            mbar_arrive_expect_tx(full(s), 2u * atoms * (kAAtomBytes2 + C::kBAtomBytes));
           for (int a = 0; a < atoms; ++a) {
             const int kx = (ks * kAtoms2 + a) * kBK2;
             const int ax = p.a_cols ? run_start_check(a == 0 ? cur0 : cur1, p.a_width, p.err) : kx;
-            tma_load_2d_pair(a_s + a * kAtomBytes2, &tmap_a, ax, a_row, leader_full);
-            tma_load_2d_pair(b_s + a * kAtomBytes2, &tmap_b, kx, b_row, leader_full);
+            tma_load_2d_pair(a_s + a * kAAtomBytes2, &tmap_a, ax, a_row, leader_full);
+            tma_load_2d_pair(b_s + a * C::kBAtomBytes, &tmap_b, kx, b_row, leader_full);
           }
         }
       }
@@ -195,7 +209,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader only)
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc = idesc_f16(DT == GW_DTYPE_BF16 ? 1u : 0u, kPairM, kPairN);
+      constexpr uint32_t idesc = idesc_f16(DT == GW_DTYPE_BF16 ? 1u : 0u, kPairM, BN);
       int num_kb = p.num_kb;
       if (p.k_dev) {                   // K' written by an earlier kernel: read it after the wait
         asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -209,7 +223,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
         const uint32_t aph = (lt >> 1) & 1u;
         if (!mbar_wait_cluster(tempty(b), aph ^ 1u, abort_flag, p.err)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + b * kPairN;
+        const uint32_t d_tmem = tmem_base + b * BN;
         for (int ks = 0; ks < num_ks; ++ks, ++it) {
           const int s = it % kStages2;
           const uint32_t ph = (it / kStages2) & 1u;
@@ -219,8 +233,8 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
           const uint64_t a_desc = smem_desc_kmajor_sw128(a_s);
           const uint64_t b_desc = smem_desc_kmajor_sw128(a_s + kABytes2);
           const bool two = ks * kAtoms2 + 1 < num_kb;
-          // Atom a starts kAtomBytes2 further on (>> 4 in the descriptor); each
-          // 16-wide k step advances 32 bytes inside the swizzle atom.
+          // Atom 1 of A and of B starts one atom further on (>> 4 in the
+          // descriptor); each 16-wide k step advances 32 bytes inside the atom.
 #pragma unroll
           for (int k = 0; k < kBK2 / 16; ++k)
             tc_mma_f16_pair(d_tmem, a_desc + 2u * k, b_desc + 2u * k, idesc,
@@ -228,8 +242,8 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
           if (two) {
 #pragma unroll
             for (int k = 0; k < kBK2 / 16; ++k)
-              tc_mma_f16_pair(d_tmem, a_desc + (kAtomBytes2 >> 4) + 2u * k,
-                              b_desc + (kAtomBytes2 >> 4) + 2u * k, idesc, 1u);
+              tc_mma_f16_pair(d_tmem, a_desc + (kAAtomBytes2 >> 4) + 2u * k,
+                              b_desc + (C::kBAtomBytes >> 4) + 2u * k, idesc, 1u);
           }
           tc_commit_pair_mc(empty(s), 0x3);
         }
@@ -243,8 +257,8 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
     // Eight warps: warp w drains TMEM lanes 32 (w % 4) .. +31 (rows of this
-    // CTA's half tile) and columns [128 h, 128 h + 128), h = (w - 2) / 4, in
-    // 64-column chunks. Each 32-column tcgen05 load is issued before the
+    // CTA's half tile) and columns [0, 128) (h = (w - 2) / 4 = 0) or
+    // [128, BN) (h = 1) of the tile, in 64-column chunks. Each 32-column tcgen05 load is issued before the
     // previous one is converted; bias + activation + one packed rounding per
     // pair of values; then a TMA store from the warp's 128-byte-swizzled
     // staging tile, or direct stores when y's rows are not 16-byte aligned.
@@ -265,18 +279,18 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
       const int64_t row = warp_row0 + lane;
       const bool row_ok = row < p.M;
       uint16_t* yrow = p.y + (row_ok ? row * p.ldy : 0);
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * kPairN + half * (kPairN / 2);
-      const int64_t n_warp = static_cast<int64_t>(n_blk) * kPairN + half * (kPairN / 2);
-      constexpr int kSteps = (kPairN / 2) / 32;        // 32-column loads per warp and tile
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * BN + half * C::kCols0;
+      const int64_t n_warp = static_cast<int64_t>(n_blk) * BN + half * C::kCols0;
+      const int steps = (half ? C::kCols1 : C::kCols0) / 32;   // 32-column loads (even)
       uint32_t acc[32];
       tc_ld_32x32b_x32(t_row, acc);
 #pragma unroll 1
-      for (int st = 0; st < kSteps; ++st) {
+      for (int st = 0; st < steps; ++st) {
         tc_wait_ld();
         float f[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(acc[j]);
-        if (st + 1 < kSteps) tc_ld_32x32b_x32(t_row + (st + 1) * 32, acc);
+        if (st + 1 < steps) tc_ld_32x32b_x32(t_row + (st + 1) * 32, acc);
         const int c = st >> 1;                          // 64-column chunk
         const int h = st & 1;                           // its 32-column half
         const int64_t n_chunk = n_warp + c * kEpiCols;
@@ -376,6 +390,22 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
 
 }  // namespace
 
+namespace {
+// Pair tile width for an M x N output: the one that minimises rounds x the
+// bytes a CTA loads per k atom (A 16 KB + B BN/2 rows), rounds = waves of
+// pair tiles over the SM pairs. Ties keep 256.
+int pair_tile_width(int64_t M, int64_t N, int sm_count) {
+  const int64_t pairs = std::max<int64_t>(1, (sm_count > 0 ? sm_count : 148) / 2);
+  const int64_t m_tiles = (M + kPairM - 1) / kPairM;
+  auto cost = [&](int bn) {
+    const int64_t tiles = m_tiles * ((N + bn - 1) / bn);
+    const int64_t rounds = (tiles + pairs - 1) / pairs;
+    return rounds * (16 + bn / 16);
+  };
+  return cost(192) < cost(256) ? 192 : 256;
+}
+}  // namespace
+
 bool use_pair_gemm(int64_t M, int64_t N, int sm_count) {
   // GW_GEMM_PAIR=0 forces the single-CTA kernel, =1 the pair kernel (tuning, tests).
   static const int forced = [] {
@@ -384,10 +414,55 @@ bool use_pair_gemm(int64_t M, int64_t N, int sm_count) {
   }();
   if (forced == 0) return false;
   if (forced == 1) return true;
-  // Pairs pay off once there are at least as many 256 x 256 tiles as SM pairs;
-  // below that, 128-row tiles spread the work over more SMs (measured).
-  const int64_t pair_tiles = ((M + kPairM - 1) / kPairM) * ((N + kPairN - 1) / kPairN);
-  return M > kHalfM && N > kHalfN && pair_tiles >= (sm_count > 0 ? sm_count : 148) / 2;
+  if (M <= kHalfM || N <= 128) return false;
+  // Pairs pay off once their tiles occupy most SM pairs; below that, 128-row
+  // tiles spread the work over more SMs (measured).
+  const int64_t pairs = (sm_count > 0 ? sm_count : 148) / 2;
+  const int bn = pair_tile_width(M, N, sm_count);
+  const int64_t pair_tiles = ((M + kPairM - 1) / kPairM) * ((N + bn - 1) / bn);
+  return bn == 256 ? pair_tiles >= pairs : 10 * pair_tiles >= 8 * pairs;
+}
+
+template <int BN>
+cudaError_t launch_tc2_bn(int dtype, Tc2Params& p, const void* a, int64_t M, int64_t K,
+                          int64_t lda, const void* w, int64_t N, int64_t ldw, void* y,
+                          int64_t ldy, int sm_count, cudaStream_t stream) {
+  using C = Tc2Cfg<BN>;
+  const int64_t m_tiles = (M + kPairM - 1) / kPairM;
+  const int64_t n_tiles = (N + BN - 1) / BN;
+  const int64_t num_tiles = m_tiles * n_tiles;
+  if (num_tiles > 0x7FFFFFFFll) return cudaErrorInvalidValue;
+  p.m_tiles = static_cast<int>(m_tiles);
+  p.n_tiles = static_cast<int>(n_tiles);
+  p.num_tiles = static_cast<int>(num_tiles);
+  CUtensorMap ta, tb, ty;
+  // With a_cols, A is x [M, a_width] (K = the alive count, a multiple of 64).
+  if (p.a_cols && (K % kBK2) != 0) return cudaErrorInvalidValue;
+  if (!make_tmap_kmajor(&ta, a, M, p.a_cols ? p.a_width : K, lda, kBK2, kHalfM))
+    return cudaErrorInvalidValue;
+  if (!make_tmap_kmajor(&tb, w, N, K, ldw, kBK2, C::kHalfN)) return cudaErrorInvalidValue;
+  // TMA-store epilogue when y's rows are 16-byte aligned (else direct stores).
+  p.y_tma = p.y_vec_ok && make_tmap_kmajor(&ty, y, M, N, ldy, kEpiCols, 32) ? 1 : 0;
+  if (!p.y_tma) ty = ta;     // not read by the kernel
+  if (p.n_peers > 0 && !p.y_tma) return cudaErrorInvalidValue;   // peer stores ride the TMA path
+
+  auto kern = dtype == GW_DTYPE_BF16 ? gemm_tc2_kernel<BN, GW_DTYPE_BF16>
+                                     : gemm_tc2_kernel<BN, GW_DTYPE_F16>;
+  cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), C::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  const int64_t pairs = std::max<int64_t>(1, (sm_count > 0 ? sm_count : 148) / 2);
+  const int grid = static_cast<int>(2 * std::min<int64_t>(num_tiles, pairs));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kThreads2);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, tb, ta, ty, p);
 }
 
 cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int64_t lda,
@@ -395,10 +470,6 @@ cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int6
                             void* y, int64_t ldy, unsigned int* err, int sm_count,
                             cudaStream_t stream, void* const* peers, int n_peers,
                             const int64_t* a_cols, int64_t a_width, const int32_t* k_dev) {
-  const int64_t m_tiles = (M + kPairM - 1) / kPairM;
-  const int64_t n_tiles = (N + kPairN - 1) / kPairN;
-  const int64_t num_tiles = m_tiles * n_tiles;
-  if (num_tiles > 0x7FFFFFFFll) return cudaErrorInvalidValue;
   Tc2Params p{};
   p.M = M;
   p.N = N;
@@ -409,43 +480,21 @@ cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int6
   p.y_vec_ok = ((reinterpret_cast<uintptr_t>(y) & 15u) == 0 && (ldy % 8) == 0) ? 1 : 0;
   p.num_kb = static_cast<int>((K + kBK2 - 1) / kBK2);
   p.num_ks = (p.num_kb + kAtoms2 - 1) / kAtoms2;
-  p.m_tiles = static_cast<int>(m_tiles);
-  p.n_tiles = static_cast<int>(n_tiles);
-  p.num_tiles = static_cast<int>(num_tiles);
   p.err = err;
   if (n_peers < 0 || n_peers > kMaxPeers || (n_peers > 0 && !peers)) return cudaErrorInvalidValue;
   p.n_peers = n_peers;
   for (int i = 0; i < n_peers; ++i) p.peers[i] = static_cast<uint16_t*>(peers[i]);
-
   p.a_cols = a_cols;
   p.a_width = a_width;
   p.k_dev = k_dev;
-  CUtensorMap ta, tb, ty;
-  // With a_cols, A is x [M, a_width] (K = the alive count, a multiple of 64).
-  if (a_cols && (K % kBK2) != 0) return cudaErrorInvalidValue;
-  if (!make_tmap_kmajor(&ta, a, M, a_cols ? a_width : K, lda, kBK2, kHalfM)) return cudaErrorInvalidValue;
-  if (!make_tmap_kmajor(&tb, w, N, K, ldw, kBK2, kHalfN)) return cudaErrorInvalidValue;
-  // TMA-store epilogue when y's rows are 16-byte aligned (else direct stores).
-  p.y_tma = p.y_vec_ok && make_tmap_kmajor(&ty, y, M, N, ldy, kEpiCols, 32) ? 1 : 0;
-  if (!p.y_tma) ty = ta;     // not read by the kernel
-  if (n_peers > 0 && !p.y_tma) return cudaErrorInvalidValue;   // peer stores ride the TMA path
-
-  auto kern = dtype == GW_DTYPE_BF16 ? gemm_tc2_kernel<GW_DTYPE_BF16> : gemm_tc2_kernel<GW_DTYPE_F16>;
-  cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), kSmemBytes2);
-  if (e != cudaSuccess) return e;
-  const int64_t pairs = std::max<int64_t>(1, (sm_count > 0 ? sm_count : 148) / 2);
-  const int grid = static_cast<int>(2 * std::min<int64_t>(num_tiles, pairs));
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3(kThreads2);
-  cfg.dynamicSmemBytes = kSmemBytes2;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, tb, ta, ty, p);
+  // GW_GEMM_PAIR_BN=256|192 overrides the tile width (tuning, tests).
+  static const int forced_bn = [] {
+    const char* v = std::getenv("GW_GEMM_PAIR_BN");
+    return v ? std::atoi(v) : 0;
+  }();
+  const int bn = (forced_bn == 256 || forced_bn == 192) ? forced_bn : pair_tile_width(M, N, sm_count);
+  return bn == 192 ? launch_tc2_bn<192>(dtype, p, a, M, K, lda, w, N, ldw, y, ldy, sm_count, stream)
+                   : launch_tc2_bn<256>(dtype, p, a, M, K, lda, w, N, ldw, y, ldy, sm_count, stream);
 }
 
 }  // namespace gw

@@ -181,6 +181,30 @@ def test_pair_gemm_ragged_vs_fp32(dt, M, K, N, kp, bias, act):
     assert _native.device_error(reset=False) & _native.DEVICE_ERR_WAIT_TIMEOUT == 0
 
 
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+@pytest.mark.parametrize("M,K,N,kp,bias,act", [
+    (4096, 768, 768, 384, True, None),          # 64 pair tiles of 256 x 192 (GPT-2 projection)
+    (8192, 768, 768, 308, True, "gelu"),        # 128 tiles, two rounds (DistilBERT projection)
+    (4000, 3072, 760, 1229, False, "gelu_tanh"),  # ragged M and N
+])
+def test_pair_gemm_192_wide_tiles_vs_fp32(dt, M, K, N, kp, bias, act):
+    """Output widths where 192-wide pair tiles fill the SM pairs better than 256-wide ones."""
+    torch_dt = DT[dt]
+    g = torch.Generator(device="cuda").manual_seed(N + kp)
+    x = torch.randn(M, K, device="cuda", dtype=torch_dt, generator=g)
+    w = (torch.randn(N, K, device="cuda", generator=g) / kp ** 0.5).to(torch_dt)
+    b = torch.randn(N, device="cuda", generator=g).to(torch_dt) if bias else None
+    idx = torch.sort(torch.randperm(K, device="cuda", generator=g)[:kp]).values
+    y = ghost_linear(x, pack_weight(w, idx), idx, bias=b, activation=act, strategy="pregather")
+    rows = torch.arange(0, M, 37, device="cuda")
+    ref = F.linear(x[rows].float()[:, idx], w.float()[:, idx], None if b is None else b.float())
+    if act == "gelu":
+        ref = F.gelu(ref)
+    elif act == "gelu_tanh":
+        ref = F.gelu(ref, approximate="tanh")
+    torch.testing.assert_close(y[rows], ref.to(torch_dt), **tols(torch_dt))
+
+
 def test_pair_gemm_unaligned_ldy_direct_stores():
     """ldy not a multiple of 8 on a pair-kernel shape: the epilogue falls back to direct stores."""
     M, K, N, kp = 2048, 1024, 2048, 512
