@@ -212,9 +212,13 @@ class GhostLinear(nn.Module):
         return packed
 
     def _alive_runs(self, alive: torch.Tensor) -> bool:
-        """Whether the frozen list is made of 64-column runs (checked once per list)."""
+        """Whether the frozen list is made of 64-column runs (checked once per list,
+        which reads one count on the host; inside CUDA-graph capture an unchecked
+        list takes the gather path instead)."""
         key = (alive.data_ptr(), alive.numel(), alive._version, alive.device)
         if self._runs is None or self._runs[0] != key:
+            if torch.cuda.is_current_stream_capturing():
+                return False
             self._runs = (key, index_runs(alive, self.in_features) == 0)
         return self._runs[1]
 
@@ -299,6 +303,9 @@ class GhostLinear(nn.Module):
         self._packed = None
         self._runs = None
         self._sparsity_pending = False
+        if (self._frozen_indices.is_cuda and self._frozen_indices.numel()
+                and not torch.cuda.is_current_stream_capturing()):
+            self._alive_runs(self._frozen_indices)     # decided now, not in the first forward
         k_alive = int(self._frozen_indices.numel())
         self._last_sparsity = float(1.0 - k_alive / self.in_features)
 

@@ -146,3 +146,23 @@ def test_device_count_edge_shapes():
     _native.gather_gemm_dev(x, wp, idx, cnt, y, bias=b)
     ref = (x.float()[:, idx] @ w.float()[:, idx].t() + b.float()).half()
     torch.testing.assert_close(y, ref, **tols(torch.float16))
+
+
+def test_frozen_layer_captured_without_warmup():
+    """Freezing decides the runs strategy at once, so the first frozen forward can run
+    inside CUDA-graph capture (no host read there)."""
+    torch.manual_seed(6)
+    lin = nn.Linear(1024, 512).half().cuda()
+    with torch.no_grad():
+        lin.weight[:, 128:384] = 0                # whole 64-column blocks: the runs strategy
+    gl = GhostLinear.from_linear(lin, threshold=0.0)
+    gl.freeze_weight_mask()
+    assert gl._runs is not None and gl._runs[1] is True
+    x = torch.randn(256, 1024, device="cuda", dtype=torch.float16)
+    g = torch.cuda.CUDAGraph()
+    with torch.no_grad(), torch.cuda.graph(g):
+        y = gl(x)
+    x.copy_(torch.randn_like(x))
+    g.replay()
+    torch.testing.assert_close(y, F.linear(x, lin.weight, lin.bias), **tols(torch.float16))
+    del g
