@@ -42,7 +42,6 @@ constexpr int kEpiWarps2 = 8;          // two per TMEM lane quadrant
 // thread waits once and issues 8 MMAs per stage, so its per-stage overhead
 // (barrier wait, fence, commit) is paid once per 1024 tensor cycles.
 constexpr int kAtoms2 = 2;
-constexpr int kStageK2 = kAtoms2 * kBK2;
 constexpr int kStages2 = 3;
 constexpr int kAAtomBytes2 = kHalfM * kBK2 * 2;      // one 128-row x 64-col atom of A (16 KB)
 constexpr int kABytes2 = kAtoms2 * kAAtomBytes2;
