@@ -542,4 +542,53 @@ __device__ __forceinline__ float apply_epilogue(float v, int epi) {
   return v;
 }
 
+// The same for epilogues that round to fp16/bf16: the tanh form uses the
+// identity 0.5 v (1 + tanh(u)) = v * sigmoid(2 u) = v / (1 + exp(-2 u)) with
+// CUDA's fast exponential and division intrinsics (a few ulp of fp32, far below
+// the 16-bit rounding), a third of tanhf's instructions; the erf form is
+// unchanged.
+__device__ __forceinline__ float apply_epilogue16(float v, int epi) {
+  if (epi == GW_EPI_GELU_TANH) {
+    const float u = 0.79788456080286535588f * (v + 0.044715f * v * v * v);
+    return __fdividef(v, 1.0f + __expf(-2.0f * u));
+  }
+  return apply_epilogue(v, epi);
+}
+
+// Epilogue arithmetic for 32 consecutive output columns [n0, n0 + 32) of one
+// row (the 32 values a lane holds after one 32-column TMEM load).
+// Bias: four 16-byte loads when the 32 values lie inside [0, N) and are
+// 16-byte aligned (every lane of the warp reads the same addresses), else one
+// load per element.
+template <int DT>
+__device__ __forceinline__ void add_bias32(float (&f)[32], const uint16_t* bias, int64_t n0,
+                                           int64_t N) {
+  const uint16_t* b = bias + n0;
+  if (n0 + 32 <= N && (reinterpret_cast<uintptr_t>(b) & 15u) == 0) {
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const uint4 q = __ldg(reinterpret_cast<const uint4*>(b) + v);
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        f[8 * v + 2 * k] += Elem<DT>::to_f(static_cast<uint16_t>(w[k] & 0xFFFFu));
+        f[8 * v + 2 * k + 1] += Elem<DT>::to_f(static_cast<uint16_t>(w[k] >> 16));
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (n0 + j < N) f[j] += Elem<DT>::to_f(__ldg(bias + n0 + j));
+  }
+}
+// Activation chosen at compile time, so a kernel instantiation carries the
+// code of one activation only.
+template <int EPI>
+__device__ __forceinline__ void activate32(float (&f)[32]) {
+  if constexpr (EPI != GW_EPI_NONE) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) f[j] = apply_epilogue16(f[j], EPI);
+  }
+}
+
 }  // namespace gw

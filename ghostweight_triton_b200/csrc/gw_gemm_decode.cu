@@ -169,7 +169,7 @@ __device__ __forceinline__ void dc_finish(const DcParams& p, const float* recv, 
     }
     if (p.epi != GW_EPI_NONE) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) f[j] = apply_epilogue(f[j], p.epi);
+      for (int j = 0; j < 4; ++j) f[j] = apply_epilogue16(f[j], p.epi);
     }
     uint16_t* yp = p.y + static_cast<int64_t>(m) * p.ldy + n0;
     if (p.y_vec_ok && n0 + 4 <= p.N) {

@@ -125,7 +125,7 @@ __device__ __forceinline__ void reduce_slice(const SkParams& p, uint32_t red_loc
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         if (p.bias && n0 + j < p.N) f[j] += Elem<DT>::to_f(__ldg(p.bias + n0 + j));
-        if (p.epi != GW_EPI_NONE) f[j] = apply_epilogue(f[j], p.epi);
+        if (p.epi != GW_EPI_NONE) f[j] = apply_epilogue16(f[j], p.epi);
       }
       uint16_t* yp = p.y + m * p.ldy + n0;
       if (p.y_vec_ok && n0 + 4 <= p.N) {

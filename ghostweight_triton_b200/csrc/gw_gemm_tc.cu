@@ -107,7 +107,7 @@ struct TcParams {
   const int32_t* k_dev;         // kATma: K' on the device (num_kb an upper bound; see device_num_kb)
 };
 
-template <int BN, int DT, int AMODE>
+template <int BN, int DT, int AMODE, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
                const __grid_constant__ CUtensorMap tmap_a, const TcParams p) {
@@ -407,15 +407,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
         for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(acc[j]);
         if (c + 1 < kSteps) tc_ld_32x32b_x32(t_row + (c + 1) * 32, acc);
         const int64_t n_base = n_warp + c * 32;
-        if (p.bias) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (n_base + j < p.N) f[j] += Elem<DT>::to_f(__ldg(p.bias + n_base + j));
-        }
-        if (p.epi != GW_EPI_NONE) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) f[j] = apply_epilogue(f[j], p.epi);
-        }
+        if (p.bias) add_bias32<DT>(f, p.bias, n_base, p.N);
+        activate32<EPI>(f);
         if (row_ok) {
           if (p.y_vec_ok && n_base + 32 <= p.N) {
             uint32_t packed[16];
@@ -452,7 +445,9 @@ template <int BN, int DT, int AMODE>
 cudaError_t launch_tc(const CUtensorMap& tb, const CUtensorMap& ta, const TcParams& p,
                       int sm_count, cudaStream_t stream) {
   using C = TcCfg<BN>;
-  auto kern = gemm_tc_kernel<BN, DT, AMODE>;
+  auto kern = p.epi == GW_EPI_GELU_ERF    ? gemm_tc_kernel<BN, DT, AMODE, GW_EPI_GELU_ERF>
+              : p.epi == GW_EPI_GELU_TANH ? gemm_tc_kernel<BN, DT, AMODE, GW_EPI_GELU_TANH>
+                                          : gemm_tc_kernel<BN, DT, AMODE, GW_EPI_NONE>;
   // Opt in to the large dynamic shared-memory carve-out (idempotent, cheap).
   cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), C::kSmemBytes);
   if (e != cudaSuccess) return e;

@@ -96,7 +96,7 @@ struct Tc2Params {
   const int32_t* k_dev;
 };
 
-template <int BN, int DT>
+template <int BN, int DT, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
 gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
                 const __grid_constant__ CUtensorMap tmap_a,
@@ -299,15 +299,8 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
           if (lane == 0) bulk_wait_group_read<0>();
           __syncwarp();
         }
-        if (p.bias) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (n_base + j < p.N) f[j] += Elem<DT>::to_f(__ldg(p.bias + n_base + j));
-        }
-        if (p.epi != GW_EPI_NONE) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) f[j] = apply_epilogue(f[j], p.epi);
-        }
+        if (p.bias) add_bias32<DT>(f, p.bias, n_base, p.N);
+        activate32<EPI>(f);
         uint32_t packed[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) packed[j] = Elem<DT>::pack2(f[2 * j], f[2 * j + 1]);
@@ -445,8 +438,15 @@ cudaError_t launch_tc2_bn(int dtype, Tc2Params& p, const void* a, int64_t M, int
   if (!p.y_tma) ty = ta;     // not read by the kernel
   if (p.n_peers > 0 && !p.y_tma) return cudaErrorInvalidValue;   // peer stores ride the TMA path
 
-  auto kern = dtype == GW_DTYPE_BF16 ? gemm_tc2_kernel<BN, GW_DTYPE_BF16>
-                                     : gemm_tc2_kernel<BN, GW_DTYPE_F16>;
+  const bool bf = dtype == GW_DTYPE_BF16;
+  auto kern = p.epi == GW_EPI_GELU_ERF
+                  ? (bf ? gemm_tc2_kernel<BN, GW_DTYPE_BF16, GW_EPI_GELU_ERF>
+                        : gemm_tc2_kernel<BN, GW_DTYPE_F16, GW_EPI_GELU_ERF>)
+              : p.epi == GW_EPI_GELU_TANH
+                  ? (bf ? gemm_tc2_kernel<BN, GW_DTYPE_BF16, GW_EPI_GELU_TANH>
+                        : gemm_tc2_kernel<BN, GW_DTYPE_F16, GW_EPI_GELU_TANH>)
+                  : (bf ? gemm_tc2_kernel<BN, GW_DTYPE_BF16, GW_EPI_NONE>
+                        : gemm_tc2_kernel<BN, GW_DTYPE_F16, GW_EPI_NONE>);
   cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), C::kSmemBytes);
   if (e != cudaSuccess) return e;
   const int64_t pairs = std::max<int64_t>(1, (sm_count > 0 ? sm_count : 148) / 2);
