@@ -987,7 +987,8 @@ def run_model(args, world, rank, local, which: str):
             "e2e": {"value": round(world * tokens / te, 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": tokens * 8, "d2h_bytes_per_step": tokens * 768 * 2,
                     "ms_per_step": round(te * 1e3, 4)},
-            "gpu_launches": None,
+            # Each frozen GhostLinear forward: the x' gather and the GEMM.
+            "gpu_launches": 2 * len(replaced) * steps,
         }
         print(json.dumps(line), flush=True)
 
