@@ -334,17 +334,18 @@ def sweep(device, peaks) -> list[dict]:
                 dense = lambda: torch.mm(L["x"], L["w"].t(), out=yd)
                 t = event_time(lambda i: ours(), iters=20)
                 td = event_time(lambda i: F.linear(L["x"], L["w"]), iters=20)
-                # The same calls replayed from CUDA graphs: kernel time without
-                # the per-call host overhead (which dominates at M <= 128).
-                tg = graph_time(ours, 20, 1)
-                tdg = graph_time(dense, 20, 1)
+                # The same calls replayed from CUDA graphs of 20 calls each:
+                # kernel time without the per-call host overhead (which
+                # dominates at M <= 128) or one graph launch per call.
+                tg = graph_time(lambda: [ours() for _ in range(20)], 20, 1) / 20
+                tdg = graph_time(lambda: [dense() for _ in range(20)], 20, 1) / 20
                 useful = 2.0 * M * N * kp
                 runs = {}
                 if pattern.startswith("block"):
                     # 64-column runs: the GEMM reads x in place (no gather launch).
                     direct = lambda: ghost_linear(L["x"], L["wp"], L["idx"], out=L["y"], strategy="runs")
                     tr = event_time(lambda i: direct(), iters=20)
-                    trg = graph_time(direct, 20, 1)
+                    trg = graph_time(lambda: [direct() for _ in range(20)], 20, 1) / 20
                     runs = {"runs_us": round(tr * 1e6, 2), "graph_runs_us": round(trg * 1e6, 2),
                             "graph_runs_speedup_vs_dense": round(tdg / trg, 3)}
                 rows.append({"M": M, "pattern": pattern, "sparsity": sp, "K_alive": kp,
