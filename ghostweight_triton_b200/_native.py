@@ -57,6 +57,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gw_packed_gemm": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i, _vp, _i64, _vp]),
     "gw_validate_indices": (_i, [_vp, _i64, _i64, _vp, _vp]),
     "gw_index_runs": (_i, [_vp, _i64, _i64, _vp, _vp]),
+    "gw_gemm_plan": (_i, [_i64, _i64, _i64, ctypes.POINTER(_i), ctypes.POINTER(_i), ctypes.POINTER(_i)]),
     "gw_gather_columns_dev": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _i64, _i64, _vp]),
     "gw_gather_rows_t_dev": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _i64, _i64, _vp]),
     "gw_gather_gemm_dev": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _vp, _i,
@@ -419,6 +420,18 @@ def index_runs(idx: torch.Tensor, K: int) -> int:
         st = load().gw_index_runs(_ptr(idx), idx.numel(), int(K), _ptr(bad), _stream(idx.device))
     _check(st, "gw_index_runs")
     return int(bad.item())
+
+
+GEMM_KERNELS = {1: "pair", 2: "decode", 3: "splitk", 4: "single"}
+
+
+def gemm_plan(M: int, N: int, K: int) -> tuple[str, int, int]:
+    """(kernel, tile width, cluster size) the dense GEMM runs for an M x N output over K
+    columns on the current device (gw_gemm_plan); 0 where the kernel has no such size."""
+    kernel, tile_n, split = _i(), _i(), _i()
+    _check(load().gw_gemm_plan(int(M), int(N), int(K), ctypes.byref(kernel), ctypes.byref(tile_n),
+                               ctypes.byref(split)), "gw_gemm_plan")
+    return GEMM_KERNELS[kernel.value], tile_n.value, split.value
 
 
 def device_error(reset: bool = True, device: torch.device | None = None) -> int:

@@ -326,23 +326,43 @@ bool decode_gemm_enabled() {
 // kernel's epilogue, tile by tile, or by a copy kernel after the other kernels.
 // With a_cols, a is x [M, a_width] and K the count of alive columns, which form
 // 64-column runs starting at a_cols[64 j] (GW_GEMM_RUNS).
+struct GemmChoice {
+  int kernel = GW_KERNEL_SINGLE;
+  gw::DecodePlan dp;
+  gw::SplitKPlan sk;
+};
+
+GemmChoice choose_gemm(int64_t M, int64_t N, int64_t K, const gw::DeviceInfo* d) {
+  GemmChoice c;
+  if (gw::use_pair_gemm(M, N, d->sm_count)) {
+    c.kernel = GW_KERNEL_PAIR;
+    return c;
+  }
+  if (decode_gemm_enabled()) c.dp = gw::plan_decode(M, N, K, d->sm_count);
+  if (c.dp.split >= 2) {
+    c.kernel = GW_KERNEL_DECODE;
+    return c;
+  }
+  c.sk = gw::plan_splitk(M, N, K, d->sm_count);
+  if (c.sk.split >= 2) c.kernel = GW_KERNEL_SPLITK;
+  return c;
+}
+
 cudaError_t launch_dense_gemm(const void* a, int dtype, int64_t M, int64_t K, int64_t lda,
                               const void* w, int64_t N, int64_t ldw, const void* bias, int epilogue,
                               void* y, int64_t ldy, const gw::DeviceInfo* d, cudaStream_t s,
                               void* const* peers = nullptr, int n_peers = 0,
                               const int64_t* a_cols = nullptr, int64_t a_width = 0) {
-  if (gw::use_pair_gemm(M, N, d->sm_count))
+  const GemmChoice c = choose_gemm(M, N, K, d);
+  if (c.kernel == GW_KERNEL_PAIR)
     return gw::launch_gemm_tc2(a, dtype, M, K, lda, w, N, ldw, bias, epilogue, y, ldy,
                                d->err_word, d->sm_count, s, peers, n_peers, a_cols, a_width);
   cudaError_t e;
-  const gw::DecodePlan dp = decode_gemm_enabled() ? gw::plan_decode(M, N, K, d->sm_count)
-                                                  : gw::DecodePlan{};
-  const gw::SplitKPlan sk = dp.split >= 2 ? gw::SplitKPlan{} : gw::plan_splitk(M, N, K, d->sm_count);
-  if (dp.split >= 2)
-    e = gw::launch_gemm_decode(dp, a, dtype, M, K, lda, w, N, ldw, bias, epilogue, y, ldy,
+  if (c.kernel == GW_KERNEL_DECODE)
+    e = gw::launch_gemm_decode(c.dp, a, dtype, M, K, lda, w, N, ldw, bias, epilogue, y, ldy,
                                d->err_word, s, a_cols, a_width);
-  else if (sk.split >= 2)
-    e = gw::launch_gemm_splitk(sk, a, dtype, M, K, lda, w, N, ldw, bias, epilogue, y, ldy,
+  else if (c.kernel == GW_KERNEL_SPLITK)
+    e = gw::launch_gemm_splitk(c.sk, a, dtype, M, K, lda, w, N, ldw, bias, epilogue, y, ldy,
                                d->err_word, s, a_cols, a_width);
   else
     e = gw::launch_gemm_tc(0, a, dtype, M, a_cols ? a_width : K, lda, w, N, ldw, nullptr, K, bias,
@@ -566,6 +586,28 @@ int gw_packed_gemm(const void* a, int dtype, int64_t M, int64_t K, int64_t lda,
     return GW_ERR_ALIGN;
   e = launch_dense_gemm(a, dtype, M, K, lda, w_packed, N, ldw, bias, epilogue, y, ldy, d, s);
   return e == cudaSuccess ? GW_OK : cuda_fail(e);
+}
+
+int gw_gemm_plan(int64_t M, int64_t N, int64_t K, int* kernel, int* tile_n, int* split) {
+  if (M < 0 || N < 0 || K < 0) return GW_ERR_SHAPE;
+  if (!kernel) return GW_ERR_NULL;
+  const gw::DeviceInfo* d = nullptr;
+  int st = current_device(&d);
+  if (st != GW_OK) return st;
+  const GemmChoice c = choose_gemm(M, N, K, d);
+  int tn = 0, sp = 0;
+  if (c.kernel == GW_KERNEL_PAIR) {
+    tn = gw::pair_gemm_tile_width(M, N, d->sm_count);
+  } else if (c.kernel == GW_KERNEL_DECODE) {
+    sp = c.dp.split;
+  } else if (c.kernel == GW_KERNEL_SPLITK) {
+    tn = c.sk.bn;
+    sp = c.sk.split;
+  }
+  *kernel = c.kernel;
+  if (tile_n) *tile_n = tn;
+  if (split) *split = sp;
+  return GW_OK;
 }
 
 int gw_validate_indices(const int64_t* idx, int64_t n, int64_t K, int32_t* bad_count,

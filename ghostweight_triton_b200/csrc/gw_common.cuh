@@ -581,6 +581,24 @@ __device__ __forceinline__ void add_bias32(float (&f)[32], const uint16_t* bias,
       if (n0 + j < N) f[j] += Elem<DT>::to_f(__ldg(bias + n0 + j));
   }
 }
+// The same for four consecutive columns [n0, n0 + 4): one 8-byte load when
+// they lie inside [0, N) and are 8-byte aligned.
+template <int DT>
+__device__ __forceinline__ void add_bias4(float (&f)[4], const uint16_t* bias, int64_t n0,
+                                          int64_t N) {
+  const uint16_t* b = bias + n0;
+  if (n0 + 4 <= N && (reinterpret_cast<uintptr_t>(b) & 7u) == 0) {
+    const uint2 q = __ldg(reinterpret_cast<const uint2*>(b));
+    f[0] += Elem<DT>::to_f(static_cast<uint16_t>(q.x & 0xFFFFu));
+    f[1] += Elem<DT>::to_f(static_cast<uint16_t>(q.x >> 16));
+    f[2] += Elem<DT>::to_f(static_cast<uint16_t>(q.y & 0xFFFFu));
+    f[3] += Elem<DT>::to_f(static_cast<uint16_t>(q.y >> 16));
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (n0 + j < N) f[j] += Elem<DT>::to_f(__ldg(bias + n0 + j));
+  }
+}
 // Activation chosen at compile time, so a kernel instantiation carries the
 // code of one activation only.
 template <int EPI>
@@ -588,6 +606,13 @@ __device__ __forceinline__ void activate32(float (&f)[32]) {
   if constexpr (EPI != GW_EPI_NONE) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) f[j] = apply_epilogue16(f[j], EPI);
+  }
+}
+template <int EPI>
+__device__ __forceinline__ void activate4(float (&f)[4]) {
+  if constexpr (EPI != GW_EPI_NONE) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) f[j] = apply_epilogue16(f[j], EPI);
   }
 }
 

@@ -25,6 +25,8 @@
 // Roles (192 threads): warp 0 TMA producer, warp 1 TMEM allocator + MMA
 // issuer, warps 2..5 TMEM drain; all six warps share the reduction.
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 #include <initializer_list>
 #include <mutex>
 
@@ -86,7 +88,7 @@ __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t cluster_addr) {
 // CTA) and emits it. A task is one row x four columns; a thread takes
 // 16 / S tasks per round and issues all their DSMEM loads before the first
 // add, so the latencies overlap; each task is summed in rank order.
-template <int S, int BN, int DT>
+template <int S, int BN, int DT, int EPI>
 __device__ __forceinline__ void reduce_slice(const SkParams& p, uint32_t red_local, int rank,
                                              int m_blk, int n_blk, int rows_valid, bool ok) {
   constexpr int kStride = SkCfg<BN>::kRedStride;
@@ -122,11 +124,8 @@ __device__ __forceinline__ void reduce_slice(const SkParams& p, uint32_t red_loc
       float f[4] = {acc.x, acc.y, acc.z, acc.w};
       const int64_t n0 = static_cast<int64_t>(n_blk) * BN + g * 4;
       const int64_t m = static_cast<int64_t>(m_blk) * kSkBM + r;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if (p.bias && n0 + j < p.N) f[j] += Elem<DT>::to_f(__ldg(p.bias + n0 + j));
-        if (p.epi != GW_EPI_NONE) f[j] = apply_epilogue16(f[j], p.epi);
-      }
+      if (p.bias) add_bias4<DT>(f, p.bias, n0, p.N);
+      activate4<EPI>(f);
       uint16_t* yp = p.y + m * p.ldy + n0;
       if (p.y_vec_ok && n0 + 4 <= p.N) {
         const uint32_t lo = static_cast<uint32_t>(Elem<DT>::from_f(f[0])) |
@@ -143,7 +142,7 @@ __device__ __forceinline__ void reduce_slice(const SkParams& p, uint32_t red_loc
   }
 }
 
-template <int BN, int DT>
+template <int BN, int DT, int EPI>
 __global__ void __launch_bounds__(kSkThreads, 1)
 gemm_splitk_kernel(const __grid_constant__ CUtensorMap tmap_b,
                    const __grid_constant__ CUtensorMap tmap_a, const SkParams p) {
@@ -290,9 +289,9 @@ gemm_splitk_kernel(const __grid_constant__ CUtensorMap tmap_b,
   // ------------------------------------------------------------ reduce-scatter over DSMEM
   {
     const bool ok = *acc_ok != 0;
-    if (p.split == 8) reduce_slice<8, BN, DT>(p, smem_u32(smem), rank, m_blk, n_blk, rows_valid, ok);
-    else if (p.split == 4) reduce_slice<4, BN, DT>(p, smem_u32(smem), rank, m_blk, n_blk, rows_valid, ok);
-    else reduce_slice<2, BN, DT>(p, smem_u32(smem), rank, m_blk, n_blk, rows_valid, ok);
+    if (p.split == 8) reduce_slice<8, BN, DT, EPI>(p, smem_u32(smem), rank, m_blk, n_blk, rows_valid, ok);
+    else if (p.split == 4) reduce_slice<4, BN, DT, EPI>(p, smem_u32(smem), rank, m_blk, n_blk, rows_valid, ok);
+    else reduce_slice<2, BN, DT, EPI>(p, smem_u32(smem), rank, m_blk, n_blk, rows_valid, ok);
   }
 
   cluster_sync();                      // peers have finished reading this CTA's partial tile
@@ -306,7 +305,12 @@ template <int BN, int DT>
 cudaError_t launch_sk(const CUtensorMap& tb, const CUtensorMap& ta, const SkParams& p,
                       int64_t tiles, cudaStream_t stream) {
   using C = SkCfg<BN>;
-  auto kern = gemm_splitk_kernel<BN, DT>;
+  // One instantiation per activation: the reduction loop is unrolled over
+  // 16 / S tasks, and runtime-selected activation code in it ran cold in the
+  // instruction cache.
+  auto kern = p.epi == GW_EPI_GELU_ERF    ? gemm_splitk_kernel<BN, DT, GW_EPI_GELU_ERF>
+              : p.epi == GW_EPI_GELU_TANH ? gemm_splitk_kernel<BN, DT, GW_EPI_GELU_TANH>
+                                          : gemm_splitk_kernel<BN, DT, GW_EPI_NONE>;
   cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), C::kSmemBytes);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
@@ -336,7 +340,7 @@ struct ClusterTable {
 
 template <int BN>
 int query_active_clusters(int s) {
-  auto kern = gemm_splitk_kernel<BN, GW_DTYPE_F16>;
+  auto kern = gemm_splitk_kernel<BN, GW_DTYPE_F16, GW_EPI_NONE>;
   constexpr int smem = SkCfg<BN>::kSmemBytes;
   if (ensure_smem_attr(reinterpret_cast<const void*>(kern), smem) != cudaSuccess) return 0;
   cudaLaunchConfig_t cfg = {};
@@ -389,23 +393,60 @@ SplitKPlan plan_splitk(int64_t M, int64_t N, int64_t K, int sm_count) {
   if (M <= 0 || N <= 0 || num_kb < 2) return best;
   // The persistent kernels already fill at least half of the SMs.
   if (m_tiles * ((N + 255) / 256) * 2 > sms) return best;
-  // Most CTAs in a single wave of clusters; ties keep the wider tile (less
-  // re-reading of x') and then the larger cluster.
+  // Among the plans whose clusters all run in one wave, the one with the
+  // least estimated time. The estimate is a least-squares fit to measured
+  // times of every feasible plan over 60 shapes (M = 48..512, N = 768..11008,
+  // K' = 768..11008; back-to-back calls, operands in L2):
+  //   0.19 kb + 0.004 load + r_S red   (microseconds)
+  // with kb the k-blocks of one CTA, load the kilobytes of x' and W' it
+  // streams, red the kilobytes it reads in the reduction (valid rows x BN
+  // fp32 values) and r_S = 0.021 / 0.029 / 0.041 for S = 2 / 4 / 8 (the DSMEM
+  // reads of a larger cluster are slower per byte). Its choices came within
+  // 0.4% of the measured best plan summed over the shapes; choosing the most
+  // CTAs instead was 5% slower, and up to 1.6x on single shapes. 32-wide
+  // tiles, never the fastest measured, are used only when no wider tile fits.
   const ClusterTable* table = cluster_table();
   if (!table) return best;
-  int64_t best_ctas = 0;
   const int bns[4] = {256, 128, 64, 32};
   const int ss[3] = {8, 4, 2};
+  // GW_SPLITK="BN,S" forces a tile width and cluster size where they fit;
+  // GW_SPLITK=0 turns the kernel off (tuning and tests).
+  static const int forced[2] = {[] {
+    const char* v = std::getenv("GW_SPLITK");
+    return v ? (v[0] == '0' ? -1 : std::atoi(v)) : 0;
+  }(), [] {
+    const char* v = std::getenv("GW_SPLITK");
+    const char* c = v ? std::strchr(v, ',') : nullptr;
+    return c ? std::atoi(c + 1) : 0;
+  }()};
+  if (forced[0] < 0) return best;
+  const int64_t rows = std::min<int64_t>((M + 7) / 8 * 8, kSkBM);   // rows of one x' box
+  const int64_t rows_valid = std::min<int64_t>(M, kSkBM);
+  auto estimate = [&](int bn, int s) {
+    const int64_t kb = (num_kb + s - 1) / s;
+    const double load = static_cast<double>(kb) * static_cast<double>(rows + bn) * kSkBK * 2 / 1024.0;
+    const double red = static_cast<double>(rows_valid) * bn * 4 / 1024.0;
+    const double r = s == 2 ? 0.021 : s == 4 ? 0.029 : 0.041;
+    return 0.19 * static_cast<double>(kb) + 0.004 * load + r * red + (bn < 64 ? 1e3 : 0.0);
+  };
+  bool found = false;
+  double best_cost = 0.0;
   for (int bi = 0; bi < 4; ++bi) {
     const int bn = bns[bi];
     const int64_t tiles = m_tiles * ((N + bn - 1) / bn);
     for (int si = 0; si < 3; ++si) {
       const int s = ss[si];
-      if (s > num_kb || tiles * s > sms) continue;
-      if (tiles > table->n[bi][si]) continue;
-      const int64_t ctas = tiles * s;
-      if (ctas > best_ctas) {
-        best_ctas = ctas;
+      if (s > num_kb || tiles * s > sms || tiles > table->n[bi][si]) continue;
+      if (bn == forced[0] && s == forced[1]) {
+        best.bn = bn;
+        best.split = s;
+        best.tiles = tiles;
+        return best;
+      }
+      const double cost = estimate(bn, s);
+      if (!found || cost < best_cost) {
+        found = true;
+        best_cost = cost;
         best.bn = bn;
         best.split = s;
         best.tiles = tiles;

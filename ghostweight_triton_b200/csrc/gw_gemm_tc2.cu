@@ -398,6 +398,15 @@ int pair_tile_width(int64_t M, int64_t N, int sm_count) {
 }
 }  // namespace
 
+int pair_gemm_tile_width(int64_t M, int64_t N, int sm_count) {
+  // GW_GEMM_PAIR_BN=256|192 overrides the tile width (tuning, tests).
+  static const int forced_bn = [] {
+    const char* v = std::getenv("GW_GEMM_PAIR_BN");
+    return v ? std::atoi(v) : 0;
+  }();
+  return (forced_bn == 256 || forced_bn == 192) ? forced_bn : pair_tile_width(M, N, sm_count);
+}
+
 bool use_pair_gemm(int64_t M, int64_t N, int sm_count) {
   // GW_GEMM_PAIR=0 forces the single-CTA kernel, =1 the pair kernel (tuning, tests).
   static const int forced = [] {
@@ -486,12 +495,7 @@ cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int6
   p.a_cols = a_cols;
   p.a_width = a_width;
   p.k_dev = k_dev;
-  // GW_GEMM_PAIR_BN=256|192 overrides the tile width (tuning, tests).
-  static const int forced_bn = [] {
-    const char* v = std::getenv("GW_GEMM_PAIR_BN");
-    return v ? std::atoi(v) : 0;
-  }();
-  const int bn = (forced_bn == 256 || forced_bn == 192) ? forced_bn : pair_tile_width(M, N, sm_count);
+  const int bn = pair_gemm_tile_width(M, N, sm_count);
   return bn == 192 ? launch_tc2_bn<192>(dtype, p, a, M, K, lda, w, N, ldw, y, ldy, sm_count, stream)
                    : launch_tc2_bn<256>(dtype, p, a, M, K, lda, w, N, ldw, y, ldy, sm_count, stream);
 }

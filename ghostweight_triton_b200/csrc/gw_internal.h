@@ -92,6 +92,8 @@ cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int6
                             const int32_t* k_dev = nullptr);
 // Whether the CTA-pair kernel serves a dense-A GEMM of this shape.
 bool use_pair_gemm(int64_t M, int64_t N, int sm_count);
+// Tile width (192 or 256) the pair kernel uses for an M x N output.
+int pair_gemm_tile_width(int64_t M, int64_t N, int sm_count);
 
 // gw_gemm_simt.cu: exact-fp32 gather-GEMM.
 // n_dev (optional): the alive count on the device, n_alive its upper bound.

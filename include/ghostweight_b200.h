@@ -327,6 +327,25 @@ GW_API int gw_validate_indices(const int64_t* idx, int64_t n, int64_t K, int32_t
 GW_API int gw_index_runs(const int64_t* idx, int64_t n, int64_t K, int32_t* bad_count,
                          void* stream);
 
+/* GEMM kernels (gw_gemm_plan). */
+typedef enum {
+  GW_KERNEL_PAIR = 1,    /* CTA pairs, 256-row tiles *tile_n columns wide (192 or 256) */
+  GW_KERNEL_DECODE = 2,  /* at most 32 rows: output features on the MMA's M side, clusters of *split */
+  GW_KERNEL_SPLITK = 3,  /* 128 x *tile_n tiles, k split over clusters of *split CTAs */
+  GW_KERNEL_SINGLE = 4   /* persistent single-CTA kernel, 128-row tiles */
+} gw_kernel;
+
+/*
+ * The kernel gw_packed_gemm runs for an M x N output over K columns on the
+ * current device (also gw_gather_gemm's GEMM after its gather, and its runs
+ * strategy): *kernel one of gw_kernel, *tile_n the tile width and *split the
+ * cluster size where the kernel has them, else 0. tile_n and split may be
+ * NULL. For callers that size batches by it and for tests of the dispatch; the
+ * reference has one Triton kernel whose launch grid follows from the block
+ * sizes (kernels/matmul.py:105-121).
+ */
+GW_API int gw_gemm_plan(int64_t M, int64_t N, int64_t K, int* kernel, int* tile_n, int* split);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -86,6 +86,19 @@ def test_no_gpu_reports_unsupported(lib):
     assert lib.gw_device_supported(0) == 0
 
 
+def test_gemm_plan_without_gpu(lib):
+    import ctypes
+
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("GPU present")
+    k, t, s = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    assert lib.gw_gemm_plan(-1, 4, 4, ctypes.byref(k), None, None) == 1          # GW_ERR_SHAPE
+    assert lib.gw_gemm_plan(4, 4, 4, None, None, None) == 4                      # GW_ERR_NULL
+    assert lib.gw_gemm_plan(4, 4, 4, ctypes.byref(k), ctypes.byref(t), ctypes.byref(s)) != 0
+
+
 def test_dtype_and_epilogue_codes():
     import torch
 

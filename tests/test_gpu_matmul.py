@@ -263,14 +263,19 @@ def test_chained_decode_pack_then_runs_gemm(M):
 # ----------------------------------------------------------------- small M (cluster split-K and decode kernels)
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
 @pytest.mark.parametrize("M,K,N,kp,bias,act", [
-    (16, 4096, 4096, 2048, False, None),        # 16 tiles of 256, clusters of 8
-    (1, 4096, 768, 2048, True, "gelu"),         # 12 tiles of 64, clusters of 8; one valid row
-    (100, 4096, 1000, 1500, True, "gelu_tanh"), # ragged last tile, 3 k-blocks per CTA
-    (128, 1024, 4096, 130, True, None),         # 3 k-blocks: clusters of 2, uneven ranges
-    (256, 4096, 2304, 4096, False, "gelu"),     # 2 m-tiles x 9 n-tiles, clusters of 8
-    (33, 768, 3072, 384, True, None),           # GPT-2 MLP-in at decode: tiles of 128, clusters of 4
-    (16, 3072, 768, 1536, True, None),          # GPT-2 MLP-out at decode
+    (16, 4096, 4096, 2048, False, None),        # at most 32 rows: the decode kernel
+    (1, 4096, 768, 2048, True, "gelu"),         # decode kernel, one valid row
+    (100, 4096, 1000, 1500, True, "gelu_tanh"), # tiles of 64, clusters of 4; ragged last tile
+    (128, 1024, 4096, 130, True, None),         # 3 k-blocks: tiles of 64, clusters of 2, uneven ranges
+    (256, 4096, 2304, 4096, False, "gelu"),     # 2 m-tiles x 18 n-tiles of 128, clusters of 4
+    (33, 768, 3072, 384, True, None),           # GPT-2 MLP-in: tiles of 64, clusters of 2
+    (16, 3072, 768, 1536, True, None),          # GPT-2 MLP-out at decode: decode kernel
     (512, 4096, 4096, 2048, True, None),        # 64 tiles of 256, clusters of 2
+    (200, 4096, 3072, 3072, True, "gelu"),      # tiles of 256, clusters of 4
+    (40, 8192, 2048, 8192, False, None),        # tiles of 256, clusters of 8
+    (40, 2048, 1000, 1536, True, "gelu_tanh"),  # tiles of 128, clusters of 8; ragged last tile
+    (200, 1024, 3072, 256, True, None),         # tiles of 128, clusters of 2
+    (40, 1024, 256, 512, False, None),          # tiles of 64, clusters of 8
 ])
 def test_cluster_split_k_vs_fp32(dt, M, K, N, kp, bias, act):
     torch_dt = DT[dt]
@@ -293,6 +298,30 @@ def test_cluster_split_k_vs_fp32(dt, M, K, N, kp, bias, act):
         ref = F.gelu(ref, approximate="tanh")
     torch.testing.assert_close(ys[0], ref.to(torch_dt), **tols(torch_dt))
     assert torch.equal(ys[0], ys[1]) and torch.equal(ys[1], ys[2])
+
+
+@pytest.mark.parametrize("M,N,K,expect", [
+    (4096, 4096, 2048, ("pair", 256, 0)),
+    (16, 4096, 2048, ("decode", 0, None)),
+    (1, 768, 2048, ("decode", 0, None)),
+    (100, 1000, 1500, ("splitk", 64, 4)),
+    (128, 4096, 130, ("splitk", 64, 2)),
+    (48, 4096, 2048, ("splitk", 128, 4)),
+    (512, 4096, 2048, ("splitk", 256, 2)),
+    (200, 3072, 3072, ("splitk", 256, 4)),
+    (40, 2048, 8192, ("splitk", 256, 8)),
+    (40, 1000, 1536, ("splitk", 128, 8)),
+    (200, 3072, 256, ("splitk", 128, 2)),
+    (40, 256, 512, ("splitk", 64, 8)),
+])
+def test_gemm_plan_dispatch(M, N, K, expect):
+    """The kernel each shape dispatches to (the split-K shapes above rely on it)."""
+    kernel, tile_n, split = _native.gemm_plan(M, N, K)
+    assert (kernel, tile_n) == expect[:2]
+    if expect[2] is None:
+        assert split >= 2
+    else:
+        assert split == expect[2]
 
 
 # ----------------------------------------------------------------- decode kernel (M <= 32)
