@@ -85,61 +85,85 @@ __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t cluster_addr) {
 
 // CTA `rank` of the cluster sums column slice [rank * BN / S, (rank + 1) * BN / S)
 // of the S partial tiles (row stride BN + 4 floats at `red_local` in every
-// CTA) and emits it. A task is one row x four columns; a thread takes
-// 16 / S tasks per round and issues all their DSMEM loads before the first
-// add, so the latencies overlap; each task is summed in rank order.
+// CTA) and emits it. Each thread owns one group of four columns of the slice
+// and walks the rows rows0, rows0 + step, ... (step = threads / groups), so the
+// bias, the column bounds and the output pointer are set up once per thread;
+// per row it loads the S partial float4s (16 / S rows per round, all loads
+// issued before the first add so their latencies overlap), sums them in rank
+// order (the result does not depend on timing), applies the epilogue and
+// stores four outputs. (A mapping of one (row, group) task per iteration spent
+// about 200 cycles of dependent index arithmetic per task with six warps per SM.)
 template <int S, int BN, int DT, int EPI>
 __device__ __forceinline__ void reduce_slice(const SkParams& p, uint32_t red_local, int rank,
                                              int m_blk, int n_blk, int rows_valid, bool ok) {
   constexpr int kStride = SkCfg<BN>::kRedStride;
-  constexpr int kSlice = BN / 4 / S;   // float4 groups per row in this CTA's slice
-  constexpr int kPerRound = 16 / S;
-  const int g0 = rank * kSlice;
-  const int tasks = rows_valid * kSlice;
-  for (int t0 = threadIdx.x; t0 < tasks; t0 += kPerRound * kSkThreads) {
-    float4 v[kPerRound][S];
+  constexpr int kGroups = BN / 4 / S;              // float4 groups per row in this CTA's slice
+  constexpr int kStep = kSkThreads / kGroups;      // rows between two rows of one thread
+  constexpr int kRows = 16 / S;                    // rows per round: 16 loads in flight
+  static_assert(kSkThreads % kGroups == 0, "every thread owns one column group");
+  const int grp = static_cast<int>(threadIdx.x) % kGroups;
+  const int row0 = static_cast<int>(threadIdx.x) / kGroups;
+  const int col = (rank * kGroups + grp) * 4;      // first column of the group in the tile
+  const int64_t n0 = static_cast<int64_t>(n_blk) * BN + col;
+  float b[4] = {0.f, 0.f, 0.f, 0.f};
+  if (p.bias) add_bias4<DT>(b, p.bias, n0, p.N);
+  const bool vec = p.y_vec_ok && n0 + 4 <= p.N;
+  const int64_t y_step = static_cast<int64_t>(kStep) * p.ldy;
+  uint16_t* yp = p.y + (static_cast<int64_t>(m_blk) * kSkBM + row0) * p.ldy + n0;
+  const uint32_t col_addr = red_local + static_cast<uint32_t>(col * 4);
+  float sink = 0.f;
+  for (int r = row0; r < rows_valid; r += kRows * kStep, yp += kRows * y_step) {
+    float4 v[kRows][S];
 #pragma unroll
-    for (int u = 0; u < kPerRound; ++u) {
-      const int t = t0 + u * kSkThreads;
-      if (t < tasks) {
-        const int r = t / kSlice;
-        const int g = g0 + (t - r * kSlice);
-        const uint32_t off = static_cast<uint32_t>((r * kStride + g * 4) * 4);
+    for (int u = 0; u < kRows; ++u) {
+      if (r + u * kStep < rows_valid) {
+        const uint32_t addr = col_addr + static_cast<uint32_t>((r + u * kStep) * kStride * 4);
 #pragma unroll
-        for (int s = 0; s < S; ++s) v[u][s] = ld_dsmem_f4(mapa_shared(red_local + off, s));
+        for (int s = 0; s < S; ++s) v[u][s] = ld_dsmem_f4(mapa_shared(addr, s));
       }
     }
-    if (!ok) continue;                 // this CTA's accumulator never arrived (error recorded)
+    if (!ok) {
+      // This CTA's accumulator never arrived (error recorded): no outputs, but
+      // the loaded values are consumed, so every read of a peer's shared memory
+      // has completed before the caller's relaxed cluster arrive.
 #pragma unroll
-    for (int u = 0; u < kPerRound; ++u) {
-      const int t = t0 + u * kSkThreads;
-      if (t >= tasks) continue;
+      for (int u = 0; u < kRows; ++u) {
+        if (r + u * kStep < rows_valid) {
+#pragma unroll
+          for (int s = 0; s < S; ++s) sink += v[u][s].x + v[u][s].y + v[u][s].z + v[u][s].w;
+        }
+      }
+      continue;
+    }
+#pragma unroll
+    for (int u = 0; u < kRows; ++u) {
+      if (r + u * kStep >= rows_valid) break;
       float4 acc = v[u][0];
 #pragma unroll
       for (int s = 1; s < S; ++s) {
         acc.x += v[u][s].x; acc.y += v[u][s].y; acc.z += v[u][s].z; acc.w += v[u][s].w;
       }
-      const int r = t / kSlice;
-      const int g = g0 + (t - r * kSlice);
       float f[4] = {acc.x, acc.y, acc.z, acc.w};
-      const int64_t n0 = static_cast<int64_t>(n_blk) * BN + g * 4;
-      const int64_t m = static_cast<int64_t>(m_blk) * kSkBM + r;
-      if (p.bias) add_bias4<DT>(f, p.bias, n0, p.N);
+      if (p.bias) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) f[j] += b[j];
+      }
       activate4<EPI>(f);
-      uint16_t* yp = p.y + m * p.ldy + n0;
-      if (p.y_vec_ok && n0 + 4 <= p.N) {
+      uint16_t* yr = yp + u * y_step;
+      if (vec) {
         const uint32_t lo = static_cast<uint32_t>(Elem<DT>::from_f(f[0])) |
                             (static_cast<uint32_t>(Elem<DT>::from_f(f[1])) << 16);
         const uint32_t hi = static_cast<uint32_t>(Elem<DT>::from_f(f[2])) |
                             (static_cast<uint32_t>(Elem<DT>::from_f(f[3])) << 16);
-        *reinterpret_cast<uint2*>(yp) = make_uint2(lo, hi);
+        *reinterpret_cast<uint2*>(yr) = make_uint2(lo, hi);
       } else {
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          if (n0 + j < p.N) yp[j] = Elem<DT>::from_f(f[j]);
+          if (n0 + j < p.N) yr[j] = Elem<DT>::from_f(f[j]);
       }
     }
   }
+  asm volatile("" ::"f"(sink));
 }
 
 template <int BN, int DT, int EPI>
@@ -294,7 +318,11 @@ gemm_splitk_kernel(const __grid_constant__ CUtensorMap tmap_b,
     else reduce_slice<2, BN, DT, EPI>(p, smem_u32(smem), rank, m_blk, n_blk, rows_valid, ok);
   }
 
-  cluster_sync();                      // peers have finished reading this CTA's partial tile
+  // Every DSMEM read of this thread has completed: its values were stored to y
+  // or consumed. The outputs need no ordering with the peers, so the arrive is
+  // relaxed and does not wait for the stores of y to be acknowledged.
+  cluster_arrive_relaxed();
+  cluster_wait();                      // peers have finished reading this CTA's partial tile
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::kTmemCols);
