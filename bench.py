@@ -628,6 +628,7 @@ def run_mlp_sharded(args, world, rank, local):
 
 # ---------------------------------------------------------------------------- decoding (small M)
 DECODE_LAYERS = 16
+SMALL_BATCH_ROWS = (64, 128, 256, 512)
 
 
 def run_decode(args, world, rank, local):
@@ -737,14 +738,119 @@ def run_decode(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
-def cpu_decode_sample(kp: int) -> dict:
-    """The oracle's restatement of the reference path for one 16-row layer call."""
+def run_small_batch(args, world, rank, local):
+    """Small batches (64 to 512 rows) through 4096 x 4096 fp16 layers at 50% dead.
+
+    The range between the decode kernel (at most 32 rows) and the CTA-pair
+    kernel, where the output has too few tiles for the SMs and the GEMM is the
+    cluster split-K kernel. 8 layers, each W [4096, 4096] ~ N(0, 1/sqrt(K)) with
+    50% of its input columns zeroed (seeded uniform), K' = 2048, packed once
+    (8 x 16.8 MB of packed weights > 126 MB L2). Step = one layer's gather-GEMM
+    through the product path (ghost_linear, frozen alive list: the gather launch
+    and the GEMM launch) on the next layer; the 8 layer calls are captured in one
+    CUDA graph and replayed. Headline: M = 256.
+    """
+    import torch.nn.functional as F
+
+    from ghostweight_triton_b200 import GhostLinear, _native
+    from ghostweight_triton_b200.kernels.matmul import ghost_linear
+
+    device = torch.device("cuda", torch.cuda.current_device())
+    peaks, peak_src = load_peaks()
+    K = N = 4096
+    n_layers = 8
+    g = torch.Generator(device=device).manual_seed(13 + rank)
+    layers = []
+    for i in range(n_layers):
+        dead = torch.from_numpy(dead_columns(K, 0.5, 200 + i, "random")).to(device)
+        lin = GhostLinear(K, N, bias=False, threshold=0.0, device=device, dtype=torch.float16)
+        with torch.no_grad():
+            lin.weight.normal_(0.0, K ** -0.5, generator=g)
+            lin.weight[:, dead] = 0
+        lin.freeze_weight_mask()
+        layers.append(lin)
+    kp = int(layers[0]._frozen_indices.numel())
+    packed = [lin._weight_packed(lin._frozen_indices, torch.float16) for lin in layers]
+    dense_w = [lin.weight.detach() for lin in layers]
+    reps = max(10, min(args.steps, 50))
+
+    def per_layer(fn_for, xs, ys):
+        fns = [fn_for(i, xs[i], ys[i]) for i in range(n_layers)]
+
+        def all_layers():
+            for f in fns:
+                f()
+        return graph_time(all_layers, reps, world) / n_layers
+
+    ms = tuple(args.rows) if args.rows else SMALL_BATCH_ROWS
+    rows = {}
+    for M in ms:
+        xs = [torch.randn(M, K, device=device, generator=g).half() for _ in range(n_layers)]
+        ys = [torch.empty(M, N, device=device, dtype=torch.float16) for _ in range(n_layers)]
+        t = per_layer(lambda i, x, y: (lambda: ghost_linear(x, packed[i], layers[i]._frozen_indices, out=y)),
+                      xs, ys)
+        err = float((ys[0].float() - F.linear(xs[0].float(), dense_w[0].float())).abs().max().item())
+        xg = [torch.randn(M, kp, device=device, generator=g).half() for _ in range(n_layers)]
+        tg = per_layer(lambda i, x, y: (lambda: _native.packed_gemm(x, packed[i], y)), xg, ys)
+        td = per_layer(lambda i, x, y: (lambda: torch.mm(x, dense_w[i].t(), out=y)), xs, ys)
+        kernel, tile_n, split = _native.gemm_plan(M, N, kp)
+        rows[M] = {"M": M, "us": round(t * 1e6, 3), "useful_tflops": round(2.0 * M * N * kp / t / 1e12, 2),
+                   "gemm_us": round(tg * 1e6, 3), "cublas_dense_us": round(td * 1e6, 3),
+                   "speedup_vs_dense": round(td / t, 3), "gemm_speedup_vs_dense": round(td / tg, 3),
+                   "plan": {"kernel": kernel, "tile_n": tile_n, "split": split},
+                   "max_abs_err_vs_fp32": err}
+        del xs, ys, xg
+    M = 256 if 256 in rows else ms[0]
+    hx = [torch.randn(M, K).half().pin_memory() for _ in range(n_layers)]
+    hy = torch.empty(M, N, dtype=torch.float16).pin_memory()
+
+    def e2e_step(i):
+        with torch.no_grad():
+            hy.copy_(layers[i % n_layers](hx[i % n_layers].to(device, non_blocking=True)), non_blocking=True)
+
+    te = None
+    if not args.no_e2e:
+        for i in range(args.warmup):
+            e2e_step(i)
+        te = timed(e2e_step, args.steps, world) / args.steps
+    if rank == 0:
+        r = rows[M]
+        t = r["us"] * 1e-6
+        useful = 2.0 * M * N * kp
+        tg = r["gemm_us"] * 1e-6
+        line = {
+            "metric": f"useful TFLOP/s of the gather-GEMM at {M} rows (2*M*N*K'), 4096x4096 fp16, 50% dead",
+            "value": round(useful / t / 1e12, 3), "unit": "TFLOP/s", "n_gpus": world, "steps": reps,
+            "warmup": args.warmup, "ms_per_step": round(t * 1e3, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+            "data": "synthetic: x ~ N(0,1), W ~ N(0,1/sqrt(K)), 50% input columns zeroed (seeded uniform)",
+            "config": {"workload": "small batches: 8 rotating 4096x4096 fp16 layers (K'=2048), M=64..512 rows",
+                       "M": M, "N": N, "K": K, "K_alive": kp,
+                       "l2": "8 layers x 16.8 MB packed weights = 134 MB > 126 MB L2",
+                       "timing": "CUDA graph of 8 layer calls, replayed"},
+            "rows": [rows[m] for m in ms],
+            "roofline": {"bound": "tensor", "achieved": round(useful / tg / 1e12, 1),
+                         "peak": float(peaks["bf16_tflops"]), "unit": "TFLOP/s",
+                         "frac": round(useful / tg / 1e12 / float(peaks["bf16_tflops"]), 4), "traffic": None,
+                         "peak_source": f"{peak_src} bf16_tflops", "us": r["gemm_us"],
+                         "kernel": "gemm_splitk_kernel on x' (csrc/gw_gemm_splitk.cu), graph replay"},
+            "cpu_baseline": None if args.no_cpu_baseline else cpu_decode_sample(kp, rows=64),
+            "e2e": None if te is None else {
+                "value": round(useful / te / 1e12, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": M * K * 2,
+                "d2h_bytes_per_step": M * N * 2, "path": "GhostLinear.forward, pinned host x and y"},
+            "gpu_launches": 2 * reps * n_layers,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def cpu_decode_sample(kp: int, rows: int = 16) -> dict:
+    """The oracle's restatement of the reference path for one layer call of `rows` rows."""
     sys.path.insert(0, str(REPO))
     from oracle import gw_oracle as O
 
     rng = np.random.default_rng(5)
     K = N = 4096
-    x = rng.standard_normal((16, K)).astype(np.float16)
+    x = rng.standard_normal((rows, K)).astype(np.float16)
     w = (rng.standard_normal((K, N)) / 64).astype(np.float16)
     idx = np.sort(rng.permutation(K)[:kp]).astype(np.int64)
     O.ghostweight_matmul(x, w, idx)
@@ -753,8 +859,13 @@ def cpu_decode_sample(kp: int) -> dict:
         t0 = time.perf_counter()
         O.ghostweight_matmul(x, w, idx)
         ts.append(time.perf_counter() - t0)
-    return {"value": round(float(np.median(ts)) * 1e6, 1), "unit": "us", "cores": os.cpu_count(),
-            "kind": "port", "sample": "one 16-row 4096x4096 layer call (K'=2048) through "
+    t = float(np.median(ts))
+    if rows == 16:
+        return {"value": round(t * 1e6, 1), "unit": "us", "cores": os.cpu_count(),
+                "kind": "port", "sample": "one 16-row 4096x4096 layer call (K'=2048) through "
+                                          "oracle.ghostweight_matmul, median of 20"}
+    return {"value": round(2.0 * rows * N * kp / t / 1e12, 5), "unit": "TFLOP/s", "cores": os.cpu_count(),
+            "kind": "port", "sample": f"one {rows}-row 4096x4096 layer call (K'={kp}) through "
                                       "oracle.ghostweight_matmul, median of 20"}
 
 
@@ -1040,9 +1151,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["gemm", "mlp-sharded", "ghostlinear-fp32", "gpt2", "distilbert",
-                                           "decode"],
+                                           "decode", "small-batch"],
                     default="gemm")
     ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--rows", type=int, nargs="+", default=None,
+                    help="small-batch workload: the row counts to run (default 64 128 256 512)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-soak", action="store_true",
@@ -1061,6 +1174,8 @@ def main():
             run_fp32_linear(args, world, rank, local)
         elif args.workload == "decode":
             run_decode(args, world, rank, local)
+        elif args.workload == "small-batch":
+            run_small_batch(args, world, rank, local)
         else:
             run_model(args, world, rank, local, args.workload)
     finally:
