@@ -18,7 +18,11 @@
 //      reading the S partial tiles over DSMEM in fixed order s' = 0..S-1 (the
 //      result does not depend on timing), adds bias, applies the activation,
 //      rounds once and stores y;
-//   4. cluster barrier (peers' shared memory stays valid until every read).
+//   4. relaxed cluster arrive once every DSMEM read of the CTA has completed,
+//      then cluster wait (peers' shared memory stays valid until every read;
+//      the stores of y need no ordering with the peers).
+// The plan (tile width BN, cluster size S) minimises a cost estimate fitted to
+// measured times (plan_splitk below).
 // The cluster is gang-scheduled, so its barriers cannot wait on a CTA that is
 // not running; every other wait is bounded (gw_common.cuh). No TMA multicast.
 //
