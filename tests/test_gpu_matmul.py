@@ -405,6 +405,25 @@ def test_cluster_split_k_unaligned_ldy():
     assert torch.count_nonzero(big[:, N]).item() == 0
 
 
+@pytest.mark.parametrize("M,kp", [(100, 1500), (64, 2048)])
+def test_cluster_split_k_partial_column_group(M, kp):
+    """N = 1002 with ldy = 1004: 8-byte stores are allowed, and the last group of four
+    columns straddles N, so it is stored element by element; columns N.. stay untouched."""
+    N, K = 1002, 4096
+    assert _native.gemm_plan(M, N, kp)[0] == "splitk"
+    g = torch.Generator(device="cuda").manual_seed(M + kp)
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16, generator=g)
+    w = (torch.randn(N, K, device="cuda", generator=g) / kp ** 0.5).bfloat16()
+    b = torch.randn(N, device="cuda", generator=g).bfloat16()
+    idx = torch.sort(torch.randperm(K, device="cuda", generator=g)[:kp]).values
+    big = torch.zeros(M, N + 2, device="cuda", dtype=torch.bfloat16)
+    y = big[:, :N]
+    _native.gather_gemm(x, pack_weight(w, idx), idx, y, bias=b, activation="gelu")
+    ref = F.gelu(F.linear(x.float()[:, idx], w.float()[:, idx], b.float())).bfloat16()
+    torch.testing.assert_close(y, ref, **tols(torch.bfloat16))
+    assert torch.count_nonzero(big[:, N:]).item() == 0
+
+
 def test_no_wait_timeouts_after_suite():
     assert _native.device_error(reset=False) & _native.DEVICE_ERR_WAIT_TIMEOUT == 0
 
