@@ -203,8 +203,14 @@ def event_time(fn, iters: int = 10, warmup: int = 3) -> float:
 
 # ---------------------------------------------------------------------------- CPU reference path
 def cpu_reference_sample(M: int, N: int, K: int, sparsity: float, pattern: str, rows: int,
-                         budget_s: float, max_reps: int, seed: int = 0) -> dict:
-    """Time the oracle (numpy, all cores) on `rows` rows of the workload."""
+                         budget_s: float, max_reps: int, seed: int = 0,
+                         exact: tuple[int, int] | None = None) -> dict:
+    """Time the oracle (numpy, all cores) on `rows` rows of the workload.
+
+    Default: up to max_reps timed calls within budget_s after one warm call.
+    exact = (warmup, steps): that many untimed, then exactly that many timed
+    calls; if they would take longer than budget_s, the sample shrinks to fewer
+    rows (at least 16) instead."""
     from oracle import gw_oracle as O
 
     try:
@@ -221,20 +227,34 @@ def cpu_reference_sample(M: int, N: int, K: int, sparsity: float, pattern: str, 
     idx = np.setdiff1d(np.arange(K), dead)
     ctx = threadpool_limits(limits=cores) if threadpool_limits else None
     try:
+        t0 = time.perf_counter()
         O.ghostweight_matmul(x, w_kn, idx)          # warm
+        t_warm = time.perf_counter() - t0
         times = []
-        t_end = time.perf_counter() + budget_s
-        while len(times) < max_reps and (not times or time.perf_counter() < t_end):
-            t0 = time.perf_counter()
-            O.ghostweight_matmul(x, w_kn, idx)
-            times.append(time.perf_counter() - t0)
+        if exact is not None:
+            warmup, steps = exact
+            if (warmup + steps) * t_warm > budget_s:
+                rows = max(16, int(rows * budget_s / ((warmup + steps) * t_warm)))
+                x = np.ascontiguousarray(x[:rows])
+            for _ in range(warmup):
+                O.ghostweight_matmul(x, w_kn, idx)
+            for _ in range(steps):
+                t0 = time.perf_counter()
+                O.ghostweight_matmul(x, w_kn, idx)
+                times.append(time.perf_counter() - t0)
+        else:
+            t_end = time.perf_counter() + budget_s
+            while len(times) < max_reps and (not times or time.perf_counter() < t_end):
+                t0 = time.perf_counter()
+                O.ghostweight_matmul(x, w_kn, idx)
+                times.append(time.perf_counter() - t0)
     finally:
         if ctx is not None:
             ctx.__exit__(None, None, None)
     t = statistics.median(times)
     flops = 2.0 * rows * N * len(idx)
     return {"value": flops / t / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
-            "seconds_per_sample": t, "reps": len(times),
+            "seconds_per_sample": t, "reps": len(times), "rows": rows,
             "sample": f"{rows} of {M} rows of x through oracle.ghostweight_matmul "
                       f"(fp32 gather + numpy sgemm over K'={len(idx)}, N={N}), median of {len(times)}"}
 
@@ -244,21 +264,20 @@ def run_reference(args, world, rank):
         return
     cfg = HEADLINE
     rows = 256
-    steps_total = args.warmup + args.steps
-    # Bound the whole run to a few minutes: at most ~150 s of CPU work.
-    per_step_budget = max(0.05, 150.0 / max(1, steps_total))
+    # W untimed and exactly K timed calls, each on a sample of the workload's
+    # rows, bounded to about 150 s of CPU work in all.
     res = cpu_reference_sample(cfg["M"], cfg["N"], cfg["K"], cfg["sparsity"], cfg["pattern"], rows,
-                               budget_s=per_step_budget * steps_total, max_reps=steps_total)
+                               budget_s=150.0, max_reps=args.steps, exact=(args.warmup, args.steps))
     kp = cfg["K"] - int(cfg["K"] * cfg["sparsity"])
     line = {
         "impl": "reference", "metric": METRIC, "value": round(res["value"], 6), "unit": "TFLOP/s",
-        "n_gpus": args.gpus, "steps": res["reps"], "warmup": 1,
+        "n_gpus": args.gpus, "steps": res["reps"], "warmup": args.warmup,
         "ms_per_step": round(res["seconds_per_sample"] * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp16 in, fp32 compute (CPU)",
         "data": "synthetic (seeded N(0,1) activations, N(0,1/sqrt(K)) weight, dead columns zeroed)",
         "config": {"workload": "gather-GEMM M=N=K=4096, 50% random dead input columns",
                    "M": cfg["M"], "N": cfg["N"], "K": cfg["K"], "K_alive": kp,
-                   "sample_rows": rows},
+                   "sample_rows": res["rows"]},
         "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": round(res["value"], 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
