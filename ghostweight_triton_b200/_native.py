@@ -58,6 +58,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gw_validate_indices": (_i, [_vp, _i64, _i64, _vp, _vp]),
     "gw_index_runs": (_i, [_vp, _i64, _i64, _vp, _vp]),
     "gw_gemm_plan": (_i, [_i64, _i64, _i64, ctypes.POINTER(_i), ctypes.POINTER(_i), ctypes.POINTER(_i)]),
+    "gw_selftest_wait_timeout": (_i, [_i64, _vp]),
     "gw_gather_columns_dev": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _i64, _i64, _vp]),
     "gw_gather_rows_t_dev": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _i64, _i64, _vp]),
     "gw_gather_gemm_dev": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _vp, _i,
@@ -442,6 +443,15 @@ def device_error(reset: bool = True, device: torch.device | None = None) -> int:
         st = load().gw_get_device_error(1 if reset else 0, ctypes.byref(out))
     _check(st, "gw_get_device_error")
     return int(out.value)
+
+
+def selftest_wait_timeout(limit_ns: int = 1_000_000, device: torch.device | None = None) -> None:
+    """Launch the bounded-wait self-test kernel on the current stream (its waits
+    give up after limit_ns and raise DEVICE_ERR_WAIT_TIMEOUT; no synchronisation)."""
+    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    with _on_device(dev):
+        st = load().gw_selftest_wait_timeout(int(limit_ns), _stream(dev))
+    _check(st, "gw_selftest_wait_timeout")
 
 
 def device_supported(device: int = 0) -> bool:

@@ -12,6 +12,23 @@
 // Module-wide device error word (GW_DEVICE_ERR_* bits). Kernels receive its
 // device address, fetched once per device with cudaGetSymbolAddress.
 __device__ unsigned int g_gw_device_error = 0;
+// A counter no code ever increments: the wait of gw_selftest_wait_timeout.
+__device__ unsigned int g_gw_never_set = 0;
+
+namespace gw {
+namespace {
+// gw_selftest_wait_timeout: both waits can only end by running out of time.
+__global__ void selftest_wait_kernel(unsigned long long limit_ns, unsigned int* err) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  const uint32_t b = smem_u32(&bar);
+  mbar_init(b, 1);               // one arrival expected, none ever made
+  mbar_init_fence();
+  mbar_wait(b, 0u, nullptr, err, limit_ns);
+  wait_counter_geq(&g_gw_never_set, 1u, nullptr, err, limit_ns);
+}
+}  // namespace
+}  // namespace gw
 
 namespace gw {
 
@@ -104,25 +121,38 @@ bool make_tmap_kmajor(CUtensorMap* map, const void* base, int64_t rows, int64_t 
 
 }  // namespace gw
 
-namespace {
+namespace gw {
 
 int cuda_fail(cudaError_t e) {
-  std::snprintf(gw::g_cuda_msg, sizeof(gw::g_cuda_msg), "%s: %s", cudaGetErrorName(e),
+  // Clear the error the runtime keeps for this thread, so the next call of
+  // this library does not see it again.
+  cudaGetLastError();
+  std::snprintf(g_cuda_msg, sizeof(g_cuda_msg), "%s: %s", cudaGetErrorName(e),
                 cudaGetErrorString(e));
   return GW_ERR_CUDA;
 }
 
-// Current device info; fails with GW_ERR_DEVICE off sm_100.
-int current_device(const gw::DeviceInfo** out) {
+int current_device(const DeviceInfo** out, int* device) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e);
-  const gw::DeviceInfo* d = gw::device_info(dev);
-  if (!d) return cuda_fail(cudaGetLastError());
+  const DeviceInfo* d = device_info(dev);
+  if (!d) {
+    e = cudaGetLastError();
+    return cuda_fail(e != cudaSuccess ? e : cudaErrorInvalidDevice);
+  }
   if (d->cc_major != 10 || !d->err_word) return GW_ERR_DEVICE;
   *out = d;
+  if (device) *device = dev;
   return GW_OK;
 }
+
+}  // namespace gw
+
+namespace {
+
+using gw::cuda_fail;
+using gw::current_device;
 
 bool valid_dtype(int dt) { return dt == GW_DTYPE_F16 || dt == GW_DTYPE_BF16 || dt == GW_DTYPE_F32; }
 bool valid_epi(int e) { return e == GW_EPI_NONE || e == GW_EPI_GELU_ERF || e == GW_EPI_GELU_TANH; }
@@ -608,6 +638,17 @@ int gw_gemm_plan(int64_t M, int64_t N, int64_t K, int* kernel, int* tile_n, int*
   if (tile_n) *tile_n = tn;
   if (split) *split = sp;
   return GW_OK;
+}
+
+int gw_selftest_wait_timeout(int64_t limit_ns, void* stream) {
+  const gw::DeviceInfo* d = nullptr;
+  int st = current_device(&d);
+  if (st != GW_OK) return st;
+  const int64_t lim = limit_ns < 100000 ? 100000 : (limit_ns > 1000000000 ? 1000000000 : limit_ns);
+  gw::selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<unsigned long long>(lim), d->err_word);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? GW_OK : cuda_fail(e);
 }
 
 int gw_validate_indices(const int64_t* idx, int64_t n, int64_t K, int32_t* bad_count,

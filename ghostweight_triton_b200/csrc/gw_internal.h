@@ -17,6 +17,13 @@ struct DeviceInfo {
   unsigned int* err_word = nullptr;   // device address of the module error word
 };
 const DeviceInfo* device_info(int device);   // nullptr on failure
+// The current device's info (and, if `device` is not null, its ordinal);
+// GW_ERR_DEVICE off sm_100, GW_ERR_CUDA (through cuda_fail) when a runtime
+// call fails.
+int current_device(const DeviceInfo** out, int* device = nullptr);
+// Records `e` as the text gw_last_cuda_error returns, clears the runtime's
+// pending error and returns GW_ERR_CUDA.
+int cuda_fail(cudaError_t e);
 
 // gw_mask.cu
 size_t mask_workspace_bytes(int64_t cols);

@@ -14,7 +14,6 @@
 // The array's name in host code is only a host-side stand-in, not a device
 // address, so the host fetches the real address with cudaGetSymbolAddress once
 // per device (with that device current) and passes it to the kernel.
-#include <cstdio>
 #include <mutex>
 
 #include "gw_common.cuh"
@@ -55,25 +54,33 @@ extern "C" int gw_mask_compact_static(const void* x, int dtype, int64_t rows, in
   if (rows < 0 || cols < 0 || ld < 0 || (rows > 1 && ld < cols)) return GW_ERR_SHAPE;
   // Sizes beyond the static scratch are rejected before anything is launched.
   if (cols > kMaxCols) return GW_ERR_WORKSPACE;
+  // Errors take the same route as gw_mask_compact's: gw::current_device and
+  // gw::cuda_fail record the CUDA error text for gw_last_cuda_error and clear
+  // the runtime's pending error.
+  const gw::DeviceInfo* d = nullptr;
   int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return GW_ERR_CUDA;
-  const gw::DeviceInfo* d = gw::device_info(dev);
-  if (!d) return GW_ERR_CUDA;
-  if (d->cc_major != 10) return GW_ERR_DEVICE;
+  int st = gw::current_device(&d, &dev);
+  if (st != GW_OK) return st;
+  if (dev >= kMaxDevices) return GW_ERR_DEVICE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
   if (cols == 0) {
-    if (alive_count && cudaMemsetAsync(alive_count, 0, sizeof(int32_t), s) != cudaSuccess)
-      return GW_ERR_CUDA;
+    if (alive_count) {
+      e = cudaMemsetAsync(alive_count, 0, sizeof(int32_t), s);
+      if (e != cudaSuccess) return gw::cuda_fail(e);
+    }
     return GW_OK;
   }
   if (rows > 0 && !x) return GW_ERR_NULL;
   void* scratch = nullptr;
-  if (static_scratch(dev, &scratch) != cudaSuccess) return GW_ERR_CUDA;
+  e = static_scratch(dev, &scratch);
+  if (e != cudaSuccess) return gw::cuda_fail(e);
   // The array keeps whatever the previous call left; the kernel needs the
   // ticket and flag words it uses to start at zero.
   const size_t used = gw::mask_workspace_bytes(cols);
-  if (cudaMemsetAsync(scratch, 0, used, s) != cudaSuccess) return GW_ERR_CUDA;
-  cudaError_t e = gw::launch_mask_compact(x, dtype, rows, cols, ld, static_cast<float>(threshold),
-                                          mask, alive_idx, alive_count, scratch, d->sm_count, s);
-  return e == cudaSuccess ? GW_OK : GW_ERR_CUDA;
+  e = cudaMemsetAsync(scratch, 0, used, s);
+  if (e != cudaSuccess) return gw::cuda_fail(e);
+  e = gw::launch_mask_compact(x, dtype, rows, cols, ld, static_cast<float>(threshold), mask,
+                              alive_idx, alive_count, scratch, d->sm_count, s);
+  return e == cudaSuccess ? GW_OK : gw::cuda_fail(e);
 }

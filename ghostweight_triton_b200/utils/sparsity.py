@@ -1,63 +1,67 @@
-"""Host-side sparsity statistics and printing.
+"""Host-side sparsity summaries (not on the hot path).
 
-Same behaviour as ghostweight_triton/utils/sparsity.py:8-89: ``sparsity_stats``
-summarises an int32 alive mask, ``log_sparsity`` pretty-prints either a mask
-or a {layer: sparsity} report.
+Keeps the reference's two names and the keys of ``sparsity_stats``'s result
+(ghostweight_triton/utils/sparsity.py:8-89) so user code that reads them keeps
+working. The counting runs on the mask's device with one host read, and
+``log_sparsity`` renders through one small table formatter for both kinds of
+input.
 """
 
 from __future__ import annotations
 
 import torch
 
+_BAR = 32
+
 
 def sparsity_stats(mask: torch.Tensor) -> dict:
-    """Counts for a [K] dead-neuron mask (1 = alive, 0 = dead).
+    """Counts for a 1-D alive mask (non-zero = alive), e.g. ``dead_neuron_mask``'s output.
 
-    Returns a dict with keys total, alive, dead, pct_dead, pct_alive.
+    Returns ``{"total", "alive", "dead", "pct_dead", "pct_alive"}``; the
+    fractions are 0.0 for an empty mask.
     """
-    assert mask.ndim == 1, f"Expected 1D mask, got shape {mask.shape}"
-    total = mask.numel()
-    alive = int(mask.sum().item())
-    dead = total - alive
-    return {
-        "total": total,
-        "alive": alive,
-        "dead": dead,
-        "pct_dead": dead / total if total > 0 else 0.0,
-        "pct_alive": alive / total if total > 0 else 0.0,
-    }
+    if mask.ndim != 1:
+        raise AssertionError(f"sparsity_stats takes a 1-D mask; got {mask.ndim} dims {tuple(mask.shape)}")
+    total = int(mask.numel())
+    alive = int(torch.count_nonzero(mask).item()) if total else 0
+    frac = (lambda n: n / total) if total else (lambda n: 0.0)
+    return {"total": total, "alive": alive, "dead": total - alive,
+            "pct_dead": frac(total - alive), "pct_alive": frac(alive)}
 
 
-def log_sparsity(
-    report: dict[str, float] | torch.Tensor,
-    title: str = "GhostWeight Sparsity Report",
-) -> None:
-    """Print a mask summary (tensor input) or a per-layer sparsity table (dict input)."""
+def _table(title: str, header: tuple[str, str, str], rows: list[tuple[str, str, str]],
+           footer: tuple[str, str, str] | None) -> str:
+    w0 = max([len(header[0])] + [len(r[0]) for r in rows] + ([len(footer[0])] if footer else []))
+    w1 = max([len(header[1])] + [len(r[1]) for r in rows] + ([len(footer[1])] if footer else []))
+    fmt = lambda r: f"  {r[0]:<{w0}}  {r[1]:>{w1}}  {r[2]}".rstrip()
+    width = w0 + w1 + _BAR + 6
+    out = [f"{title} ".ljust(width, "="), fmt(header), "-" * width]
+    out += [fmt(r) for r in rows]
+    if footer:
+        out += ["-" * width, fmt(footer)]
+    return "\n".join(out)
+
+
+def _bar(frac: float) -> str:
+    n = max(0, min(_BAR, round(frac * _BAR)))
+    return "|" + "#" * n + " " * (_BAR - n) + "|"
+
+
+def log_sparsity(report: dict[str, float] | torch.Tensor,
+                 title: str = "GhostWeight Sparsity Report") -> None:
+    """Print a mask summary (tensor) or a {layer name: dead fraction} table (dict,
+    e.g. ``get_sparsity_report``'s result)."""
     if isinstance(report, torch.Tensor):
         s = sparsity_stats(report)
-        rule = "-" * 60
-        print(f"\n{rule}\n  {title}\n{rule}")
-        print(f"  Total neurons : {s['total']}")
-        print(f"  Alive         : {s['alive']} ({s['pct_alive']:.1%})")
-        print(f"  Dead          : {s['dead']} ({s['pct_dead']:.1%})")
-        print(f"{rule}\n")
+        rows = [("alive", f"{s['alive']}/{s['total']}", f"{s['pct_alive']:.1%}"),
+                ("dead", f"{s['dead']}/{s['total']}", f"{s['pct_dead']:.1%} {_bar(s['pct_dead'])}")]
+        print(_table(title, ("neurons", "count", "share"), rows, None))
         return
-
     if not report:
-        print(f"[{title}] No GhostLinear layers found.")
+        print(f"{title}: no GhostLinear layers in the report")
         return
-
-    width = max(20, max(len(n) for n in report))
-    bar_w = 40
-    rule = "-" * (width + bar_w + 20)
-    print(f"\n{rule}\n  {title}\n{rule}")
-    print(f"  {'Layer':<{width}}  {'Sparsity':>8}  Dead neurons")
-    total = 0.0
-    for name, sp in report.items():
-        sp = float(sp)
-        filled = int(sp * bar_w)
-        print(f"  {name:<{width}}  {sp:>7.1%}  {'#' * filled}{'.' * (bar_w - filled)}")
-        total += sp
-    print(rule)
-    print(f"  {'Average':<{width}}  {total / len(report):>7.1%}")
-    print(f"{rule}\n")
+    fracs = {name: float(v) for name, v in report.items()}
+    rows = [(name, f"{f:.1%}", _bar(f)) for name, f in fracs.items()]
+    mean = sum(fracs.values()) / len(fracs)
+    print(_table(title, ("layer", "dead", ""), rows, (f"mean of {len(fracs)} layers", f"{mean:.1%}",
+                                                       _bar(mean))))

@@ -327,6 +327,17 @@ GW_API int gw_validate_indices(const int64_t* idx, int64_t n, int64_t K, int32_t
 GW_API int gw_index_runs(const int64_t* idx, int64_t n, int64_t K, int32_t* bad_count,
                          void* stream);
 
+/*
+ * Self-test of the bounded waits every kernel of this library relies on. One
+ * thread of one CTA waits on an mbarrier that nothing arrives on, then on a
+ * device counter that nothing increments, each with a wall-clock limit of
+ * limit_ns (clamped to [1e5, 1e9] ns) instead of the kernels' 2 s. Both waits
+ * give up, raise GW_DEVICE_ERR_WAIT_TIMEOUT in the device error word and the
+ * kernel returns normally; read the word with gw_get_device_error. For tests of
+ * the give-up path (no GPU fault, no hang); the reference has no device waits.
+ */
+GW_API int gw_selftest_wait_timeout(int64_t limit_ns, void* stream);
+
 /* GEMM kernels (gw_gemm_plan). */
 typedef enum {
   GW_KERNEL_PAIR = 1,    /* CTA pairs, 256-row tiles *tile_n columns wide (192 or 256) */

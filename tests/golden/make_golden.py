@@ -8,8 +8,10 @@ matmul.py:125-140) -- the wrappers themselves assert CUDA tensors. The outputs
 are written to tests/golden/*.npz together with their inputs (small cases) or
 the seeds that regenerate them (tests/golden/gw_inputs.py).
 
-Needs the reference checkout (default /root/reference, or GW_REFERENCE_DIR);
-run from anywhere:  python tests/golden/make_golden.py
+Needs the reference package: the directory named by GW_REFERENCE_DIR (a
+checkout, or any directory holding the ghostweight_triton package), else the
+copy installed under baseline/_ref of this repository. Run from anywhere:
+  GW_REFERENCE_DIR=<reference checkout> python tests/golden/make_golden.py
 The GPU test box never runs this; it only reads the committed .npz files.
 """
 
@@ -24,7 +26,20 @@ from pathlib import Path
 os.environ["TRITON_INTERPRET"] = "1"
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("GW_REFERENCE_DIR", "/root/reference"))
+
+
+def _reference_dir() -> Path:
+    env = os.environ.get("GW_REFERENCE_DIR")
+    if env:
+        return Path(env)
+    installed = HERE.parents[1] / "baseline" / "_ref"
+    if (installed / "ghostweight_triton" / "__init__.py").exists():
+        return installed
+    raise SystemExit("set GW_REFERENCE_DIR to the reference checkout (or install the reference "
+                     "into baseline/_ref) before generating golden vectors")
+
+
+REF = _reference_dir()
 sys.path.insert(0, str(REF))
 sys.path.insert(1, str(HERE))
 

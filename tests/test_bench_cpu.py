@@ -37,6 +37,16 @@ def test_reference_sample_shrinks_rows_to_the_time_bound():
     assert res["reps"] == 4 and res["rows"] == 16
 
 
+def test_reference_sample_never_grows_a_small_sample():
+    # A sample smaller than the 16-row floor stays as drawn, and the FLOP count
+    # follows the rows actually multiplied.
+    b = _bench()
+    res = b.cpu_reference_sample(256, 128, 256, 0.5, "random", rows=8, budget_s=1e-9, max_reps=2,
+                                 exact=(1, 2))
+    assert res["rows"] == 8
+    assert abs(res["value"] * 1e12 * res["seconds_per_sample"] - 2.0 * 8 * 128 * 128) < 1.0
+
+
 def test_reference_arm_line():
     out = subprocess.run([sys.executable, str(REPO / "bench.py"), "--impl", "reference", "--steps", "2",
                           "--warmup", "3"], cwd=REPO, capture_output=True, text=True, timeout=600)

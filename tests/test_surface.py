@@ -174,9 +174,16 @@ def test_sparsity_utils_cpu(capsys):
     s = sparsity_stats(m)
     assert s == {"total": 4, "alive": 3, "dead": 1, "pct_dead": 0.25, "pct_alive": 0.75}
     log_sparsity(m)
+    out = capsys.readouterr().out
+    assert "3/4" in out and "25.0%" in out
     log_sparsity({"a": 0.5, "b": 0.25})
+    out = capsys.readouterr().out
+    assert "mean of 2 layers" in out and "37.5%" in out
     log_sparsity({})
-    assert "Average" in capsys.readouterr().out
+    assert "no GhostLinear layers" in capsys.readouterr().out
+    assert sparsity_stats(torch.zeros(0, dtype=torch.int32))["pct_dead"] == 0.0
+    with pytest.raises(AssertionError):
+        sparsity_stats(torch.zeros(2, 2))
 
 
 def test_check_environment_reports_native_library():

@@ -68,6 +68,24 @@ def test_two_calls_in_a_row_match_regular_entry():
         assert n_s == int((x.abs().float().amax(0) > thr).sum().item())
 
 
+@pytest.mark.parametrize("rows,cols,dtype,thr", [
+    (257, 8191, torch.float16, 0.0),       # odd column count: the scalar (one column per thread) kernel
+    (33, 4096, torch.bfloat16, -1.0),      # negative threshold: every column alive
+    (16, 0, torch.float32, 0.0),           # no columns: nothing launched, the count reads 0
+])
+def test_scalar_path_negative_threshold_and_empty(rows, cols, dtype, thr):
+    # Each case is run twice through the static entry point, so the second
+    # run starts from whatever the first left in the shared array.
+    x = _input(rows, max(cols, 1), dtype, 0.5, 3)[:, :cols].contiguous()
+    ref = _run("regular", x, thr)
+    for _ in range(2):
+        m_s, i_s, n_s = _run("static", x, thr)
+        assert n_s == ref[2]
+        assert np.array_equal(m_s, ref[0])
+        assert np.array_equal(i_s, ref[1])
+    assert n_s == (cols if thr < 0 else int((x.abs().float().amax(0) > thr).sum().item()) if cols else 0)
+
+
 def test_oversized_request_is_rejected_without_launch():
     lib = _native.load()
     x = torch.zeros(1, 16, device="cuda")
