@@ -146,6 +146,9 @@ def dist_setup(args):
 
         import torch.distributed as dist
 
+        # NCCL's communicator set-up lines (rank count per communicator) on stderr.
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         if args.impl == "ours":
             torch.cuda.set_device(local)
         dist.init_process_group("nccl" if args.impl == "ours" else "gloo",
@@ -286,6 +289,180 @@ def run_reference(args, world, rank):
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------- reference's Triton kernels on the GPU
+REF_DIR = REPO / "baseline" / "_ref"
+REF_WARMUP, REF_ITERS = 10, 100              # benchmarks/bench_kernels.py:45-46 of the reference
+# (name, M, N, K, dead fraction): the headline point, the standalone sweep's
+# other row counts and 90%, and the reference benchmark's own layer shapes
+# (benchmarks/bench_kernels.py:34-41) at 50%.
+REF_MATMUL_CASES = [("headline_4096x4096x4096_s50", 4096, 4096, 4096, 0.5),
+                    ("sweep_4096x4096x4096_s90", 4096, 4096, 4096, 0.9),
+                    ("sweep_1024x4096x4096_s50", 1024, 4096, 4096, 0.5),
+                    ("sweep_128x4096x4096_s50", 128, 4096, 4096, 0.5),
+                    ("sweep_16x4096x4096_s50", 16, 4096, 4096, 0.5),
+                    ("layer_1x3072x768_s50", 1, 3072, 768, 0.5),
+                    ("layer_16x3072x768_s50", 16, 3072, 768, 0.5),
+                    ("layer_128x3072x768_s50", 128, 3072, 768, 0.5),
+                    ("layer_128x768x3072_s50", 128, 768, 3072, 0.5)]
+
+
+def cuda_mean_ms(fn, warmup: int = REF_WARMUP, iters: int = REF_ITERS) -> float:
+    """Mean per-call time of fn() by CUDA events, as the reference's benchmark measures it."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def _ref_inputs(device) -> dict:
+    """Seeded inputs shared by the reference child process and the comparison."""
+    g = torch.Generator(device=device).manual_seed(2026)
+    out = {}
+    for name, M, N, K, sp in REF_MATMUL_CASES:
+        x = torch.randn(M, K, device=device, generator=g).half()
+        w_kn = (torch.randn(K, N, device=device, generator=g) / K ** 0.5).half()
+        dead = torch.from_numpy(dead_columns(K, sp, M + N, "random")).to(device)
+        x[:, dead] = 0
+        w_kn[dead, :] = 0
+        out[name] = (x, w_kn)
+    # Mask semantics cases: NaN handling (mask.py:55), the fp16 threshold
+    # boundary (fp32 compare, mask.py:53-58), an fp32 matrix, all-dead rows.
+    nan = torch.randn(64, 256, device=device, generator=g).half()
+    nan[:, :64] = 0
+    nan[5, 0] = float("nan")                     # NaN + zeros: dead
+    nan[7, 1] = float("nan")
+    nan[9, 1] = 0.5                              # NaN + a live value: alive
+    nan[:, 2] = float("nan")                     # all NaN: dead
+    bound = torch.zeros(16, 128, device=device).half()
+    bound[3, :64] = 1.0133e-06                   # just above 1e-6 in fp32, not in fp16
+    bound[4, 64:] = 9.5e-07
+    f32 = torch.randn(200, 320, device=device, generator=g)
+    f32[:, ::3] = 0
+    out["mask_nan"] = (nan, 1e-6)
+    out["mask_fp16_threshold_boundary"] = (bound, 1e-6)
+    out["mask_f32"] = (f32, 0.0)
+    return out
+
+
+def reference_triton_child(outdir: str) -> None:
+    """Runs in a separate process: the unmodified reference package from baseline/_ref.
+
+    This repository also holds a package under the reference's import name, so
+    the repository is taken off sys.path before the reference is imported.
+    Times dead_neuron_mask, gather_compact and ghostweight_matmul (CUDA events,
+    10 warm-up, 100 iterations) and saves their outputs for the comparison.
+    """
+    sys.path[:] = [p for p in sys.path if Path(p or ".").resolve() != REPO]
+    sys.path.insert(0, str(REF_DIR))
+    import triton
+
+    import ghostweight_triton as ref
+    from ghostweight_triton.kernels import dead_neuron_mask, gather_compact, ghostweight_matmul
+
+    assert Path(ref.__file__).resolve().is_relative_to(REF_DIR.resolve()), ref.__file__
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    inp = _ref_inputs(device)
+    res = {"triton": triton.__version__, "package": str(Path(ref.__file__).parent.relative_to(REPO)),
+           "ms": {}, "outputs": {}}
+    saved = {}
+    for name, (x, thr) in [(k, v) for k, v in inp.items() if k.startswith("mask_")]:
+        saved[name] = dead_neuron_mask(x, threshold=thr).cpu()
+    x, w_kn = inp["headline_4096x4096x4096_s50"]
+    res["ms"]["dead_neuron_mask_4096x4096_fp16"] = cuda_mean_ms(lambda: dead_neuron_mask(x, threshold=0.0))
+    m = dead_neuron_mask(x, threshold=0.0)
+    idx = torch.nonzero(m).squeeze(-1).to(torch.int64)
+    saved["mask_headline"] = m.cpu()
+    res["ms"]["gather_compact_4096x4096_s50_fp16"] = cuda_mean_ms(lambda: gather_compact(x, w_kn, idx))
+    a_c, w_c = gather_compact(x, w_kn, idx)
+    saved["gather_a"], saved["gather_w"] = a_c.cpu(), w_c.cpu()
+    for name, M, N, K, sp in REF_MATMUL_CASES:
+        x, w_kn = inp[name]
+        m = dead_neuron_mask(x, threshold=0.0)
+        idx = torch.nonzero(m).squeeze(-1).to(torch.int64)
+        res["ms"][f"ghostweight_matmul_{name}"] = cuda_mean_ms(lambda: ghostweight_matmul(x, w_kn, idx))
+        if M <= 1024:
+            saved[f"matmul_{name}"] = ghostweight_matmul(x, w_kn, idx).cpu()
+    torch.save(saved, Path(outdir) / "ref_outputs.pt")
+    (Path(outdir) / "ref_times.json").write_text(json.dumps(res))
+
+
+def reference_triton_record(timeout_s: float = 420.0) -> dict:
+    """The reference's own Triton kernels timed on this GPU beside ours, outputs compared.
+
+    Both sides run the same calls through the same Python surface
+    (dead_neuron_mask, gather_compact, ghostweight_matmul) on the same seeded
+    inputs; speed-up = reference time / our time. Masks and alive lists must
+    be bit-identical (a NaN column and the fp16 threshold boundary included),
+    gathers identical, matmul outputs within 1e-2.
+    """
+    import tempfile
+
+    if not (REF_DIR / "ghostweight_triton" / "__init__.py").exists():
+        return {"unavailable": "reference package not installed under baseline/_ref"}
+    from ghostweight_triton_b200.kernels import dead_neuron_mask, gather_compact, ghostweight_matmul
+
+    with tempfile.TemporaryDirectory() as td:
+        env = dict(os.environ)
+        env.pop("PYTHONPATH", None)
+        try:
+            proc = subprocess.run([sys.executable, str(REPO / "bench.py"), "--reference-triton-child", td],
+                                  cwd=td, env=env, capture_output=True, text=True, timeout=timeout_s)
+        except subprocess.TimeoutExpired:
+            return {"unavailable": f"reference child did not finish in {timeout_s:.0f} s"}
+        if proc.returncode != 0:
+            return {"unavailable": "reference child failed: " + proc.stderr.strip().splitlines()[-1][:300]
+                    if proc.stderr.strip() else f"reference child exit {proc.returncode}"}
+        ref = json.loads((Path(td) / "ref_times.json").read_text())
+        outs = torch.load(Path(td) / "ref_outputs.pt")
+    device = torch.device("cuda", torch.cuda.current_device())
+    inp = _ref_inputs(device)
+    parity = {}
+    for name in [k for k in inp if k.startswith("mask_")]:
+        x, thr = inp[name]
+        parity[name] = bool(torch.equal(dead_neuron_mask(x, threshold=thr).cpu(), outs[name]))
+    ours = {}
+    x, w_kn = inp["headline_4096x4096x4096_s50"]
+    ours["dead_neuron_mask_4096x4096_fp16"] = cuda_mean_ms(lambda: dead_neuron_mask(x, threshold=0.0))
+    m = dead_neuron_mask(x, threshold=0.0)
+    parity["mask_headline"] = bool(torch.equal(m.cpu(), outs["mask_headline"]))
+    idx = torch.nonzero(m).squeeze(-1).to(torch.int64)
+    ours["gather_compact_4096x4096_s50_fp16"] = cuda_mean_ms(lambda: gather_compact(x, w_kn, idx))
+    a_c, w_c = gather_compact(x, w_kn, idx)
+    parity["gather_compact"] = bool(torch.equal(a_c.cpu(), outs["gather_a"]) and
+                                    torch.equal(w_c.cpu(), outs["gather_w"]))
+    worst = 0.0
+    for name, M, N, K, sp in REF_MATMUL_CASES:
+        x, w_kn = inp[name]
+        idx = torch.nonzero(dead_neuron_mask(x, threshold=0.0)).squeeze(-1).to(torch.int64)
+        ours[f"ghostweight_matmul_{name}"] = cuda_mean_ms(lambda: ghostweight_matmul(x, w_kn, idx))
+        key = f"matmul_{name}"
+        if key in outs:
+            y = ghostweight_matmul(x, w_kn, idx).float().cpu()
+            r = outs[key].float()
+            worst = max(worst, float(((y - r).abs() - (1e-2 + 1e-2 * r.abs())).max()))
+    parity["matmul_max_excess_vs_reference"] = round(worst, 6)
+    parity["native_parity"] = all(v for k, v in parity.items() if isinstance(v, bool)) and worst <= 0.0
+    kernels = {}
+    for k, t_ref in ref["ms"].items():
+        t_ours = ours.get(k)
+        kernels[k] = {"reference_ms": round(t_ref, 5), "ours_ms": round(t_ours, 5) if t_ours else None,
+                      "speedup": round(t_ref / t_ours, 3) if t_ours else None}
+    return {"what": "the reference's Triton kernels (unmodified, baseline/_ref) JIT-compiled on this GPU, "
+                    "and ours, through the same Python calls; CUDA events, 10 warm-up + 100 iterations, mean",
+            "triton": ref["triton"], "kernels": kernels, "parity": parity,
+            "native_parity": parity["native_parity"],
+            "note": "ghostweight_matmul takes W as [K, N] per call on both sides, so ours packs W' "
+                    "(the transposing gather) inside every call; a GhostLinear packs it once"}
 
 
 # ---------------------------------------------------------------------------- ours: headline GEMM
@@ -530,10 +707,20 @@ def run_ours(args, world, rank, local):
 
     extra = {}
     cpu = None
+    del layers
+    torch.cuda.empty_cache()
+    # The sharded MLP projection at this job's GPU count (every rank takes part).
+    if not args.no_sharded:
+        extra["sharded"] = sharded_record(args, world, rank, peaks, peak_src)
     if rank == 0 and world == 1:
         if not args.no_sweep:
             extra["sweep"] = sweep(device, peaks)
             extra["kernels"] = kernel_metrics(device, peaks)
+        if not args.no_models:
+            extra["models"] = {w: model_record(w, args.steps, args.warmup, world, rank, full=False)
+                               for w in ("gpt2", "distilbert")}
+        if not args.no_reference_triton:
+            extra["reference_triton"] = reference_triton_record()
         if not args.no_cpu_baseline:
             r = cpu_reference_sample(M, N, K, cfg["sparsity"], cfg["pattern"], rows=256,
                                      budget_s=15.0, max_reps=50)
@@ -583,76 +770,138 @@ def run_ours(args, world, rank, local):
 
 
 # ---------------------------------------------------------------------------- ours: sharded MLP
-def run_mlp_sharded(args, world, rank, local):
+def sharded_parity(layer, x: torch.Tensor, y_full: torch.Tensor, rows: torch.Tensor, world: int) -> float:
+    """How far sampled rows of a gathered [M, N] output are outside the output contract.
+
+    Every rank computes the fp32 product of the sampled rows of x with its own
+    weight rows, the blocks are all-gathered, and each rank compares the rows
+    of its own full output with them: |y - r| <= 1e-2 + 1e-2 |r|, r the fp32
+    product rounded to y's dtype. Returns the largest excess over all ranks
+    (<= 0 passes).
+    """
+    n_real = layer.row_stop - layer.row_start
+    ref_local = torch.zeros(rows.numel(), layer.n_local, dtype=torch.float32, device=x.device)
+    ref_local[:, :n_real] = x[rows].float() @ layer.weight[:n_real].float().t()
+    if layer.bias is not None:
+        ref_local[:, :n_real] += layer.bias[:n_real].float()
+    if world > 1:
+        import torch.distributed as dist
+
+        parts = torch.empty(world, rows.numel(), layer.n_local, dtype=torch.float32, device=x.device)
+        dist.all_gather_into_tensor(parts, ref_local)
+        ref = parts.permute(1, 0, 2).reshape(rows.numel(), world * layer.n_local)[:, :layer.out_features]
+    else:
+        ref = ref_local[:, :layer.out_features]
+    r = ref.to(y_full.dtype).float()
+    excess = ((y_full[rows].float() - r).abs() - (1e-2 + 1e-2 * r.abs())).max().item()
+    return max_over_ranks(excess, world)
+
+
+def sharded_record(args, world: int, rank: int, peaks: dict, peak_src: str) -> dict:
+    """The sharded MLP projection, column-parallel over the job's GPUs.
+
+    x [8192, 8192] bf16 ~ N(0, 1); W [28672, 8192] ~ N(0, 1/sqrt(K)) pre-sharded
+    by output features (each rank draws only its rows) with 70% of the
+    128-column blocks of input columns dead (seeded), K' = 2560. Times, max
+    over ranks: the GEMM alone (this rank's columns), the full output on every
+    rank through the GEMM whose epilogue stores each tile into all ranks'
+    outputs over NVLink, and the same through NCCL all-gather + re-layout. The
+    output of both full-output paths is checked in the run (sampled rows on
+    every rank against the fp32 product, 1e-2 contract).
+    """
     from ghostweight_triton_b200.sharded import ColumnParallelGhostLinear
 
     device = torch.device("cuda", torch.cuda.current_device())
-    peaks, peak_src = load_peaks()
     cfg = MLP
     M, N, K = cfg["M"], cfg["N"], cfg["K"]
-    g = torch.Generator(device=device).manual_seed(5)
+    g = torch.Generator(device=device).manual_seed(5)          # the same x on every rank
     x = torch.randn(M, K, device=device, generator=g).to(torch.bfloat16)
     layer = ColumnParallelGhostLinear.from_full_weight_seed(
         N, K, seed=5, dead=dead_columns(K, cfg["sparsity"], 5, cfg["pattern"]),
         dtype=torch.bfloat16, device=device)
     kp = layer.k_alive
     useful = 2.0 * M * N * kp
+    steps = max(1, args.steps)
+    rows = torch.from_numpy(np.sort(np.random.default_rng(17).choice(M, 64, replace=False))).to(device)
 
     def step_gemm(i):
         layer.local_forward(x)
 
     def step_nccl(i):
         layer.gather_output = True
-        layer(x)
+        return layer(x)
 
     def step_peers(i):
         layer.gather_output = "peers"
-        layer(x)
+        return layer(x)
 
     for i in range(args.warmup):
+        step_gemm(i)
         step_nccl(i)
         if world > 1:
             step_peers(i)
-    t_gemm = timed(step_gemm, args.steps, world)
-    t_nccl = timed(step_nccl, args.steps, world)
-    t_peers = timed(step_peers, args.steps, world) if world > 1 else t_nccl
+    t_gemm = timed(step_gemm, steps, world) / steps
+    t_nccl = timed(step_nccl, steps, world) / steps
+    t_peers = timed(step_peers, steps, world) / steps if world > 1 else None
+    parity = {"rows_checked_per_rank": int(rows.numel()), "contract": "atol = rtol = 1e-2 vs fp32 rounded to bf16"}
+    parity["nccl_max_excess"] = round(sharded_parity(layer, x, step_nccl(0), rows, world), 6)
+    if world > 1:
+        y = step_peers(0)
+        parity["peers_max_excess"] = round(sharded_parity(layer, x, y, rows, world), 6)
+    parity["ok"] = all(v <= 0.0 for k, v in parity.items() if k.endswith("_excess"))
     layer.close()
-    t_full = min(t_nccl, t_peers)
-    # Roofline of the step: the slower of the tensor work per GPU and the bytes
-    # each GPU must receive over NVLink ((world-1)/world of y), at the measured
-    # peer-copy bandwidth of 770 GB/s per direction.
-    per = t_full / args.steps
+    strategy = layer.strategy
+    del layer, x
+    torch.cuda.empty_cache()
+
+    t_full = min(t_nccl, t_peers) if t_peers is not None else t_nccl
+    recv_bytes = (world - 1) / world * M * N * 2        # bytes of y each GPU receives
     t_flop = useful / world / (float(peaks["bf16_tflops"]) * 1e12)
-    link_bytes = (world - 1) / world * M * N * 2
-    t_link = link_bytes / 770e9
-    roof = {"bound": "nvlink" if t_link > t_flop else "tensor",
-            "achieved": round((link_bytes / per / 1e9) if t_link > t_flop else (useful / world / per / 1e12), 2),
-            "peak": 770.0 if t_link > t_flop else float(peaks["bf16_tflops"]),
-            "unit": "GB/s" if t_link > t_flop else "TFLOP/s",
-            "frac": round(max(t_link, t_flop) / per, 4), "traffic": None,
-            "peak_source": ("measured peer copy, 770 GB/s per direction" if t_link > t_flop
-                            else f"{peak_src} bf16_tflops")}
+    t_link = recv_bytes / 770e9
+    bound = "nvlink" if t_link > t_flop else "tensor"
+    return {
+        "workload": "sharded MLP projection x[8192,8192] W[28672,8192] bf16, 70% dead 128-col blocks",
+        "K_alive": kp, "n_gpus": world, "scaling": "strong", "strategy": strategy,
+        "parallelism": f"column-parallel N over {world} GPU(s), full output on every rank",
+        "gemm_only_ms": round(t_gemm * 1e3, 4),
+        "gemm_only_tflops_per_gpu": round(useful / world / t_gemm / 1e12, 2),
+        "gemm_only_frac_of_peak": round(useful / world / t_gemm / 1e12 / float(peaks["bf16_tflops"]), 4),
+        "nccl_allgather_step_ms": round(t_nccl * 1e3, 4),
+        "peer_fused_step_ms": round(t_peers * 1e3, 4) if t_peers is not None else None,
+        "full_output_step_ms": round(t_full * 1e3, 4),
+        "full_output_tflops": round(useful / t_full / 1e12, 2),
+        "full_output_tflops_per_gpu": round(useful / world / t_full / 1e12, 2),
+        "bytes_received_per_gpu": int(recv_bytes),
+        "step_bound": bound,
+        "frac_of_step_bound": round(max(t_link, t_flop) / t_full, 4),
+        "link_bound_note": "slower of tensor work per GPU (measured bf16 peak) and (world-1)/world of y "
+                           "received per GPU at the measured 770 GB/s peer copy",
+        "gathered_by": ("GEMM epilogue peer stores over NVLink (CUDA IPC)"
+                        if t_peers is not None and t_peers <= t_nccl else
+                        ("NCCL all-gather + re-layout" if world > 1 else "nothing to gather (one GPU)")),
+        "parity": parity, "peak_source": peak_src,
+    }
+
+
+def run_mlp_sharded(args, world, rank, local):
+    peaks, peak_src = load_peaks()
+    rec = sharded_record(args, world, rank, peaks, peak_src)
     if rank == 0:
+        per = rec["full_output_step_ms"] * 1e-3
         line = {
-            "metric": METRIC, "value": round(useful / per / 1e12, 3), "unit": "TFLOP/s",
+            "metric": METRIC, "value": rec["full_output_tflops"], "unit": "TFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(per * 1e3, 4), "higher_is_better": True, "scaling": "strong",
+            "ms_per_step": rec["full_output_step_ms"], "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic, seeded",
-            "config": {"workload": "sharded MLP projection x[8192,8192] W[28672,8192] bf16, 70% dead 128-col blocks",
-                       "K_alive": kp, "parallelism": f"column-parallel N over {world} GPUs, full output on every rank",
-                       "strategy": layer.strategy},
-            "gather": ("GEMM epilogue stores every tile into all ranks' outputs over NVLink (CUDA IPC)"
-                       if world > 1 and t_peers <= t_nccl else "NCCL all-gather + re-layout"),
-            "peer_fused_ms": round(t_peers / args.steps * 1e3, 4) if world > 1 else None,
-            "nccl_allgather_ms": round(t_nccl / args.steps * 1e3, 4),
-            "gemm_only_tflops": round(useful / (t_gemm / args.steps) / 1e12, 3),
-            "gemm_only_ms": round(t_gemm / args.steps * 1e3, 4),
-            "roofline": roof,
-            "gemm_roofline": {"bound": "tensor", "achieved": round(useful / world / (t_gemm / args.steps) / 1e12, 2),
-                              "peak": float(peaks["bf16_tflops"]), "unit": "TFLOP/s",
-                              "frac": round(useful / world / (t_gemm / args.steps) / 1e12 / float(peaks["bf16_tflops"]), 4),
-                              "peak_source": peak_src},
-            "gpu_launches": (1 if layer.strategy == "runs" else 2) * args.steps,
+            "config": {"workload": rec["workload"], "K_alive": rec["K_alive"],
+                       "parallelism": rec["parallelism"], "strategy": rec["strategy"]},
+            "sharded": rec,
+            "roofline": {"bound": rec["step_bound"], "frac": rec["frac_of_step_bound"],
+                         "achieved": rec["full_output_tflops_per_gpu"], "unit": "TFLOP/s per GPU",
+                         "peak": float(peaks["bf16_tflops"]), "traffic": None,
+                         "peak_source": f"{peak_src} bf16_tflops; link bound 770 GB/s"},
+            "gpu_launches": (1 if rec["strategy"] == "runs" else 2) * args.steps,
+            "ms_per_step_note": f"full output on every rank, {per * 1e3:.4f} ms",
         }
         print(json.dumps(line), flush=True)
 
@@ -1039,10 +1288,20 @@ def build_model(which: str, device, seed: int = 0):
     return model.half().to(device).eval()
 
 
-def run_model(args, world, rank, local, which: str):
+def model_record(which: str, steps: int, warmup: int, world: int, rank: int, full: bool = True) -> dict:
+    """Tokens/s of the random-init model with every projection rewritten, next to the dense model.
+
+    Drop-in (``replace_linears``, masks frozen from the weights), eager and
+    replayed from a CUDA graph, and with the MLP blocks fused
+    (``fuse_mlp_chains``), against the same dense fp16 model on the same GPU;
+    relative error of the final hidden state against the dense model. With
+    full=True also the end-to-end forward with token ids from pinned host
+    memory and the hidden state copied back.
+    """
     import copy
 
     from ghostweight_triton_b200 import replace_linears
+    from ghostweight_triton_b200.fuse import fuse_mlp_chains
 
     device = torch.device("cuda", torch.cuda.current_device())
     cfg = MODELS[which]
@@ -1061,77 +1320,87 @@ def run_model(args, world, rank, local, which: str):
         with torch.no_grad():
             return model(input_ids=ids[i % 2], **kwargs).last_hidden_state
 
-    for i in range(args.warmup):
+    for i in range(warmup):
         fwd(ghost, i)
         fwd(dense, i)
-    steps = max(1, min(args.steps, 50))
+    steps = max(1, min(steps, 50))
     t = timed(lambda i: fwd(ghost, i), steps, world) / steps
     t_dense = timed(lambda i: fwd(dense, i), steps, world) / steps
     with torch.no_grad():
-        a = fwd(ghost, 0).float()
-        b = fwd(dense, 0).float()
-        rel = float(((a - b).norm() / b.norm()).item())
+        ref = fwd(dense, 0).float()
+        rel = float(((fwd(ghost, 0).float() - ref).norm() / ref.norm()).item())
     # The same forwards captured in CUDA graphs: no per-call host overhead.
     t_graph = graph_time(lambda: fwd(ghost, 0), steps, world)
     t_graph_dense = graph_time(lambda: fwd(dense, 0), steps, world)
-    # Extension: MLP blocks fused (the first projection computes only the second's
-    # alive features, written compacted; no gather before the second).
-    from ghostweight_triton_b200.fuse import fuse_mlp_chains
-
+    # MLP blocks fused (the first projection computes only the second's alive
+    # features, written compacted; no gather before the second).
     fused = copy.deepcopy(ghost)
     n_fused = len(fuse_mlp_chains(fused))
-    for i in range(args.warmup):
+    for i in range(warmup):
         fwd(fused, i)
     t_graph_fused = graph_time(lambda: fwd(fused, 0), steps, world)
     with torch.no_grad():
-        c = fwd(fused, 0).float()
-        rel_fused = float(((c - fwd(dense, 0).float()).norm() / fwd(dense, 0).float().norm()).item())
+        rel_fused = float(((fwd(fused, 0).float() - ref).norm() / ref.norm()).item())
     del fused
     # Linear-layer FLOPs of one forward over the alive columns (what the kernels compute).
     useful = 0.0
     for mod in ghost.modules():
         if mod.__class__.__name__ == "GhostLinear" and mod.mask_frozen:
             useful += 2.0 * tokens * mod.out_features * mod._frozen_indices.numel()
-    hids = [x.cpu().pin_memory() for x in ids]
-    hout = torch.empty(cfg["batch"], cfg["seq"], 768, dtype=torch.float16).pin_memory()
+    rec = {
+        "metric": f"{which} {'prefill' if which == 'gpt2' else 'encoder'} tokens/s",
+        "workload": cfg["desc"], "tokens_per_step": tokens, "layers_replaced": len(replaced),
+        "tokens_per_s": round(world * tokens / t, 1), "ms_per_step": round(t * 1e3, 4),
+        "dense_tokens_per_s": round(world * tokens / t_dense, 1),
+        "speedup_vs_dense": round(t_dense / t, 3),
+        "cuda_graph": {"tokens_per_s": round(world * tokens / t_graph, 1),
+                       "dense_tokens_per_s": round(world * tokens / t_graph_dense, 1),
+                       "speedup_vs_dense": round(t_graph_dense / t_graph, 3),
+                       "ms_per_step": round(t_graph * 1e3, 4)},
+        "mlp_chains_fused": {"blocks": n_fused, "tokens_per_s": round(world * tokens / t_graph_fused, 1),
+                             "speedup_vs_dense": round(t_graph_dense / t_graph_fused, 3),
+                             "ms_per_step": round(t_graph_fused * 1e3, 4),
+                             "rel_err_vs_dense_model": rel_fused, "timing": "CUDA graph, as cuda_graph"},
+        "linear_useful_tflops": round(useful / t / 1e12, 2),
+        "rel_err_vs_dense_model": rel,
+        "steps": steps,
+        # Each frozen GhostLinear forward: the x' gather and the GEMM (or the GEMM alone).
+        "gpu_launches_per_step_at_most": 2 * len(replaced),
+    }
+    if full:
+        hids = [x.cpu().pin_memory() for x in ids]
+        hout = torch.empty(cfg["batch"], cfg["seq"], 768, dtype=torch.float16).pin_memory()
 
-    def e2e_step(i):
-        with torch.no_grad():
-            out = ghost(input_ids=hids[i % 2].to(device, non_blocking=True), **kwargs).last_hidden_state
-        hout.copy_(out, non_blocking=True)
+        def e2e_step(i):
+            with torch.no_grad():
+                out = ghost(input_ids=hids[i % 2].to(device, non_blocking=True), **kwargs).last_hidden_state
+            hout.copy_(out, non_blocking=True)
 
-    for i in range(2):
-        e2e_step(i)
-    te = timed(e2e_step, steps, world) / steps
+        for i in range(2):
+            e2e_step(i)
+        te = timed(e2e_step, steps, world) / steps
+        rec["e2e"] = {"value": round(world * tokens / te, 1), "unit": "tokens/s",
+                      "h2d_bytes_per_step": tokens * 8, "d2h_bytes_per_step": tokens * 768 * 2,
+                      "ms_per_step": round(te * 1e3, 4)}
+    del ghost, dense
+    torch.cuda.empty_cache()
+    return rec
+
+
+def run_model(args, world, rank, local, which: str):
+    rec = model_record(which, args.steps, args.warmup, world, rank, full=True)
     if rank == 0:
         cpu = cpu_model_sample(which)
         line = {
-            "metric": f"{which} {'prefill' if which == 'gpt2' else 'encoder'} tokens/s",
-            "value": round(world * tokens / t, 1), "unit": "tokens/s", "n_gpus": world,
-            "steps": steps, "warmup": args.warmup, "ms_per_step": round(t * 1e3, 4),
+            "metric": rec["metric"], "value": rec["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
+            "steps": rec["steps"], "warmup": args.warmup, "ms_per_step": rec["ms_per_step"],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
             "data": "synthetic: random-init weights, token ids uniform in [0, vocab)",
-            "config": {"workload": cfg["desc"], "tokens_per_step": tokens,
-                       "layers_replaced": len(replaced), "parallelism": f"independent batches x{world}"},
-            "dense_tokens_per_s": round(world * tokens / t_dense, 1),
-            "speedup_vs_dense": round(t_dense / t, 3),
-            "cuda_graph": {"tokens_per_s": round(world * tokens / t_graph, 1),
-                           "dense_tokens_per_s": round(world * tokens / t_graph_dense, 1),
-                           "speedup_vs_dense": round(t_graph_dense / t_graph, 3),
-                           "ms_per_step": round(t_graph * 1e3, 4)},
-            "mlp_chains_fused": {"blocks": n_fused, "tokens_per_s": round(world * tokens / t_graph_fused, 1),
-                                 "speedup_vs_dense": round(t_graph_dense / t_graph_fused, 3),
-                                 "ms_per_step": round(t_graph_fused * 1e3, 4),
-                                 "rel_err_vs_dense_model": rel_fused,
-                                 "timing": "CUDA graph, as cuda_graph"},
-            "linear_useful_tflops": round(useful / t / 1e12, 2),
-            "rel_err_vs_dense_model": rel,
-            "cpu_baseline": cpu,
-            "e2e": {"value": round(world * tokens / te, 1), "unit": "tokens/s",
-                    "h2d_bytes_per_step": tokens * 8, "d2h_bytes_per_step": tokens * 768 * 2,
-                    "ms_per_step": round(te * 1e3, 4)},
-            # Each frozen GhostLinear forward: the x' gather and the GEMM.
-            "gpu_launches": 2 * len(replaced) * steps,
+            "config": {"workload": rec["workload"], "tokens_per_step": rec["tokens_per_step"],
+                       "layers_replaced": rec["layers_replaced"], "parallelism": f"independent batches x{world}"},
+            "cpu_baseline": cpu, "e2e": rec["e2e"],
+            "gpu_launches": rec["gpu_launches_per_step_at_most"] * rec["steps"],
+            **{k: v for k, v in rec.items() if k not in ("e2e", "metric", "workload", "steps")},
         }
         print(json.dumps(line), flush=True)
 
@@ -1191,7 +1460,15 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-soak", action="store_true",
                     help="skip the 1 s clock-sampling soak (for short profiler runs)")
+    ap.add_argument("--no-sharded", action="store_true", help="skip the sharded MLP sub-record")
+    ap.add_argument("--no-models", action="store_true", help="skip the GPT-2 / DistilBERT sub-record")
+    ap.add_argument("--no-reference-triton", action="store_true",
+                    help="skip timing the reference's Triton kernels")
+    ap.add_argument("--reference-triton-child", metavar="DIR", default=None, help=argparse.SUPPRESS)
     args = ap.parse_args()
+    if args.reference_triton_child:
+        reference_triton_child(args.reference_triton_child)
+        return
     args.warmup = max(3, args.warmup)
     world, rank, local = dist_setup(args)
     try:
