@@ -440,7 +440,7 @@ def reference_triton_record(timeout_s: float = 420.0) -> dict:
     a_c, w_c = gather_compact(x, w_kn, idx)
     parity["gather_compact"] = bool(torch.equal(a_c.cpu(), outs["gather_a"]) and
                                     torch.equal(w_c.cpu(), outs["gather_w"]))
-    worst = 0.0
+    worst = -float("inf")
     for name, M, N, K, sp in REF_MATMUL_CASES:
         x, w_kn = inp[name]
         idx = torch.nonzero(dead_neuron_mask(x, threshold=0.0)).squeeze(-1).to(torch.int64)
@@ -596,8 +596,7 @@ def run_ours(args, world, rank, local):
     ws = torch.empty(_native.gather_gemm_workspace_bytes(M, kp, torch.float16), dtype=torch.uint8,
                      device=device)
     ldp = (kp + 63) // 64 * 64
-    hdr = (((kp + 63) // 64) * 4 + 255) // 256 * 256
-    xg = ws[hdr: hdr + M * ldp * 2].view(torch.float16).view(M, ldp)[:, :kp]
+    xg = torch.empty(M, ldp, dtype=torch.float16, device=device)[:, :kp]   # x' for the kernels timed alone
 
     def step(i):
         L = layers[i % N_SETS]

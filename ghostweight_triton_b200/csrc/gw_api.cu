@@ -311,12 +311,11 @@ int gw_gather_rows_t(const void* src, int dtype, int64_t rows, int64_t cols, int
 }
 
 namespace {
-// GEMM workspace layout: [k-block ready counters, 256-aligned][x' = M x ldp, 16-bit]
+// GEMM workspace layout: [header: the in-kernel gather's epoch, claim counters
+// and unit flags, 256-aligned][x' = M x ldp, 16-bit]. Its contents on entry
+// do not matter (the overlap strategy tags its flags with a call number).
 int64_t gemm_ld_pad(int64_t n_alive) { return (n_alive + 63) / 64 * 64; }
-size_t gemm_ws_header(int64_t n_alive) {
-  const size_t kb = static_cast<size_t>((n_alive + 63) / 64);
-  return (kb * sizeof(unsigned int) + 255) / 256 * 256;
-}
+size_t gemm_ws_header(int64_t M, int64_t n_alive) { return gw::tc2_gather_header_bytes(M, n_alive); }
 }  // namespace
 
 int gw_gather_rows_t_dev(const void* src, int dtype, int64_t rows, int64_t cols, int64_t ld_src,
@@ -396,8 +395,7 @@ cudaError_t launch_dense_gemm(const void* a, int dtype, int64_t M, int64_t K, in
                                d->err_word, s, a_cols, a_width);
   else
     e = gw::launch_gemm_tc(0, a, dtype, M, a_cols ? a_width : K, lda, w, N, ldw, nullptr, K, bias,
-                           epilogue, y, ldy, d->err_word, d->sm_count, s, nullptr, 0, nullptr,
-                           a_cols);
+                           epilogue, y, ldy, d->err_word, d->sm_count, s, a_cols);
   if (e != cudaSuccess || n_peers == 0) return e;
   return gw::launch_copy_to_peers(y, M, N, ldy, peers, n_peers, d->sm_count, s);
 }
@@ -405,7 +403,7 @@ cudaError_t launch_dense_gemm(const void* a, int dtype, int64_t M, int64_t K, in
 
 size_t gw_gather_gemm_workspace_bytes(int64_t M, int64_t n_alive, int dtype) {
   if (M <= 0 || n_alive <= 0 || dtype == GW_DTYPE_F32) return 0;
-  return gemm_ws_header(n_alive) +
+  return gemm_ws_header(M, n_alive) +
          static_cast<size_t>((M * gemm_ld_pad(n_alive) * 2 + 255) / 256 * 256);
 }
 
@@ -473,18 +471,28 @@ int gw_gather_gemm(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
   if (!ws_ok) return GW_ERR_WORKSPACE;
   if (!aligned16(workspace)) return GW_ERR_ALIGN;
   const int64_t ldp = gemm_ld_pad(n_alive);
-  unsigned int* counters = static_cast<unsigned int*>(workspace);
-  void* xg = static_cast<char*>(workspace) + gemm_ws_header(n_alive);
-  if (strat == GW_GEMM_PREGATHER) {
-    e = gw::launch_gather_columns(x, dtype, M, ldx, K, idx, n_alive, xg, ldp, n_alive,
-                                  d->err_word, d->sm_count, s, true);
-    if (e != cudaSuccess) return cuda_fail(e);
-    e = launch_dense_gemm(xg, dtype, M, n_alive, ldp, w_packed, N, ldw, bias, epilogue, y, ldy,
-                          d, s);
-  } else {
-    e = gw::launch_gemm_tc(2, x, dtype, M, K, ldx, w_packed, N, ldw, idx, n_alive, bias,
-                           epilogue, y, ldy, d->err_word, d->sm_count, s, xg, ldp, counters);
+  void* xg = static_cast<char*>(workspace) + gemm_ws_header(M, n_alive);
+  if (strat == GW_GEMM_OVERLAP && gw::use_pair_gemm(M, N, d->sm_count) &&
+      gw::tc2_gather_supported(M, n_alive)) {
+    // One launch: the pair kernel gathers x' into the workspace while its MMAs
+    // consume the finished units.
+    gw::Tc2Gather g;
+    g.x = x;
+    g.ldx = ldx;
+    g.K = K;
+    g.idx = idx;
+    g.xg = xg;
+    g.ldp = ldp;
+    g.header = workspace;
+    e = gw::launch_gemm_tc2(xg, dtype, M, n_alive, ldp, w_packed, N, ldw, bias, epilogue, y, ldy,
+                            d->err_word, d->sm_count, s, nullptr, 0, nullptr, 0, nullptr, &g);
+    return e == cudaSuccess ? GW_OK : cuda_fail(e);
   }
+  // Pregather (also the overlap strategy's shapes that do not run on CTA pairs).
+  e = gw::launch_gather_columns(x, dtype, M, ldx, K, idx, n_alive, xg, ldp, n_alive,
+                                d->err_word, d->sm_count, s, true);
+  if (e != cudaSuccess) return cuda_fail(e);
+  e = launch_dense_gemm(xg, dtype, M, n_alive, ldp, w_packed, N, ldw, bias, epilogue, y, ldy, d, s);
   return e == cudaSuccess ? GW_OK : cuda_fail(e);
 }
 
@@ -524,7 +532,7 @@ int gw_gather_gemm_dev(const void* x, int dtype, int64_t M, int64_t K, int64_t l
   if (!workspace) return GW_ERR_NULL;
   if (workspace_bytes < gw_gather_gemm_workspace_bytes(M, n_alive_max, dtype)) return GW_ERR_WORKSPACE;
   if (!aligned16(workspace)) return GW_ERR_ALIGN;
-  void* xg = static_cast<char*>(workspace) + gemm_ws_header(n_alive_max);
+  void* xg = static_cast<char*>(workspace) + gemm_ws_header(M, n_alive_max);
   e = gw::launch_gather_columns(x, dtype, M, ldx, K, idx, n_alive_max, xg, ldp, ldp, d->err_word,
                                 d->sm_count, s, true, n_alive_dev);
   if (e != cudaSuccess) return cuda_fail(e);
@@ -535,8 +543,7 @@ int gw_gather_gemm_dev(const void* x, int dtype, int64_t M, int64_t K, int64_t l
                             d->err_word, d->sm_count, s, nullptr, 0, nullptr, 0, n_alive_dev);
   else
     e = gw::launch_gemm_tc(0, xg, dtype, M, ldp, ldp, w_packed, N, ldw, nullptr, ldp, bias,
-                           epilogue, y, ldy, d->err_word, d->sm_count, s, nullptr, 0, nullptr,
-                           nullptr, n_alive_dev);
+                           epilogue, y, ldy, d->err_word, d->sm_count, s, nullptr, n_alive_dev);
   return e == cudaSuccess ? GW_OK : cuda_fail(e);
 }
 
@@ -584,7 +591,7 @@ int gw_gather_gemm_peers(const void* x, int dtype, int64_t M, int64_t K, int64_t
   if (workspace_bytes < gw_gather_gemm_workspace_bytes(M, n_alive, dtype)) return GW_ERR_WORKSPACE;
   if (!aligned16(workspace)) return GW_ERR_ALIGN;
   const int64_t ldp = gemm_ld_pad(n_alive);
-  void* xg = static_cast<char*>(workspace) + gemm_ws_header(n_alive);
+  void* xg = static_cast<char*>(workspace) + gemm_ws_header(M, n_alive);
   e = gw::launch_gather_columns(x, dtype, M, ldx, K, idx, n_alive, xg, ldp, n_alive,
                                 d->err_word, d->sm_count, s, true);
   if (e != cudaSuccess) return cuda_fail(e);

@@ -14,19 +14,12 @@
 //   * warp 1      : TMEM allocator and the single-thread tcgen05.mma issuer
 //                   (128 x BN x 16 per instruction, 4 per k-block), commits
 //                   free smem stages and publish finished accumulators;
-//   * warps 2..9  : A-operand gather, in one of two modes --
-//       SMEM    : two groups of four warps take alternate k-blocks; a warp
-//                 loads 32 rows x 64 alive columns of x straight from global
-//                 memory (lane <-> alive column), waits for the stage to be
-//                 free and writes the values into the 128B-swizzled K-major
-//                 shared-memory layout tcgen05 reads (no scratch, one launch);
-//       OVERLAP : the eight warps of every CTA cooperatively gather x[:, alive]
-//                 into a dense scratch matrix x' (k-block-major order over all
-//                 CTAs, 128 rows x 64 columns per unit) and publish a per-k-block
-//                 ready counter; the TMA warp waits for a k-block's counter the
-//                 first time it needs it and then streams x' like a dense
-//                 operand. The gather runs concurrently with the MMAs; the
-//                 launch is cooperative so every CTA is resident;
+//   * warps 2..9  : A-operand gather (SMEM mode): two groups of four warps
+//                   take alternate k-blocks; a warp loads 32 rows x 64 alive
+//                   columns of x straight from global memory (lane <-> alive
+//                   column), waits for the stage to be free and writes the
+//                   values into the 128B-swizzled K-major shared-memory layout
+//                   tcgen05 reads (no scratch, one launch);
 //   * warps 10..13: epilogue -- tcgen05.ld of the fp32 accumulator (one TMEM
 //                   lane per output row), bias, optional GELU, one rounding to
 //                   the output type, 16-byte stores;
@@ -65,7 +58,6 @@ template <int AMODE> constexpr int epi_warps() { return AMODE == 0 ? 8 : 4; }
 // How the A operand (x[:, alive]) reaches shared memory.
 constexpr int kATma = 0;        // dense [M, K'] matrix by TMA (already compacted)
 constexpr int kASmemGather = 1; // producer warps gather into shared memory
-constexpr int kAOverlap = 2;    // in-kernel cooperative gather to scratch, then TMA
 
 constexpr int pow2_at_least(int v) { int p = 32; while (p < v) p <<= 1; return p; }
 
@@ -100,9 +92,6 @@ struct TcParams {
   int n_tiles;
   int num_tiles;
   unsigned int* err;
-  uint16_t* xg;                 // kAOverlap: scratch x' [M, ldg]
-  int64_t ldg;
-  unsigned int* kb_ready;       // kAOverlap: per-k-block count of gathered 128-row units
   const int64_t* a_cols;        // kATma: k-block kb of A starts at x column a_cols[64 kb] (or null)
   const int32_t* k_dev;         // kATma: K' on the device (num_kb an upper bound; see device_num_kb)
 };
@@ -170,7 +159,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
       if (AMODE == kATma) asm volatile("griddepcontrol.wait;" ::: "memory");
       const int num_kb = (AMODE == kATma && p.k_dev) ? device_num_kb(p.k_dev, p.num_kb) : p.num_kb;
       uint32_t it = 0;
-      int ready_kb = 0;   // kAOverlap: k-blocks of x' known to be complete
       bool ok = true;
       const int64_t* a_cols = AMODE == kATma ? p.a_cols : nullptr;
       int64_t nxt = a_cols ? run_start_load(a_cols, 0) : 0;   // next k-block's run start
@@ -182,15 +170,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
           const uint32_t ph = (it / C::kStages) & 1u;
           const int64_t cur = nxt;
           if (a_cols) nxt = run_start_load(a_cols, kb + 1 == num_kb ? 0 : kb + 1);
-          if (AMODE == kAOverlap && ready_kb <= kb) {
-            while (ready_kb <= kb) {
-              if (!wait_counter_geq(p.kb_ready + ready_kb, static_cast<uint32_t>(p.m_tiles),
-                                    abort_flag, p.err)) { ok = false; break; }
-              ++ready_kb;
-            }
-            if (!ok) break;
-            fence_proxy_async_global();   // generic-proxy writes of x' before our TMA reads
-          }
           if (!mbar_wait(empty(s), ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
           const uint32_t a_s = sbase + s * C::kStageBytes;
           const uint32_t b_s = a_s + C::kABytes;
@@ -256,70 +235,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b,
     __syncwarp();
   } else if (warp < (AMODE == kATma ? kWarpEpi0Dense : kWarpEpi0)) {
     // ------------------------------------------------------------ gather producers
-    if (AMODE == kAOverlap) {
-      // Cooperative gather of x[:, alive] -> x' in k-block-major unit order.
-      // A unit is 128 rows x 64 alive columns; each warp owns 16 of the rows and
-      // each lane two adjacent output columns (one 4-byte store per row). Two
-      // units are handled per iteration so 64 independent loads are in flight
-      // per thread. After the stores, every writer orders them for the async
-      // proxy, the eight warps meet at a named barrier, and one thread
-      // publishes the units with a release increment of their k-block counter.
-      const int gt = warp - kWarpGather0;                  // 0..7, 16 rows each
-      const int units = p.num_kb * p.m_tiles;
-      const int64_t step = p.ldg / 2;
-      bool bad = false;
-      for (int u0 = blockIdx.x; u0 < units; u0 += 2 * gridDim.x) {
-        uint32_t v[2][16];
-        int64_t row0[2];
-        int rows_here[2], kbu[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int u = u0 + h * gridDim.x;
-          const bool has = u < units;
-          const int kb = has ? u / p.m_tiles : 0;
-          const int m_blk = has ? u - kb * p.m_tiles : 0;
-          kbu[h] = has ? kb : -1;
-          const int64_t k0 = static_cast<int64_t>(kb) * kBK + 2 * lane;
-          int64_t c0 = -1, c1 = -1;
-          if (has && k0 < p.n_alive) {
-            c0 = __ldg(p.idx + k0);
-            if (c0 < 0 || c0 >= p.K) { bad = true; c0 = -1; }
-          }
-          if (has && k0 + 1 < p.n_alive) {
-            c1 = __ldg(p.idx + k0 + 1);
-            if (c1 < 0 || c1 >= p.K) { bad = true; c1 = -1; }
-          }
-          row0[h] = static_cast<int64_t>(m_blk) * kBM + gt * 16;
-          const int64_t rem = p.M - row0[h];
-          rows_here[h] = (!has || rem <= 0) ? 0 : (rem >= 16 ? 16 : static_cast<int>(rem));
-          const uint16_t* xr = p.x + (rows_here[h] > 0 ? row0[h] * p.ldx : 0);
-#pragma unroll
-          for (int r = 0; r < 16; ++r) {
-            const bool rv = r < rows_here[h];
-            const uint32_t lo = (rv && c0 >= 0) ? ld_stream_u16(xr + r * p.ldx + c0) : 0u;
-            const uint32_t hi = (rv && c1 >= 0) ? ld_stream_u16(xr + r * p.ldx + c1) : 0u;
-            v[h][r] = lo | (hi << 16);
-          }
-        }
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          if (rows_here[h] > 0) {
-            uint32_t* dst = reinterpret_cast<uint32_t*>(p.xg + row0[h] * p.ldg +
-                                                        static_cast<int64_t>(kbu[h]) * kBK) + lane;
-#pragma unroll
-            for (int r = 0; r < 16; ++r)
-              if (r < rows_here[h]) dst[r * step] = v[h][r];
-          }
-        }
-        fence_proxy_async_global();
-        named_bar_sync(1, kGatherWarps * 32);
-        if (warp == kWarpGather0 && lane == 0) {
-          if (kbu[0] >= 0) red_release_gpu_add(p.kb_ready + kbu[0], 1u);
-          if (kbu[1] >= 0) red_release_gpu_add(p.kb_ready + kbu[1], 1u);
-        }
-      }
-      if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) raise_error(p.err, GW_DERR_BAD_INDEX);
-    } else if (AMODE == kASmemGather) {
+    if (AMODE == kASmemGather) {
       const int gw_idx = warp - kWarpGather0;
       const uint32_t grp = static_cast<uint32_t>(gw_idx >> 2);
       const int wrow = (gw_idx & 3) * 32;
@@ -456,7 +372,7 @@ cudaError_t launch_tc(const CUtensorMap& tb, const CUtensorMap& ta, const TcPara
     kern<<<grid, kThreads, C::kSmemBytes, stream>>>(tb, ta, p);
     return cudaGetLastError();
   }
-  if (AMODE == kATma) {
+  {
     // Programmatic dependent launch: the prologue (barriers, TMEM, descriptor
     // prefetch) overlaps the tail of the previous kernel on the stream; the
     // TMA warp waits for that kernel before it reads the A operand.
@@ -472,19 +388,6 @@ cudaError_t launch_tc(const CUtensorMap& tb, const CUtensorMap& ta, const TcPara
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kern, tb, ta, p);
   }
-  // The in-kernel gather makes CTAs wait on each other's units: launch
-  // cooperatively so that all of them are resident (the launch fails otherwise).
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = C::kSmemBytes;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, tb, ta, p);
 }
 
 }  // namespace
@@ -493,8 +396,7 @@ cudaError_t launch_gemm_tc(int a_mode, const void* x, int dtype, int64_t M, int6
                            int64_t ldx, const void* w, int64_t N, int64_t ldw,
                            const int64_t* idx, int64_t n_alive, const void* bias, int epilogue,
                            void* y, int64_t ldy, unsigned int* err, int sm_count,
-                           cudaStream_t stream, void* scratch_xg, int64_t ldg,
-                           unsigned int* kb_ready, const int64_t* a_cols, const int32_t* k_dev) {
+                           cudaStream_t stream, const int64_t* a_cols, const int32_t* k_dev) {
   // Tile width 256 (measured best on B200 where there are several waves:
   // wider tiles reuse A more per byte moved), 128 for narrow N. When 256-wide
   // tiles leave SMs idle in a single wave and 192-wide ones still fit in one
@@ -517,7 +419,7 @@ cudaError_t launch_gemm_tc(int a_mode, const void* x, int dtype, int64_t M, int6
   const int64_t num_tiles = m_tiles * n_tiles;
   if (num_tiles > 0x7FFFFFFFll || m_tiles > 0x7FFFFFFFll) return cudaErrorInvalidValue;
   const int64_t num_kb = (n_alive + kBK - 1) / kBK;
-  if (a_mode == kAOverlap && num_kb * m_tiles > 0x7FFFFFFFll) return cudaErrorInvalidValue;
+  if (a_mode != kATma && a_mode != kASmemGather) return cudaErrorInvalidValue;
 
   TcParams p{};
   p.x = static_cast<const uint16_t*>(x);
@@ -537,9 +439,6 @@ cudaError_t launch_gemm_tc(int a_mode, const void* x, int dtype, int64_t M, int6
   p.n_tiles = static_cast<int>(n_tiles);
   p.num_tiles = static_cast<int>(num_tiles);
   p.err = err;
-  p.xg = static_cast<uint16_t*>(scratch_xg);
-  p.ldg = ldg;
-  p.kb_ready = kb_ready;
   p.a_cols = a_mode == kATma ? a_cols : nullptr;
   p.k_dev = a_mode == kATma ? k_dev : nullptr;
   if (p.a_cols && (n_alive % kBK) != 0) return cudaErrorInvalidValue;
@@ -551,20 +450,13 @@ cudaError_t launch_gemm_tc(int a_mode, const void* x, int dtype, int64_t M, int6
   } else if (a_mode == kATma) {
     // A is the compacted x' [M, n_alive], or x [M, K] itself with a_cols.
     if (!make_tmap_kmajor(&ta, x, M, a_cols ? K : n_alive, ldx, kBK, kBM)) return cudaErrorInvalidValue;
-  } else {
-    if (!scratch_xg || !kb_ready || (ldg % 8) != 0) return cudaErrorInvalidValue;
-    if (!make_tmap_kmajor(&ta, scratch_xg, M, n_alive, ldg, kBK, kBM)) return cudaErrorInvalidValue;
-    cudaError_t e = cudaMemsetAsync(kb_ready, 0, static_cast<size_t>(num_kb) * sizeof(unsigned int),
-                                    stream);
-    if (e != cudaSuccess) return e;
   }
 
 #define GW_TC_MODES(BNV, DTV)                                                                     \
   switch (a_mode) {                                                                              \
     case kATma: return launch_tc<BNV, DTV, kATma>(tb, ta, p, static_cast<int>(sms), stream);      \
-    case kASmemGather:                                                                           \
+    default:                                                                                     \
       return launch_tc<BNV, DTV, kASmemGather>(tb, ta, p, static_cast<int>(sms), stream);        \
-    default: return launch_tc<BNV, DTV, kAOverlap>(tb, ta, p, static_cast<int>(sms), stream);    \
   }
   if (BN == 256) {
     if (dtype == GW_DTYPE_BF16) { GW_TC_MODES(256, GW_DTYPE_BF16) }

@@ -21,6 +21,28 @@
 // No TMA multicast: each CTA loads only its own halves.
 // Every wait is bounded (gw_common.cuh); the kernel never hangs on a lost
 // arrival, it records GW_DEVICE_ERR_WAIT_TIMEOUT and unwinds.
+//
+// In-kernel gather (GATHER = true, gw_gather_gemm's overlap strategy): A is
+// x' = x[:, idx] in the workspace, and the kernel builds it itself while the
+// MMAs run. x' is cut into units of 128 rows (half a pair tile) x 64 alive
+// columns (one k atom). Before their first epilogue, the eight epilogue warps
+// of every CTA claim units (two at a time) from a counter in the workspace
+// header, gather them with 2-byte loads (lane l: alive columns 2l and 2l+1,
+// one 4-byte store per row) and publish each finished unit through its flag.
+// The TMA producer waits for a unit's flag before loading it. Units are
+// claimed in the order the tiles consume them (groups of as many row blocks
+// as one wave of tiles covers, k atom by k atom inside a group) and tiles are
+// walked row block by row block, so the first wave of MMAs waits only for the
+// first units. Units are claimed, not assigned, so no CTA ever waits for a
+// unit that only a CTA which is not resident could produce.
+// Flags and counters carry the call's number: the header's 64-bit epoch E is
+// read by every CTA after griddepcontrol.wait (so the previous call on the
+// stream has finished), the call works with E + 1 (a flag is ready when it
+// equals E + 1; the counters hold E + 1 in their upper 40 bits and reset
+// themselves when they see an older number), and the last CTA to finish
+// stores E + 1 as the new epoch. Nothing needs clearing between calls, the
+// workspace's contents on entry do not matter, and every replay of a CUDA
+// graph gets a fresh number.
 #include <algorithm>
 #include <cstdlib>
 
@@ -94,9 +116,174 @@ struct Tc2Params {
   int64_t a_width;          // columns of x (with a_cols)
   // K' on the device (num_kb is then an upper bound; see device_num_kb).
   const int32_t* k_dev;
+  // In-kernel gather (GATHER): A = x' [M, n_alive] (leading dimension ldp) is
+  // built from x [M, gK] (leading dimension ldgx) through the alive list.
+  const uint16_t* gx;
+  int64_t ldgx;
+  int64_t gK;
+  const int64_t* gidx;
+  int64_t n_alive;
+  uint16_t* xg;
+  int64_t ldp;
+  // Workspace header, 64-bit words: [0] epoch, [1] unit claim counter, [2]
+  // finished-CTA counter, [3] unused, then one flag per unit (half-panel hp,
+  // k atom kb) at 4 + hp * num_kb + kb.
+  unsigned long long* ghdr;
+  int g_hp;                 // half-panels (128-row blocks) per claim group
+  int h_total;              // half-panels: 2 * m_tiles
+  int m_major;              // tiles walked row block by row block (gather order)
 };
 
-template <int BN, int DT, int EPI>
+// Tile t -> (row block, column block): column blocks fastest when m_major
+// (the in-kernel gather's order), row blocks fastest otherwise.
+__device__ __forceinline__ void tile_coords(int tile, const Tc2Params& p, int& m_blk, int& n_blk) {
+  if (p.m_major) {
+    m_blk = tile / p.n_tiles;
+    n_blk = tile - m_blk * p.n_tiles;
+  } else {
+    n_blk = tile / p.m_tiles;
+    m_blk = tile - n_blk * p.m_tiles;
+  }
+}
+
+__device__ __forceinline__ void st_release_gpu_u64(unsigned long long* p, uint64_t v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" :: "l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_acquire_gpu_u64(const unsigned long long* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Counters tagged with the call's number: (number << 24) | count. Adds n and
+// returns the count before the add; a counter holding another number (an
+// earlier call's, or whatever the workspace held) counts as 0. The common case
+// is one atomicAdd; only the first claims of a call, which find the old
+// number, install the new one with compare-and-swap.
+constexpr int kCountBits = 24;
+__device__ __forceinline__ uint32_t tagged_add(unsigned long long* ctr, uint64_t call, uint32_t n) {
+  constexpr uint64_t kCountMask = (uint64_t{1} << kCountBits) - 1;
+  const uint64_t tag = call & ((uint64_t{1} << (64 - kCountBits)) - 1);
+  uint64_t old = atomicAdd(ctr, static_cast<unsigned long long>(n));
+  if ((old >> kCountBits) == tag) return static_cast<uint32_t>(old & kCountMask);
+  uint64_t cur = old + n;                      // the counter as our add left it
+  for (;;) {
+    const uint64_t prev = atomicCAS(ctr, cur, (tag << kCountBits) | n);
+    if (prev == cur) return 0u;                // installed: we own [0, n)
+    if ((prev >> kCountBits) == tag) {         // someone else installed it: count on it
+      old = atomicAdd(ctr, static_cast<unsigned long long>(n));
+      if ((old >> kCountBits) == tag) return static_cast<uint32_t>(old & kCountMask);
+      cur = old + n;
+    } else {
+      cur = prev;                              // still an old number: try again on it
+    }
+  }
+}
+
+// Bounded wait until *flag == value (acquire); same contract as wait_counter_geq.
+__device__ __forceinline__ bool wait_flag_eq(const unsigned long long* flag, uint64_t value,
+                                             volatile int* abort_flag, unsigned int* err) {
+  if (ld_acquire_gpu_u64(flag) == value) return true;
+  const unsigned long long t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (ld_acquire_gpu_u64(flag) == value) return true;
+    if ((i & 63u) == 0u) {
+      if (abort_flag && *abort_flag) return false;
+      if (global_timer_ns() - t0 > GW_WAIT_LIMIT_NS) {
+        if (abort_flag) *abort_flag = 1;
+        raise_error(err, GW_DERR_WAIT_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+// Unit u of the claim order -> (half-panel, k atom). Groups of g_hp
+// half-panels (the last one may be smaller), k atom by k atom inside a group.
+__device__ __forceinline__ void unit_coords(int u, const Tc2Params& p, int& hp, int& kb) {
+  const int g_units = p.g_hp * p.num_kb;
+  const int g = u / g_units;
+  const int r = u - g * g_units;
+  const int hp0 = g * p.g_hp;
+  const int gsz = min(p.g_hp, p.h_total - hp0);
+  kb = r / gsz;
+  hp = hp0 + (r - kb * gsz);
+}
+
+// The epilogue warps' gather of x' (see the file comment). e: 0..7, the
+// warp's 16 rows of a unit; call: this call's number (epoch + 1). Returns
+// when every unit has been claimed.
+template <int DT>
+__device__ __forceinline__ void gather_units(const Tc2Params& p, int e, int lane,
+                                             volatile int* slot, uint64_t call) {
+  const int units = p.h_total * p.num_kb;
+  bool bad = false;
+  for (;;) {
+    if (e == 0 && lane == 0) *slot = static_cast<int>(tagged_add(p.ghdr + 1, call, 2u));
+    named_bar_sync(1, kEpiWarps2 * 32);
+    const int u0 = *slot;
+    if (u0 >= units) break;
+    uint32_t v[2][16];
+    int64_t row0[2];
+    int rows_here[2], kbu[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int u = u0 + h;
+      int hp = 0, kb = 0;
+      if (u < units) unit_coords(u, p, hp, kb);
+      kbu[h] = kb;
+      row0[h] = static_cast<int64_t>(hp) * kHalfM + e * 16;
+      const int64_t rem = p.M - row0[h];
+      rows_here[h] = (u >= units || rem <= 0) ? 0 : (rem >= 16 ? 16 : static_cast<int>(rem));
+      const int64_t j0 = static_cast<int64_t>(kb) * kBK2 + 2 * lane;
+      int64_t c0 = -1, c1 = -1;
+      if (rows_here[h] > 0 && j0 < p.n_alive) {
+        c0 = __ldg(p.gidx + j0);
+        if (c0 < 0 || c0 >= p.gK) { bad = true; c0 = -1; }
+      }
+      if (rows_here[h] > 0 && j0 + 1 < p.n_alive) {
+        c1 = __ldg(p.gidx + j0 + 1);
+        if (c1 < 0 || c1 >= p.gK) { bad = true; c1 = -1; }
+      }
+      const uint16_t* xr = p.gx + (rows_here[h] > 0 ? row0[h] * p.ldgx : 0);
+#pragma unroll
+      for (int r = 0; r < 16; ++r) {
+        const bool rv = r < rows_here[h];
+        const uint32_t lo = (rv && c0 >= 0) ? static_cast<uint32_t>(__ldg(xr + r * p.ldgx + c0)) : 0u;
+        const uint32_t hi = (rv && c1 >= 0) ? static_cast<uint32_t>(__ldg(xr + r * p.ldgx + c1)) : 0u;
+        v[h][r] = lo | (hi << 16);
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      if (rows_here[h] > 0) {
+        uint32_t* dst = reinterpret_cast<uint32_t*>(p.xg + row0[h] * p.ldp +
+                                                    static_cast<int64_t>(kbu[h]) * kBK2) + lane;
+        const int64_t step = p.ldp / 2;
+#pragma unroll
+        for (int r = 0; r < 16; ++r)
+          if (r < rows_here[h]) dst[r * step] = v[h][r];
+      }
+    }
+    fence_proxy_async_global();        // x' stores -> visible to the TMA (async proxy) loads
+    named_bar_sync(1, kEpiWarps2 * 32);
+    if (e == 0 && lane == 0) {
+      __threadfence();                 // every warp's stores (ordered by the barrier) before the flags
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int u = u0 + h;
+        if (u < units) {
+          int hp, kb;
+          unit_coords(u, p, hp, kb);
+          st_release_gpu_u64(p.ghdr + 4 + static_cast<int64_t>(hp) * p.num_kb + kb, call);
+        }
+      }
+    }
+  }
+  if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) raise_error(p.err, GW_DERR_BAD_INDEX);
+}
+
+template <int BN, int DT, int EPI, bool GATHER>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
 gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
                 const __grid_constant__ CUtensorMap tmap_a,
@@ -119,6 +306,8 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
   static_assert(8 * (2 * kStages2 + 5) <= 192, "barrier region overflows into the TMEM slot");
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_region + 192);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_region + 196);
+  volatile int* claim_slot = reinterpret_cast<volatile int*>(bar_region + 200);   // GATHER
+  uint64_t call = 0;           // GATHER: this call's number (the header's epoch + 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -159,6 +348,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
     // ------------------------------------------------------------ TMA producer (both CTAs)
     if (lane == 0) {
       asm volatile("griddepcontrol.wait;" ::: "memory");   // A may come from the previous kernel
+      if constexpr (GATHER) call = *reinterpret_cast<volatile unsigned long long*>(p.ghdr) + 1;
       const int num_kb = p.k_dev ? device_num_kb(p.k_dev, p.num_kb) : p.num_kb;
       const int num_ks = (num_kb + kAtoms2 - 1) / kAtoms2;
       uint32_t it = 0;
@@ -170,8 +360,8 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
         if (num_kb > 1) nxt1 = run_start_load(p.a_cols, 1);
       }
       for (int tile = pair; ok && tile < p.num_tiles; tile += num_pairs) {
-        const int m_blk = tile % p.m_tiles;
-        const int n_blk = tile / p.m_tiles;
+        int m_blk, n_blk;
+        tile_coords(tile, p, m_blk, n_blk);
         const int a_row = m_blk * kPairM + static_cast<int>(rank) * kHalfM;
         const int b_row = n_blk * BN + static_cast<int>(rank) * kHalfN;
         for (int ks = 0; ks < num_ks; ++ks, ++it) {
@@ -191,11 +381,28 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
           const int atoms = min(kAtoms2, num_kb - ks * kAtoms2);
           if (rank == 0)
             mbar_arrive_expect_tx(full(s), 2u * atoms * (kAAtomBytes2 + C::kBAtomBytes));
-          for (int a = 0; a < atoms; ++a) {
-            const int kx = (ks * kAtoms2 + a) * kBK2;
-            const int ax = p.a_cols ? run_start_check(a == 0 ? cur0 : cur1, p.a_width, p.err) : kx;
-            tma_load_2d_pair(a_s + a * kAAtomBytes2, &tmap_a, ax, a_row, leader_full);
-            tma_load_2d_pair(b_s + a * C::kBAtomBytes, &tmap_b, kx, b_row, leader_full);
+          if constexpr (GATHER) {
+            // W' first (it does not depend on the gather), then each unit of x'
+            // once its flag says it is complete; count the flag down.
+            for (int a = 0; a < atoms; ++a)
+              tma_load_2d_pair(b_s + a * C::kBAtomBytes, &tmap_b, (ks * kAtoms2 + a) * kBK2, b_row,
+                               leader_full);
+            const int hp = 2 * m_blk + static_cast<int>(rank);
+            for (int a = 0; a < atoms; ++a) {
+              const int kb = ks * kAtoms2 + a;
+              const unsigned long long* flag = p.ghdr + 4 + static_cast<int64_t>(hp) * p.num_kb + kb;
+              if (!wait_flag_eq(flag, call, abort_flag, p.err)) { ok = false; break; }
+              fence_proxy_async_global();   // the gatherers' generic stores -> our TMA reads
+              tma_load_2d_pair(a_s + a * kAAtomBytes2, &tmap_a, kb * kBK2, a_row, leader_full);
+            }
+            if (!ok) break;
+          } else {
+            for (int a = 0; a < atoms; ++a) {
+              const int kx = (ks * kAtoms2 + a) * kBK2;
+              const int ax = p.a_cols ? run_start_check(a == 0 ? cur0 : cur1, p.a_width, p.err) : kx;
+              tma_load_2d_pair(a_s + a * kAAtomBytes2, &tmap_a, ax, a_row, leader_full);
+              tma_load_2d_pair(b_s + a * C::kBAtomBytes, &tmap_b, kx, b_row, leader_full);
+            }
           }
         }
       }
@@ -266,10 +473,16 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
     const uint32_t leader_tempty0 = mapa_shared(tempty(0), 0);
     const uint32_t leader_tempty1 = mapa_shared(tempty(1), 0);
     uint8_t* sb = epi_stage + (warp - 2) * kEpiTileBytes;
+    if constexpr (GATHER) {
+      // x, the alive list and the workspace may come from the previous kernel.
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      call = *reinterpret_cast<volatile unsigned long long*>(p.ghdr) + 1;
+      gather_units<DT>(p, warp - 2, lane, claim_slot, call);
+    }
     uint32_t lt = 0;
     for (int tile = pair; tile < p.num_tiles; tile += num_pairs, ++lt) {
-      const int m_blk = tile % p.m_tiles;
-      const int n_blk = tile / p.m_tiles;
+      int m_blk, n_blk;
+      tile_coords(tile, p, m_blk, n_blk);
       const uint32_t b = lt & 1u;
       const uint32_t aph = (lt >> 1) & 1u;
       if (!mbar_wait_cluster(tfull(b), aph, abort_flag, p.err)) break;
@@ -378,6 +591,12 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, kTmemCols2);
   }
+  if constexpr (GATHER) {
+    // The last CTA to finish moves the epoch on (every CTA has read it by now).
+    // Thread 0 is the TMA producer, which read the call number after its wait.
+    if (threadIdx.x == 0 && tagged_add(p.ghdr + 2, call, 1u) + 1u == gridDim.x)
+      st_release_gpu_u64(p.ghdr, call);
+  }
 }
 
 }  // namespace
@@ -447,19 +666,31 @@ cudaError_t launch_tc2_bn(int dtype, Tc2Params& p, const void* a, int64_t M, int
   if (!p.y_tma) ty = ta;     // not read by the kernel
   if (p.n_peers > 0 && !p.y_tma) return cudaErrorInvalidValue;   // peer stores ride the TMA path
 
-  const bool bf = dtype == GW_DTYPE_BF16;
-  auto kern = p.epi == GW_EPI_GELU_ERF
-                  ? (bf ? gemm_tc2_kernel<BN, GW_DTYPE_BF16, GW_EPI_GELU_ERF>
-                        : gemm_tc2_kernel<BN, GW_DTYPE_F16, GW_EPI_GELU_ERF>)
-              : p.epi == GW_EPI_GELU_TANH
-                  ? (bf ? gemm_tc2_kernel<BN, GW_DTYPE_BF16, GW_EPI_GELU_TANH>
-                        : gemm_tc2_kernel<BN, GW_DTYPE_F16, GW_EPI_GELU_TANH>)
-                  : (bf ? gemm_tc2_kernel<BN, GW_DTYPE_BF16, GW_EPI_NONE>
-                        : gemm_tc2_kernel<BN, GW_DTYPE_F16, GW_EPI_NONE>);
-  cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), C::kSmemBytes);
-  if (e != cudaSuccess) return e;
   const int64_t pairs = std::max<int64_t>(1, (sm_count > 0 ? sm_count : 148) / 2);
   const int grid = static_cast<int>(2 * std::min<int64_t>(num_tiles, pairs));
+  if (p.ghdr) {
+    // In-kernel gather: tiles row block by row block; claim groups of as many
+    // half-panels as one wave of tiles spans.
+    p.m_major = 1;
+    p.h_total = static_cast<int>(2 * m_tiles);
+    const int64_t wave_rows = (pairs + n_tiles - 1) / n_tiles;      // row blocks per wave
+    p.g_hp = static_cast<int>(std::min<int64_t>(2 * m_tiles, 2 * std::max<int64_t>(1, wave_rows)));
+  }
+
+  const bool bf = dtype == GW_DTYPE_BF16;
+#define GW_TC2_KERN(G)                                                          \
+  (p.epi == GW_EPI_GELU_ERF                                                     \
+       ? (bf ? gemm_tc2_kernel<BN, GW_DTYPE_BF16, GW_EPI_GELU_ERF, G>           \
+             : gemm_tc2_kernel<BN, GW_DTYPE_F16, GW_EPI_GELU_ERF, G>)           \
+   : p.epi == GW_EPI_GELU_TANH                                                  \
+       ? (bf ? gemm_tc2_kernel<BN, GW_DTYPE_BF16, GW_EPI_GELU_TANH, G>          \
+             : gemm_tc2_kernel<BN, GW_DTYPE_F16, GW_EPI_GELU_TANH, G>)          \
+       : (bf ? gemm_tc2_kernel<BN, GW_DTYPE_BF16, GW_EPI_NONE, G>               \
+             : gemm_tc2_kernel<BN, GW_DTYPE_F16, GW_EPI_NONE, G>))
+  auto kern = p.ghdr ? GW_TC2_KERN(true) : GW_TC2_KERN(false);
+#undef GW_TC2_KERN
+  cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), C::kSmemBytes);
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
   cfg.blockDim = dim3(kThreads2);
@@ -477,7 +708,8 @@ cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int6
                             const void* w, int64_t N, int64_t ldw, const void* bias, int epilogue,
                             void* y, int64_t ldy, unsigned int* err, int sm_count,
                             cudaStream_t stream, void* const* peers, int n_peers,
-                            const int64_t* a_cols, int64_t a_width, const int32_t* k_dev) {
+                            const int64_t* a_cols, int64_t a_width, const int32_t* k_dev,
+                            const Tc2Gather* gather) {
   Tc2Params p{};
   p.M = M;
   p.N = N;
@@ -495,9 +727,37 @@ cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int6
   p.a_cols = a_cols;
   p.a_width = a_width;
   p.k_dev = k_dev;
+  if (gather) {
+    if (a_cols || k_dev || !gather->x || !gather->idx || !gather->xg || !gather->header ||
+        (gather->ldp % 8) != 0 || gather->ldp < K)
+      return cudaErrorInvalidValue;
+    p.gx = static_cast<const uint16_t*>(gather->x);
+    p.ldgx = gather->ldx;
+    p.gK = gather->K;
+    p.gidx = gather->idx;
+    p.n_alive = K;
+    p.xg = static_cast<uint16_t*>(gather->xg);
+    p.ldp = gather->ldp;
+    if (!tc2_gather_supported(M, K)) return cudaErrorInvalidValue;
+    p.ghdr = static_cast<unsigned long long*>(gather->header);
+    a = gather->xg;
+    lda = gather->ldp;
+  }
   const int bn = pair_gemm_tile_width(M, N, sm_count);
   return bn == 192 ? launch_tc2_bn<192>(dtype, p, a, M, K, lda, w, N, ldw, y, ldy, sm_count, stream)
                    : launch_tc2_bn<256>(dtype, p, a, M, K, lda, w, N, ldw, y, ldy, sm_count, stream);
+}
+
+size_t tc2_gather_header_bytes(int64_t M, int64_t n_alive) {
+  const int64_t half_panels = 2 * ((M + kPairM - 1) / kPairM);
+  const int64_t kb = (n_alive + kBK2 - 1) / kBK2;
+  return static_cast<size_t>((8 * (4 + half_panels * kb) + 255) / 256 * 256);
+}
+
+bool tc2_gather_supported(int64_t M, int64_t n_alive) {
+  const int64_t half_panels = 2 * ((M + kPairM - 1) / kPairM);
+  const int64_t kb = (n_alive + kBK2 - 1) / kBK2;
+  return half_panels * kb + 2 < (int64_t{1} << kCountBits);
 }
 
 }  // namespace gw

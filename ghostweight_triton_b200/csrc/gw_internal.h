@@ -65,9 +65,6 @@ cudaError_t launch_index_runs(const int64_t* idx, int64_t n, int64_t K, int32_t*
 // gw_gemm_tc.cu: tcgen05 gather-GEMM / packed GEMM (fp16, bf16).
 // a_mode: 0 -> A is a dense [M, n_alive] matrix loaded by TMA (idx unused)
 //         1 -> producer warps gather x[:, idx] into shared memory
-//         2 -> warps gather x[:, idx] into scratch_xg [M, ldg] inside the kernel
-//              (per-k-block counters kb_ready[num_kb], zeroed by the launcher),
-//              then TMA streams it; cooperative launch
 // a_mode 0 with a_cols: as launch_gemm_tc2's a_cols (A = x [M, K], k-block kb
 // loaded from column a_cols[64 kb], n_alive a multiple of 64). a_mode 0 with
 // k_dev: as launch_gemm_tc2's k_dev (n_alive an upper bound).
@@ -75,8 +72,7 @@ cudaError_t launch_gemm_tc(int a_mode, const void* x, int dtype, int64_t M, int6
                            int64_t ldx, const void* w, int64_t N, int64_t ldw,
                            const int64_t* idx, int64_t n_alive, const void* bias, int epilogue,
                            void* y, int64_t ldy, unsigned int* err, int sm_count,
-                           cudaStream_t stream, void* scratch_xg = nullptr, int64_t ldg = 0,
-                           unsigned int* kb_ready = nullptr, const int64_t* a_cols = nullptr,
+                           cudaStream_t stream, const int64_t* a_cols = nullptr,
                            const int32_t* k_dev = nullptr);
 
 // gw_gemm_tc2.cu: CTA-pair (cta_group::2) tcgen05 GEMM, dense A [M, K] by TMA,
@@ -91,12 +87,30 @@ constexpr int kMaxPeers = 7;
 // kb is loaded from column a_cols[64 kb]: no compacted copy of x is needed.
 // With k_dev, K is an upper bound and the kernel reads K' from the device (A
 // and W' must be zero in columns [K', round_up(max(K', 1), 64))).
+// With gather, the kernel builds A = x[:, idx] itself (K = the alive count):
+// its epilogue warps gather x' into gather->xg (leading dimension ldp >= K, a
+// multiple of 8) in 128-row x 64-column units published through flags in
+// gather->header (tc2_gather_header_bytes(M, K) bytes, 8-byte aligned, any
+// contents; see gw_gemm_tc2.cu), while the TMA producer streams finished units.
+// Not combined with a_cols or k_dev. tc2_gather_supported says whether the
+// unit count fits the header's counters.
+struct Tc2Gather {
+  const void* x = nullptr;          // [M, K_x], leading dimension ldx
+  int64_t ldx = 0;
+  int64_t K = 0;                    // columns of x (index bound)
+  const int64_t* idx = nullptr;     // alive list, K' entries
+  void* xg = nullptr;               // x' [M, ldp]
+  int64_t ldp = 0;
+  void* header = nullptr;
+};
+size_t tc2_gather_header_bytes(int64_t M, int64_t n_alive);
+bool tc2_gather_supported(int64_t M, int64_t n_alive);
 cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int64_t lda,
                             const void* w, int64_t N, int64_t ldw, const void* bias, int epilogue,
                             void* y, int64_t ldy, unsigned int* err, int sm_count,
                             cudaStream_t stream, void* const* peers = nullptr, int n_peers = 0,
                             const int64_t* a_cols = nullptr, int64_t a_width = 0,
-                            const int32_t* k_dev = nullptr);
+                            const int32_t* k_dev = nullptr, const Tc2Gather* gather = nullptr);
 // Whether the CTA-pair kernel serves a dense-A GEMM of this shape.
 bool use_pair_gemm(int64_t M, int64_t N, int sm_count);
 // Tile width (192 or 256) the pair kernel uses for an M x N output.

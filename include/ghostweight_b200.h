@@ -194,9 +194,11 @@ GW_API int gw_gather_rows_t(const void* src, int dtype, int64_t rows, int64_t co
  *                     M <= 4 the decode kernel's gather, as with AUTO);
  *   GW_GEMM_PREGATHER two launches: x[:, idx] -> workspace (dense [M, K'_pad]),
  *                     then the GEMM with both operands loaded by TMA;
- *   GW_GEMM_OVERLAP   one cooperative kernel: its gather warps write x[:, idx] to
- *                     the workspace k-block by k-block while the TMA/MMA warps
- *                     already consume the finished k-blocks.
+ *   GW_GEMM_OVERLAP   one launch where the shape runs on the CTA-pair kernel: its
+ *                     epilogue warps gather x[:, idx] into the workspace in
+ *                     128-row x 64-column units (before their first epilogue)
+ *                     while the TMA/MMA warps already consume the finished
+ *                     units; other shapes run GW_GEMM_PREGATHER;
  *   GW_GEMM_RUNS      for alive lists made of 64-column runs (a mask that kills
  *                     whole 64- or 128-column blocks): idx[64 j + r] = idx[64 j] + r
  *                     for r < 64, idx[64 j] a multiple of 8, n_alive a multiple
@@ -208,7 +210,9 @@ GW_API int gw_gather_rows_t(const void* src, int dtype, int64_t rows, int64_t co
  *                     wrong result); gw_index_runs checks the whole list once.
  * workspace: device scratch of at least gw_gather_gemm_workspace_bytes(M, n_alive,
  * dtype) bytes, 16-byte aligned (may be NULL for GW_GEMM_FUSED, GW_GEMM_RUNS and
- * fp32). Its contents on entry do not matter; concurrent calls must not share it.
+ * fp32): a header (the overlap strategy's unit flags, tagged with a call number
+ * the header also keeps) and x'. Its contents on entry do not matter; calls
+ * that use one workspace must be ordered on one stream.
  *
  * Weights are read early: the GEMMs are launched as programmatic dependents
  * of the previous kernel on the stream, and for M <= 64 the kernel requests

@@ -71,9 +71,12 @@ def test_mask_workspace_sizing(lib):
 
 
 def test_gemm_workspace_sizing(lib):
-    # 256-byte header of k-block counters + x' [M, round_up(K', 64)] 16-bit
+    # Header (epoch, two counters and one 8-byte flag per 128-row x 64-column
+    # unit of x', rounded up to 256 bytes) + x' [M, round_up(K', 64)] 16-bit.
     assert lib.gw_gather_gemm_workspace_bytes(8, 64, 0) == 256 + 8 * 64 * 2
-    assert lib.gw_gather_gemm_workspace_bytes(4096, 2048, 0) == 256 + 4096 * 2048 * 2
+    units = (2 * 4096 // 256) * (2048 // 64)
+    hdr = (8 * (4 + units) + 255) // 256 * 256
+    assert lib.gw_gather_gemm_workspace_bytes(4096, 2048, 0) == hdr + 4096 * 2048 * 2
     assert lib.gw_gather_gemm_workspace_bytes(4096, 2048, 2) == 0     # fp32 needs none
     assert lib.gw_gather_gemm_workspace_bytes(0, 2048, 0) == 0
 

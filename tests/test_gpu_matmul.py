@@ -159,7 +159,8 @@ def test_workspace_reuse_between_shapes(strategy):
     (2500, 512, 4000, 100, True, "gelu_tanh"),  # 2 k-blocks, the second one zero-filled past K'
     (4096, 1024, 4608, 1000, True, None),       # 288 tiles, 3.9 waves
 ])
-def test_pair_gemm_ragged_vs_fp32(dt, M, K, N, kp, bias, act):
+@pytest.mark.parametrize("strategy", ["pregather", "overlap"])
+def test_pair_gemm_ragged_vs_fp32(dt, M, K, N, kp, bias, act, strategy):
     torch_dt = DT[dt]
     g = torch.Generator(device="cuda").manual_seed(M + N + kp)
     x = torch.randn(M, K, device="cuda", dtype=torch_dt, generator=g)
@@ -170,7 +171,7 @@ def test_pair_gemm_ragged_vs_fp32(dt, M, K, N, kp, bias, act):
     ws = torch.empty(_native.gather_gemm_workspace_bytes(M, kp, torch_dt), dtype=torch.uint8, device="cuda")
     big = torch.full((M, N + 8), float("nan"), device="cuda", dtype=torch_dt)
     y = big[:, :N]                             # ldy = N + 8: still 16-byte rows, columns past N untouched
-    _native.gather_gemm(x, wp, idx, y, bias=b, activation=act, strategy="pregather", workspace=ws)
+    _native.gather_gemm(x, wp, idx, y, bias=b, activation=act, strategy=strategy, workspace=ws)
     ref = F.linear(x.float()[:, idx], w.float()[:, idx], None if b is None else b.float())
     if act == "gelu":
         ref = F.gelu(ref)
@@ -179,6 +180,90 @@ def test_pair_gemm_ragged_vs_fp32(dt, M, K, N, kp, bias, act):
     torch.testing.assert_close(y, ref.to(torch_dt), **tols(torch_dt))
     assert torch.isnan(big[:, N:]).all()
     assert _native.device_error(reset=False) & _native.DEVICE_ERR_WAIT_TIMEOUT == 0
+
+
+# ----------------------------------------------------------------- pair GEMM gathering x' itself
+def _overlap_case(M, K, N, kp, seed, dtype=torch.float16):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x = torch.randn(M, K, device="cuda", dtype=dtype, generator=g)
+    w = (torch.randn(N, K, device="cuda", generator=g) / kp ** 0.5).to(dtype)
+    idx = torch.sort(torch.randperm(K, device="cuda", generator=g)[:kp]).values
+    return x, w, idx, pack_weight(w, idx)
+
+
+def test_overlap_garbage_workspace_and_repeated_calls():
+    """The in-kernel gather's flags carry a per-call number kept in the workspace header:
+    a workspace full of random bytes works, and successive calls with new inputs in the
+    same workspace never read an earlier call's x' (each result matches its own inputs)."""
+    M, K, N, kp = 4096, 4096, 4096, 2048
+    _, w, idx, wp = _overlap_case(M, K, N, kp, 5)
+    nbytes = _native.gather_gemm_workspace_bytes(M, kp, torch.float16)
+    ws = torch.randint(0, 256, (nbytes,), dtype=torch.uint8, device="cuda")
+    y = torch.empty(M, N, device="cuda", dtype=torch.float16)
+    g = torch.Generator(device="cuda").manual_seed(9)
+    for step in range(4):
+        x = torch.randn(M, K, device="cuda", dtype=torch.float16, generator=g)
+        _native.gather_gemm(x, wp, idx, y, strategy="overlap", workspace=ws)
+        ref = (x.float()[:, idx] @ w.float()[:, idx].t()).half()
+        torch.testing.assert_close(y, ref, **tols(torch.float16), msg=f"call {step}")
+    assert _native.device_error(reset=True) == 0
+
+
+def test_overlap_shares_workspace_with_pregather_of_other_shapes():
+    """x' of a pregather call of another shape lands where the overlap call keeps its flags."""
+    ws = torch.empty(96 << 20, dtype=torch.uint8, device="cuda")
+    for M, K, N, kp, strat in [(128, 4096, 4096, 4000, "pregather"), (4096, 4096, 4096, 2048, "overlap"),
+                               (512, 8192, 1024, 8000, "pregather"), (4096, 4096, 4096, 1024, "overlap"),
+                               (2500, 4096, 4000, 2048, "overlap")]:
+        x, w, idx, wp = _overlap_case(M, K, N, kp, M + kp)
+        y = torch.empty(M, N, device="cuda", dtype=torch.float16)
+        _native.gather_gemm(x, wp, idx, y, strategy=strat, workspace=ws)
+        ref = (x.float()[:, idx] @ w.float()[:, idx].t()).half()
+        torch.testing.assert_close(y, ref, **tols(torch.float16), msg=f"{strat} {M}x{K}x{N} K'={kp}")
+    assert _native.device_error(reset=True) == 0
+
+
+def test_overlap_replayed_from_a_cuda_graph():
+    """Every replay of a captured call reads a new call number from the workspace header."""
+    M, K, N, kp = 4096, 2048, 4096, 1536
+    x, w, idx, wp = _overlap_case(M, K, N, kp, 21)
+    ws = torch.empty(_native.gather_gemm_workspace_bytes(M, kp, torch.float16), dtype=torch.uint8,
+                     device="cuda")
+    y = torch.empty(M, N, device="cuda", dtype=torch.float16)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        _native.gather_gemm(x, wp, idx, y, strategy="overlap", workspace=ws)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        _native.gather_gemm(x, wp, idx, y, strategy="overlap", workspace=ws)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    for rep in range(3):
+        x.copy_(torch.randn(M, K, device="cuda", dtype=torch.float16, generator=g))
+        graph.replay()
+        torch.cuda.synchronize()
+        ref = (x.float()[:, idx] @ w.float()[:, idx].t()).half()
+        torch.testing.assert_close(y, ref, **tols(torch.float16), msg=f"replay {rep}")
+    del graph
+    assert _native.device_error(reset=True) == 0
+
+
+def test_overlap_bad_index_reads_zero_and_flags():
+    M, K, N, kp = 4096, 4096, 4096, 1024
+    x, w, idx, wp = _overlap_case(M, K, N, kp, 33)
+    bad = idx.clone()
+    bad[100] = K + 5                               # outside [0, K)
+    _native.device_error(reset=True)
+    y = torch.empty(M, N, device="cuda", dtype=torch.float16)
+    _native.gather_gemm(x, wp, bad, y, strategy="overlap",
+                        workspace=_native.gemm_workspace(x.device, _native.gather_gemm_workspace_bytes(
+                            M, kp, torch.float16)))
+    xs = x.float()[:, idx]
+    xs[:, 100] = 0                                 # the bad column contributes zero
+    ref = (xs @ w.float()[:, idx].t()).half()
+    torch.testing.assert_close(y, ref, **tols(torch.float16))
+    assert _native.device_error(reset=True) == _native.DEVICE_ERR_BAD_INDEX
 
 
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
