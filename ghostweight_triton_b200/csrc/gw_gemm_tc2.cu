@@ -180,6 +180,32 @@ __device__ __forceinline__ uint32_t tagged_add(unsigned long long* ctr, uint64_t
   }
 }
 
+__device__ __forceinline__ uint64_t ld_relaxed_gpu_u64(const unsigned long long* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_acq_rel_gpu() {
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+__device__ __forceinline__ void st_relaxed_gpu_u64(unsigned long long* p, uint64_t v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" :: "l"(p), "l"(v) : "memory");
+}
+
+// Which of the flags f[0, n) (n <= 16) already equal `value`: 16 independent
+// relaxed loads (one round trip for all), then one acquire fence if any was
+// set, which makes the data published before those flags visible.
+__device__ __forceinline__ uint32_t flags_ready(const unsigned long long* f, int n, uint64_t value) {
+  uint64_t v[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = i < n ? ld_relaxed_gpu_u64(f + i) : 0;
+  uint32_t bits = 0;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) bits |= (i < n && v[i] == value) ? (1u << i) : 0u;
+  if (bits) fence_acq_rel_gpu();
+  return bits;
+}
+
 // Bounded wait until *flag == value (acquire); same contract as wait_counter_geq.
 __device__ __forceinline__ bool wait_flag_eq(const unsigned long long* flag, uint64_t value,
                                              volatile int* abort_flag, unsigned int* err) {
@@ -216,13 +242,35 @@ __device__ __forceinline__ void unit_coords(int u, const Tc2Params& p, int& hp, 
 template <int DT>
 __device__ __forceinline__ void gather_units(const Tc2Params& p, int e, int lane,
                                              volatile int* slot, uint64_t call) {
+  // Software-pipelined over batches of two units: the claim of the next batch
+  // is issued before this batch's loads, and the next batch's alive indices
+  // are loaded while this batch is published, so one iteration costs about
+  // one round trip to memory instead of four in series.
   const int units = p.h_total * p.num_kb;
+  const bool leader = e == 0 && lane == 0;
   bool bad = false;
-  for (;;) {
-    if (e == 0 && lane == 0) *slot = static_cast<int>(tagged_add(p.ghdr + 1, call, 2u));
-    named_bar_sync(1, kEpiWarps2 * 32);
-    const int u0 = *slot;
-    if (u0 >= units) break;
+  int64_t c[2][2];                       // [unit of the batch][column 2 lane + i]
+  auto load_idx = [&](int u0) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int u = u0 + h;
+      c[h][0] = c[h][1] = -1;
+      if (u < units) {
+        int hp, kb;
+        unit_coords(u, p, hp, kb);
+        const int64_t j0 = static_cast<int64_t>(kb) * kBK2 + 2 * lane;
+        if (j0 < p.n_alive) c[h][0] = __ldg(p.gidx + j0);
+        if (j0 + 1 < p.n_alive) c[h][1] = __ldg(p.gidx + j0 + 1);
+      }
+    }
+  };
+  if (leader) slot[0] = static_cast<int>(tagged_add(p.ghdr + 1, call, 2u));
+  named_bar_sync(1, kEpiWarps2 * 32);
+  int u0 = slot[0];
+  load_idx(u0);
+  for (int it = 0; u0 < units; ++it) {
+    // Next batch's claim, into the other slot (read after the barrier below).
+    if (leader) slot[(it + 1) & 1] = static_cast<int>(tagged_add(p.ghdr + 1, call, 2u));
     uint32_t v[2][16];
     int64_t row0[2];
     int rows_here[2], kbu[2];
@@ -235,23 +283,25 @@ __device__ __forceinline__ void gather_units(const Tc2Params& p, int e, int lane
       row0[h] = static_cast<int64_t>(hp) * kHalfM + e * 16;
       const int64_t rem = p.M - row0[h];
       rows_here[h] = (u >= units || rem <= 0) ? 0 : (rem >= 16 ? 16 : static_cast<int>(rem));
-      const int64_t j0 = static_cast<int64_t>(kb) * kBK2 + 2 * lane;
-      int64_t c0 = -1, c1 = -1;
-      if (rows_here[h] > 0 && j0 < p.n_alive) {
-        c0 = __ldg(p.gidx + j0);
-        if (c0 < 0 || c0 >= p.gK) { bad = true; c0 = -1; }
-      }
-      if (rows_here[h] > 0 && j0 + 1 < p.n_alive) {
-        c1 = __ldg(p.gidx + j0 + 1);
-        if (c1 < 0 || c1 >= p.gK) { bad = true; c1 = -1; }
-      }
-      const uint16_t* xr = p.gx + (rows_here[h] > 0 ? row0[h] * p.ldgx : 0);
+      int64_t c0 = c[h][0], c1 = c[h][1];
+      if (c0 >= p.gK || c0 < -1 || c1 >= p.gK || c1 < -1) bad = true;
+      if (c0 >= p.gK || c0 < 0) c0 = -1;
+      if (c1 >= p.gK || c1 < 0) c1 = -1;
+      // Branch-free loads, so that all of the batch's loads are in flight at
+      // once: rows past M re-read the last valid row and dead or bad columns
+      // read column 0; both are masked to zero.
+      const int rlast = max(rows_here[h] - 1, 0);
+      const int64_t rbase = rows_here[h] > 0 ? row0[h] * p.ldgx : 0;
+      const uint16_t* b0 = p.gx + rbase + (c0 >= 0 ? c0 : 0);
+      const uint16_t* b1 = p.gx + rbase + (c1 >= 0 ? c1 : 0);
+      const uint32_t m0 = c0 >= 0 ? 0xFFFFu : 0u;
+      const uint32_t m1 = c1 >= 0 ? 0xFFFF0000u : 0u;
 #pragma unroll
       for (int r = 0; r < 16; ++r) {
-        const bool rv = r < rows_here[h];
-        const uint32_t lo = (rv && c0 >= 0) ? static_cast<uint32_t>(__ldg(xr + r * p.ldgx + c0)) : 0u;
-        const uint32_t hi = (rv && c1 >= 0) ? static_cast<uint32_t>(__ldg(xr + r * p.ldgx + c1)) : 0u;
-        v[h][r] = lo | (hi << 16);
+        const int64_t off = static_cast<int64_t>(min(r, rlast)) * p.ldgx;
+        const uint32_t lo = __ldg(b0 + off);
+        const uint32_t hi = __ldg(b1 + off);
+        v[h][r] = (lo & m0) | ((hi << 16) & m1);
       }
     }
 #pragma unroll
@@ -266,19 +316,24 @@ __device__ __forceinline__ void gather_units(const Tc2Params& p, int e, int lane
       }
     }
     fence_proxy_async_global();        // x' stores -> visible to the TMA (async proxy) loads
-    named_bar_sync(1, kEpiWarps2 * 32);
-    if (e == 0 && lane == 0) {
-      __threadfence();                 // every warp's stores (ordered by the barrier) before the flags
+    named_bar_sync(1, kEpiWarps2 * 32);  // this batch stored; the next claim is in its slot
+    const int u_next = slot[(it + 1) & 1];
+    load_idx(u_next);                  // in flight while the batch is published
+    if (leader) {
+      // One release fence for the batch (it covers every warp's stores, which
+      // the barrier ordered before it), then both flags as relaxed stores.
+      fence_acq_rel_gpu();
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int u = u0 + h;
         if (u < units) {
           int hp, kb;
           unit_coords(u, p, hp, kb);
-          st_release_gpu_u64(p.ghdr + 4 + static_cast<int64_t>(hp) * p.num_kb + kb, call);
+          st_relaxed_gpu_u64(p.ghdr + 4 + static_cast<int64_t>(hp) * p.num_kb + kb, call);
         }
       }
     }
+    u0 = u_next;
   }
   if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) raise_error(p.err, GW_DERR_BAD_INDEX);
 }
@@ -306,7 +361,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
   static_assert(8 * (2 * kStages2 + 5) <= 192, "barrier region overflows into the TMEM slot");
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_region + 192);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_region + 196);
-  volatile int* claim_slot = reinterpret_cast<volatile int*>(bar_region + 200);   // GATHER
+  volatile int* claim_slot = reinterpret_cast<volatile int*>(bar_region + 200);   // GATHER: 2 ints
   uint64_t call = 0;           // GATHER: this call's number (the header's epoch + 1)
 
   const int warp = threadIdx.x >> 5;
@@ -355,6 +410,8 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
       bool ok = true;
       // a_cols: run starts of the stage after the current one, loaded ahead.
       int64_t nxt0 = 0, nxt1 = 0;
+      int snap_kb = -16;            // GATHER: first k atom of the last flag snapshot
+      uint32_t ready_bits = 0;
       if (p.a_cols) {
         nxt0 = run_start_load(p.a_cols, 0);
         if (num_kb > 1) nxt1 = run_start_load(p.a_cols, 1);
@@ -387,12 +444,28 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
             for (int a = 0; a < atoms; ++a)
               tma_load_2d_pair(b_s + a * C::kBAtomBytes, &tmap_b, (ks * kAtoms2 + a) * kBK2, b_row,
                                leader_full);
-            const int hp = 2 * m_blk + static_cast<int>(rank);
+            // The flags of this half-panel are read 16 at a time (ready_bits
+            // covers k atoms [snap_kb, snap_kb + 16)); only an atom that was not
+            // ready in the last snapshot takes a fresh snapshot and, if still
+            // not ready, polls its own flag.
+            const unsigned long long* hp_flags =
+                p.ghdr + 4 + static_cast<int64_t>(2 * m_blk + static_cast<int>(rank)) * p.num_kb;
+            if (ks == 0) snap_kb = -16;
             for (int a = 0; a < atoms; ++a) {
               const int kb = ks * kAtoms2 + a;
-              const unsigned long long* flag = p.ghdr + 4 + static_cast<int64_t>(hp) * p.num_kb + kb;
-              if (!wait_flag_eq(flag, call, abort_flag, p.err)) { ok = false; break; }
-              fence_proxy_async_global();   // the gatherers' generic stores -> our TMA reads
+              bool ready = kb - snap_kb < 16 && ((ready_bits >> (kb - snap_kb)) & 1u);
+              if (!ready) {
+                snap_kb = kb;
+                ready_bits = flags_ready(hp_flags + kb, min(16, num_kb - kb), call);
+                if (!(ready_bits & 1u) && !wait_flag_eq(hp_flags + kb, call, abort_flag, p.err)) {
+                  ok = false;
+                  break;
+                }
+                // One proxy fence after each acquisition orders everything it
+                // made visible (the gatherers' generic stores) before all of our
+                // later TMA reads; atoms covered by an earlier snapshot need none.
+                fence_proxy_async_global();
+              }
               tma_load_2d_pair(a_s + a * kAAtomBytes2, &tmap_a, kb * kBK2, a_row, leader_full);
             }
             if (!ok) break;
@@ -594,8 +667,15 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
   if constexpr (GATHER) {
     // The last CTA to finish moves the epoch on (every CTA has read it by now).
     // Thread 0 is the TMA producer, which read the call number after its wait.
-    if (threadIdx.x == 0 && tagged_add(p.ghdr + 2, call, 1u) + 1u == gridDim.x)
+    if (threadIdx.x == 0 && tagged_add(p.ghdr + 2, call, 1u) + 1u == gridDim.x) {
+      // Both counters start the next call at zero under its number, so its
+      // first claims take the single-atomicAdd path.
+      constexpr uint64_t kTagMask = (uint64_t{1} << (64 - kCountBits)) - 1;
+      const uint64_t next = ((call + 1) & kTagMask) << kCountBits;
+      p.ghdr[1] = next;
+      p.ghdr[2] = next;
       st_release_gpu_u64(p.ghdr, call);
+    }
   }
 }
 
