@@ -67,6 +67,42 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
 
 _lib: ctypes.CDLL | None = None
 _lib_lock = threading.Lock()
+_api = None
+# Entry points the CPython fast-call module (_gwfast, built from csrc/gw_pyfast.c)
+# binds; the same arguments as the ctypes functions, a fraction of the host time.
+FAST_ENTRIES = ("gw_gather_gemm", "gw_gather_gemm_dev", "gw_packed_gemm", "gw_gather_columns",
+                "gw_gather_rows_t", "gw_gather_columns_dev", "gw_gather_rows_t_dev", "gw_mask_compact",
+                "gw_gather_gemm_workspace_bytes")
+
+
+class _Api:
+    """The library's entry points by C name: the fast-call binding where it covers
+    them and the one library copy checks out, else the ctypes functions."""
+
+    def __init__(self, lib: ctypes.CDLL):
+        for name in SIGNATURES:
+            setattr(self, name, getattr(lib, name))
+        self.fast = False
+        try:
+            from ghostweight_triton_b200 import _gwfast
+        except ImportError:
+            return
+        if _gwfast.library_anchor() != ctypes.cast(lib.gw_version, ctypes.c_void_p).value:
+            return          # a second copy of the library: keep everything on ctypes
+        for name in FAST_ENTRIES:
+            setattr(self, name, getattr(_gwfast, name[3:]))
+        self.fast = True
+
+
+def api() -> _Api:
+    """Entry points of the loaded library (see _Api); loads it on first use."""
+    global _api
+    if _api is None:
+        lib = load()
+        with _lib_lock:
+            if _api is None:
+                _api = _Api(lib)
+    return _api
 
 
 class GhostweightError(RuntimeError):
@@ -204,7 +240,7 @@ def mask_compact(x: torch.Tensor, threshold: float, mask: torch.Tensor | None = 
     rows, cols = x.shape
     ws = mask_workspace(x.device, cols)
     with _on_device(x.device):
-        st = load().gw_mask_compact(
+        st = api().gw_mask_compact(
             _ptr(x), dtype_code(x.dtype), rows, cols, max(x.stride(0), cols), float(threshold),
             _ptr(mask), _ptr(alive_idx), _ptr(count), _ptr(ws), ws.numel(), _stream(x.device))
     _check(st, "gw_mask_compact")
@@ -218,7 +254,7 @@ def gather_columns(src: torch.Tensor, idx: torch.Tensor, dst: torch.Tensor, pad_
     n = idx.numel()
     pad = n if pad_to is None else int(pad_to)
     with _on_device(src.device):
-        st = load().gw_gather_columns(
+        st = api().gw_gather_columns(
             _ptr(src), dtype_code(src.dtype), rows, cols, max(src.stride(0), cols), _ptr(idx), n,
             _ptr(dst), max(dst.stride(0), pad), pad, _stream(src.device))
     _check(st, "gw_gather_columns")
@@ -245,14 +281,24 @@ def gather_rows_t(src: torch.Tensor, idx: torch.Tensor, dst: torch.Tensor, pad_t
     n = idx.numel()
     pad = n if pad_to is None else int(pad_to)
     with _on_device(src.device):
-        st = load().gw_gather_rows_t(
+        st = api().gw_gather_rows_t(
             _ptr(src), dtype_code(src.dtype), rows, cols, max(src.stride(0), cols), _ptr(idx), n,
             _ptr(dst), max(dst.stride(0), pad), pad, _stream(src.device))
     _check(st, "gw_gather_rows_t")
 
 
+_ws_bytes: dict[tuple[int, int, torch.dtype], int] = {}
+
+
 def gather_gemm_workspace_bytes(M: int, n_alive: int, dtype: torch.dtype) -> int:
-    return int(load().gw_gather_gemm_workspace_bytes(int(M), int(n_alive), dtype_code(dtype)))
+    key = (M, n_alive, dtype)
+    n = _ws_bytes.get(key)
+    if n is None:
+        n = int(api().gw_gather_gemm_workspace_bytes(int(M), int(n_alive), dtype_code(dtype)))
+        if len(_ws_bytes) > 4096:
+            _ws_bytes.clear()
+        _ws_bytes[key] = n
+    return n
 
 
 # GEMM workspaces reused across calls: one per (device, stream), grown as
@@ -297,8 +343,8 @@ def gather_gemm(x: torch.Tensor, w_packed: torch.Tensor, idx: torch.Tensor, y: t
     if dev != cur:
         torch.cuda.set_device(dev)
     try:
-        st = load().gw_gather_gemm(
-            x.data_ptr(), dtype_code(x.dtype), M, K, max(x.stride(0), K), w_packed.data_ptr(), N,
+        st = api().gw_gather_gemm(
+            x.data_ptr(), DTYPE_CODES[x.dtype], M, K, max(x.stride(0), K), w_packed.data_ptr(), N,
             max(w_packed.stride(0), n), idx.data_ptr(), n, _ptr(bias), epilogue_code(activation),
             y.data_ptr(), max(y.stride(0), N), GEMM_STRATEGIES[strategy], ws_ptr, ws_bytes,
             _raw_stream(dev) if _raw_stream is not None else torch.cuda.current_stream().cuda_stream)
@@ -317,7 +363,7 @@ def gather_columns_dev(src: torch.Tensor, idx: torch.Tensor, n_dev: torch.Tensor
     assert idx.dtype == torch.int64 and n_dev.dtype == torch.int32
     rows, cols = src.shape
     with _on_device(src.device):
-        st = load().gw_gather_columns_dev(
+        st = api().gw_gather_columns_dev(
             _ptr(src), dtype_code(src.dtype), rows, cols, max(src.stride(0), cols), _ptr(idx),
             idx.numel(), _ptr(n_dev), _ptr(dst), max(dst.stride(0), pad_to), int(pad_to),
             _stream(src.device))
@@ -331,7 +377,7 @@ def gather_rows_t_dev(src: torch.Tensor, idx: torch.Tensor, n_dev: torch.Tensor,
     assert idx.dtype == torch.int64 and n_dev.dtype == torch.int32
     rows, cols = src.shape
     with _on_device(src.device):
-        st = load().gw_gather_rows_t_dev(
+        st = api().gw_gather_rows_t_dev(
             _ptr(src), dtype_code(src.dtype), rows, cols, max(src.stride(0), cols), _ptr(idx),
             idx.numel(), _ptr(n_dev), _ptr(dst), max(dst.stride(0), pad_to), int(pad_to),
             _stream(src.device))
@@ -352,7 +398,7 @@ def gather_gemm_dev(x: torch.Tensor, w_packed: torch.Tensor, idx: torch.Tensor, 
         workspace = gemm_workspace(x.device, nbytes) if nbytes else None
     ws_ptr, ws_bytes = (None, 0) if workspace is None else (workspace.data_ptr(), workspace.numel() * workspace.element_size())
     with _on_device(x.device):
-        st = load().gw_gather_gemm_dev(
+        st = api().gw_gather_gemm_dev(
             _ptr(x), dtype_code(x.dtype), M, K, max(x.stride(0), K), _ptr(w_packed), N,
             w_packed.stride(0), _ptr(idx), n, _ptr(n_dev), _ptr(bias), epilogue_code(activation),
             _ptr(y), max(y.stride(0), N), ws_ptr, ws_bytes, _stream(x.device))
@@ -397,7 +443,7 @@ def packed_gemm(a: torch.Tensor, w_packed: torch.Tensor, y: torch.Tensor,
     M, K = a.shape
     N = w_packed.shape[0]
     with _on_device(a.device):
-        st = load().gw_packed_gemm(
+        st = api().gw_packed_gemm(
             _ptr(a), dtype_code(a.dtype), M, K, max(a.stride(0), K), _ptr(w_packed), N,
             max(w_packed.stride(0), K), _ptr(bias), epilogue_code(activation), _ptr(y),
             max(y.stride(0), N), _stream(a.device))

@@ -16,6 +16,7 @@ import os
 import shutil
 import subprocess
 import sys
+import sysconfig
 from pathlib import Path
 
 CSRC = Path(__file__).resolve().parent
@@ -87,13 +88,47 @@ def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | N
                 if res.returncode != 0:
                     raise RuntimeError(f"nvcc failed on {cmd[-3]}")
     if force or jobs or _stale(LIB_PATH, objs):
-        cmd = [nvcc, *ARCH_FLAGS, "-shared", "-o", str(LIB_PATH), *map(str, objs)]
+        cmd = [nvcc, *ARCH_FLAGS, "-shared", "-Xlinker", f"-soname={LIB_NAME}", "-o", str(LIB_PATH),
+               *map(str, objs)]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if verbose or res.returncode != 0:
             sys.stderr.write(" ".join(cmd) + "\n" + res.stdout + res.stderr)
         if res.returncode != 0:
             raise RuntimeError("link of libghostweight_b200.so failed")
+    build_fast(force=force, verbose=verbose)
     return LIB_PATH
+
+
+FAST_SRC = CSRC / "gw_pyfast.c"
+
+
+def fast_module_path() -> Path:
+    suffix = sysconfig.get_config_var("EXT_SUFFIX") or ".so"
+    return PKG / f"_gwfast{suffix}"
+
+
+def build_fast(force: bool = False, verbose: bool = False) -> Path | None:
+    """Compile the CPython fast-call bindings (gw_pyfast.c) against libghostweight_b200.so.
+
+    Plain C against the Python headers (no torch), linked to the library in this
+    directory through an $ORIGIN run path. Returns None (the ctypes binding is
+    used instead) when no C compiler or no Python headers are available.
+    """
+    out = fast_module_path()
+    cc = os.environ.get("CC") or shutil.which("gcc") or shutil.which("cc")
+    inc = sysconfig.get_paths().get("include")
+    if not cc or not inc or not (Path(inc) / "Python.h").exists():
+        return None
+    if not force and not _stale(out, [FAST_SRC, LIB_PATH, INCLUDE / "ghostweight_b200.h", Path(__file__)]):
+        return out
+    cmd = [cc, "-O2", "-shared", "-fPIC", "-std=c11", f"-I{inc}", f"-I{INCLUDE}", str(FAST_SRC),
+           f"-L{PKG}", "-l:" + LIB_NAME, "-Wl,-rpath,$ORIGIN", "-o", str(out)]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if verbose or res.returncode != 0:
+        sys.stderr.write(" ".join(cmd) + "\n" + res.stdout + res.stderr)
+    if res.returncode != 0:
+        raise RuntimeError("build of the fast-call bindings failed")
+    return out
 
 
 def main() -> None:

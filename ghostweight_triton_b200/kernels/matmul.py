@@ -59,24 +59,89 @@ def ghostweight_matmul(
     K_w, N = weights.shape
     assert K == K_w, f"K mismatch: A K={K}, W K={K_w}"
 
-    activations = activations.contiguous()
-    weights = weights.contiguous()
-    alive_indices = alive_indices.contiguous().to(device=activations.device, dtype=torch.int64)
+    if not activations.is_contiguous():
+        activations = activations.contiguous()
+    if not weights.is_contiguous():
+        weights = weights.contiguous()
+    if alive_indices.dtype != torch.int64 or alive_indices.device != activations.device:
+        alive_indices = alive_indices.to(device=activations.device, dtype=torch.int64)
+    if not alive_indices.is_contiguous():
+        alive_indices = alive_indices.contiguous()
     C = torch.empty((M, N), dtype=activations.dtype, device=activations.device)
     if M == 0 or N == 0:
         return C
-    w_packed = pack_weight(weights.t(), alive_indices, dtype=activations.dtype)
-    if bias is not None:
+    w_packed = _packed_cache.get(weights, alive_indices, activations.dtype)
+    if bias is not None and (bias.dtype != activations.dtype or not bias.is_contiguous()):
         bias = bias.contiguous().to(dtype=activations.dtype)
     _gemm(activations, w_packed, alive_indices, C, bias, activation, strategy)
     return C
+
+
+class _PackedCache:
+    """Packed weights of recent ghostweight_matmul calls.
+
+    The reference API passes the weight [K, N] and the alive list on every
+    call, and a loop over layers passes the same tensors again and again; the
+    packing (a transposing gather of W[alive, :]) is then done once. An entry
+    is used only for the very same tensor objects (held by weak reference, so
+    an entry never outlives its weight) at the same in-place version counts
+    (any in-place update of either tensor, or of a view sharing their storage,
+    changes them) and the same output dtype. Small LRU: at most `max_entries`
+    entries and `max_bytes` of packed data.
+    """
+
+    def __init__(self, max_entries: int = 32, max_bytes: int = 2 << 30):
+        import collections
+        import weakref
+
+        self._weakref = weakref
+        self._entries: "collections.OrderedDict" = collections.OrderedDict()
+        self.max_entries = max_entries
+        self.max_bytes = max_bytes
+        self.bytes = 0
+
+    def get(self, weights: torch.Tensor, idx: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+        key = (id(weights), id(idx), dtype)
+        e = self._entries.get(key)
+        if e is not None:
+            w_ref, i_ref, w_ver, i_ver, packed = e
+            if (w_ref() is weights and i_ref() is idx and w_ver == weights._version
+                    and i_ver == idx._version and not torch.cuda.is_current_stream_capturing()):
+                self._entries.move_to_end(key)
+                return packed
+            self._drop(key)
+        packed = pack_weight(weights.t(), idx, dtype=dtype)
+        if torch.cuda.is_current_stream_capturing():
+            return packed           # a graph's private pool: do not keep it
+        nbytes = packed.untyped_storage().nbytes()
+        if nbytes > self.max_bytes:
+            return packed
+        cb = lambda _ref, key=key: self._drop(key)
+        self._entries[key] = (self._weakref.ref(weights, cb), self._weakref.ref(idx, cb),
+                              weights._version, idx._version, packed)
+        self.bytes += nbytes
+        while len(self._entries) > self.max_entries or self.bytes > self.max_bytes:
+            self._drop(next(iter(self._entries)))
+        return packed
+
+    def _drop(self, key) -> None:
+        e = self._entries.pop(key, None)
+        if e is not None:
+            self.bytes -= e[4].untyped_storage().nbytes()
+
+    def clear(self) -> None:
+        self._entries.clear()
+        self.bytes = 0
+
+
+_packed_cache = _PackedCache()
 
 
 def _gemm(x, w_packed, idx, y, bias, activation, strategy):
     ws = None
     if strategy == "runs" and (x.data_ptr() % 16 or x.stride(0) % 8):
         strategy = "auto"          # direct TMA of x needs 16-byte aligned rows
-    if strategy not in ("fused", "runs") and x.dtype != torch.float32:
+    if strategy != "fused" and strategy != "runs" and x.dtype is not torch.float32:
         nbytes = _native.gather_gemm_workspace_bytes(x.shape[0], idx.numel(), x.dtype)
         if nbytes:
             ws = _native.gemm_workspace(x.device, nbytes)
@@ -101,7 +166,8 @@ def ghost_linear(
 ) -> torch.Tensor:
     """y = act(x[:, alive] @ w_packed^T + bias) for x [M, K], w_packed [N, K_alive]."""
     assert x.ndim == 2 and x.is_cuda
-    x = x.contiguous()
+    if not x.is_contiguous():
+        x = x.contiguous()
     M = x.shape[0]
     N = w_packed.shape[0]
     y = out if out is not None else torch.empty((M, N), dtype=x.dtype, device=x.device)

@@ -143,7 +143,7 @@ class GhostLinear(nn.Module):
         # weight, its dtype/device or the index list changes.
         self._packed: tuple[tuple, torch.Tensor] | None = None
         # (key, whether the frozen list is made of 64-column runs), same key rule.
-        self._runs: tuple[tuple, bool] | None = None
+        self._runs: tuple | None = None
         # Dynamic mode without host synchronisation (see the module docstring).
         self.sync_free: bool = True
         self._readback = _CountReadback()
@@ -202,25 +202,30 @@ class GhostLinear(nn.Module):
 
     # ------------------------------------------------------------------ forward
     def _weight_packed(self, alive: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+        """W' for the frozen list, rebuilt when the weight (object, storage or an
+        in-place update), the list or the dtype changes. The check is a few
+        identity and integer compares, so a frozen forward pays no hashing."""
         w = self.weight
-        key = (w.data_ptr(), w._version, tuple(w.stride()), dtype, w.device,
-               alive.data_ptr(), alive.numel(), alive._version)
-        if self._packed is not None and self._packed[0] == key:
-            return self._packed[1]
+        c = self._packed
+        if c is not None:
+            k = c[0]
+            if (k[0] is w and k[1] == w._version and k[2] == w.data_ptr() and k[3] is alive
+                    and k[4] == alive._version and k[5] is dtype):
+                return c[1]
         packed = pack_weight(w.detach(), alive, dtype=dtype)
-        self._packed = (key, packed)
+        self._packed = ((w, w._version, w.data_ptr(), alive, alive._version, dtype), packed)
         return packed
 
     def _alive_runs(self, alive: torch.Tensor) -> bool:
         """Whether the frozen list is made of 64-column runs (checked once per list,
         which reads one count on the host; inside CUDA-graph capture an unchecked
         list takes the gather path instead)."""
-        key = (alive.data_ptr(), alive.numel(), alive._version, alive.device)
-        if self._runs is None or self._runs[0] != key:
+        r = self._runs
+        if r is None or r[0] is not alive or r[1] != alive._version:
             if torch.cuda.is_current_stream_capturing():
                 return False
-            self._runs = (key, index_runs(alive, self.in_features) == 0)
-        return self._runs[1]
+            r = self._runs = (alive, alive._version, index_runs(alive, self.in_features) == 0)
+        return r[2]
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         """x : [..., in_features] -> [..., out_features] (arbitrary batch dims)."""
@@ -243,7 +248,7 @@ class GhostLinear(nn.Module):
         self._last_sparsity = float(sparsity)
 
         bias = self.bias
-        if bias is not None and bias.dtype != x_2d.dtype:
+        if bias is not None and bias.dtype is not x_2d.dtype:
             bias = bias.to(x_2d.dtype)
         if sparsity < self.min_sparsity_to_activate or k_alive == 0:
             out = F.linear(x_2d, self.weight.to(x_2d.dtype), bias)
@@ -253,7 +258,7 @@ class GhostLinear(nn.Module):
             strategy = "auto"
             if frozen:
                 w_packed = self._weight_packed(alive, x_2d.dtype)
-                if x_2d.dtype != torch.float32 and self._alive_runs(alive):
+                if x_2d.dtype is not torch.float32 and self._alive_runs(alive):
                     strategy = "runs"
             else:
                 w_packed = pack_weight(self.weight.detach(), alive, dtype=x_2d.dtype)
