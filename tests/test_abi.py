@@ -127,3 +127,25 @@ def test_ctypes_signatures_match_arity(lib):
         assert m, name
         params = [p for p in m.group(1).split(",") if p.strip() and p.strip() != "void"]
         assert len(params) == len(args), f"{name}: header has {len(params)} params, binding {len(args)}"
+
+
+def test_fast_call_binding_shares_the_library(lib):
+    """The CPython fast-call module binds the same library copy ctypes loaded, and
+    covers the hot entry points with the same argument lists."""
+    import ctypes as C
+
+    api = _native.api()
+    assert api.fast, "fast-call module not built or bound to a second library copy"
+    from ghostweight_triton_b200 import _gwfast
+
+    assert _gwfast.library_anchor() == C.cast(lib.gw_version, C.c_void_p).value
+    for name in _native.FAST_ENTRIES:
+        assert name in _native.SIGNATURES and hasattr(_gwfast, name[3:])
+        assert len(_native.SIGNATURES[name][1]) >= 3
+    # Pure host arithmetic through both bindings agrees.
+    for M, n, dt in [(4096, 2048, 0), (8, 64, 1), (0, 10, 0), (300, 77, 2)]:
+        assert api.gw_gather_gemm_workspace_bytes(M, n, dt) == lib.gw_gather_gemm_workspace_bytes(M, n, dt)
+    import pytest as _pt
+
+    with _pt.raises(TypeError):
+        _gwfast.gather_gemm(1, 2, 3)            # wrong argument count is a Python error, not a call
