@@ -146,9 +146,13 @@ def dist_setup(args):
 
         import torch.distributed as dist
 
-        # NCCL's communicator set-up lines (rank count per communicator) on stderr.
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        # NCCL's communicator set-up lines (the rank count of every communicator)
+        # on stderr, so that stdout keeps only the JSON line; unless the caller
+        # asked for more than INFO already.
+        if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
+            os.environ["NCCL_DEBUG"] = "INFO"
+            os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
+            os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         if args.impl == "ours":
             torch.cuda.set_device(local)
         dist.init_process_group("nccl" if args.impl == "ours" else "gloo",
