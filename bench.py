@@ -653,6 +653,7 @@ def run_ours(args, world, rank, local):
         gl.freeze_weight_mask()
         hx = [L["x"].cpu().pin_memory() for L in layers]
         hy = [torch.empty(M, N, dtype=torch.float16).pin_memory() for _ in range(2)]
+        layers_y0 = layers[0]["y"]
         # Three streams, two slots: the upload of step i+1 and the download of
         # step i-1 run while step i computes (PCIe carries both directions at
         # once). Events order each slot's reuse.
@@ -702,9 +703,14 @@ def run_ours(args, world, rank, local):
         torch.cuda.synchronize()
         e_steps = max(1, min(args.steps, 200))
         te = e2e_timed(e_steps)
+        # The link itself: one pinned 32 MiB upload and download, timed alone.
+        t_h2d = event_time(lambda i: xd[0].copy_(hx[0], non_blocking=True), iters=10)
+        t_d2h = event_time(lambda i: hy[0].copy_(layers_y0, non_blocking=True), iters=10)
         e2e = {"value": round(world * useful / (te / e_steps) / 1e12, 3), "unit": "TFLOP/s",
                "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2,
                "steps": e_steps, "ms_per_step": round(te / e_steps * 1e3, 4),
+               "pcie_h2d_GBps": round(M * K * 2 / t_h2d / 1e9, 1),
+               "pcie_d2h_GBps": round(M * N * 2 / t_d2h / 1e9, 1),
                "path": "GhostLinear.forward (frozen weight mask) with pinned-host x -> device -> pinned-host y; "
                        "upload, compute and download of consecutive steps overlap on three streams"}
 

@@ -28,7 +28,7 @@ constexpr int kColChunk = 32 * kColsPerLane;       // 256 output columns per CTA
 
 // Column index codes held in registers: >= 0 source column, -1 write zero.
 template <typename raw>
-__global__ void __launch_bounds__(kGThreads, 8)
+__global__ void __launch_bounds__(kGThreads)
 gather_columns_kernel(const raw* __restrict__ src, int64_t rows, int64_t ld_src, int64_t cols_src,
                       const int64_t* __restrict__ idx, int64_t n_idx, raw* __restrict__ dst,
                       int64_t ld_dst, int64_t pad_to, unsigned int* err, int early_dependents,
@@ -56,22 +56,19 @@ gather_columns_kernel(const raw* __restrict__ src, int64_t rows, int64_t ld_src,
     if (c0 >= pad_to) return;
   }
 
-  // Source columns as 32-bit offsets (the launcher takes this kernel only for
-  // rows shorter than 2^31 elements): half the registers of 64-bit indices, so
-  // that eight CTAs fit on an SM and the grid runs in one wave.
-  int32_t scol[kColsPerLane];
-  uint32_t live = 0;
+  int64_t scol[kColsPerLane];
+  bool live[kColsPerLane];
   bool bad = false;
 #pragma unroll
   for (int e = 0; e < kColsPerLane; ++e) {
     const int64_t j = c0 + lane + 32 * e;
-    if (j < pad_to) live |= 1u << e;
+    live[e] = j < pad_to;
     int64_t c = -1;
     if (j < n_idx) {
       c = __ldg(idx + j);
       if (c < 0 || c >= cols_src) { bad = true; c = -1; }
     }
-    scol[e] = static_cast<int32_t>(c);
+    scol[e] = c;
   }
   if (bad && blockIdx.y == 0 && warp == 0) raise_error(err, GW_DERR_BAD_INDEX);
 
@@ -84,7 +81,7 @@ gather_columns_kernel(const raw* __restrict__ src, int64_t rows, int64_t ld_src,
     for (int e = 0; e < kColsPerLane; ++e) vals[e] = (scol[e] >= 0) ? __ldg(srow + scol[e]) : raw(0);
 #pragma unroll
     for (int e = 0; e < kColsPerLane; ++e)
-      if ((live >> e) & 1u) drow[c0 + lane + 32 * e] = vals[e];
+      if (live[e]) drow[c0 + lane + 32 * e] = vals[e];
   }
 }
 
@@ -216,19 +213,8 @@ cudaError_t launch_gather_columns(const void* src, int dtype, int64_t rows, int6
                                   int sm_count, cudaStream_t stream, bool early_dependents,
                                   const int32_t* n_dev) {
   if (rows == 0 || pad_to == 0) return cudaSuccess;
-  if (cols_src > 0x7FFFFFFFll) return cudaErrorInvalidValue;     // 32-bit column offsets
   const int64_t col_blocks = (pad_to + kColChunk - 1) / kColChunk;
-  // One wave: as many CTAs as are resident at once on all SMs.
-  static int resident = [] {
-    int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gather_columns_kernel<uint16_t>, kGThreads, 0) !=
-            cudaSuccess || n < 1) {
-      cudaGetLastError();
-      n = 4;
-    }
-    return n;
-  }();
-  const int64_t target = static_cast<int64_t>(sm_count > 0 ? sm_count : 148) * resident;
+  const int64_t target = static_cast<int64_t>(sm_count > 0 ? sm_count : 148) * 8;
   const unsigned gy = clamp_grid(std::min<int64_t>((rows + kGWarps - 1) / kGWarps,
                                                    (target + col_blocks - 1) / col_blocks),
                                  65535);
