@@ -59,6 +59,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gw_index_runs": (_i, [_vp, _i64, _i64, _vp, _vp]),
     "gw_gemm_plan": (_i, [_i64, _i64, _i64, ctypes.POINTER(_i), ctypes.POINTER(_i), ctypes.POINTER(_i)]),
     "gw_selftest_wait_timeout": (_i, [_i64, _vp]),
+    "gw_dynamic_linear": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _i64, _d, _vp, _i, _vp, _i64,
+                               _vp, _vp, _vp]),
     "gw_gather_columns_dev": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _i64, _i64, _vp]),
     "gw_gather_rows_t_dev": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _i64, _i64, _vp]),
     "gw_gather_gemm_dev": (_i, [_vp, _i, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _vp, _i,
@@ -70,7 +72,7 @@ _lib_lock = threading.Lock()
 _api = None
 # Entry points the CPython fast-call module (_gwfast, built from csrc/gw_pyfast.c)
 # binds; the same arguments as the ctypes functions, a fraction of the host time.
-FAST_ENTRIES = ("gw_gather_gemm", "gw_gather_gemm_dev", "gw_packed_gemm", "gw_gather_columns",
+FAST_ENTRIES = ("gw_gather_gemm", "gw_gather_gemm_dev", "gw_packed_gemm", "gw_gather_columns", "gw_dynamic_linear",
                 "gw_gather_rows_t", "gw_gather_columns_dev", "gw_gather_rows_t_dev", "gw_mask_compact",
                 "gw_gather_gemm_workspace_bytes")
 
@@ -448,6 +450,25 @@ def packed_gemm(a: torch.Tensor, w_packed: torch.Tensor, y: torch.Tensor,
             max(w_packed.stride(0), K), _ptr(bias), epilogue_code(activation), _ptr(y),
             max(y.stride(0), N), _stream(a.device))
     _check(st, "gw_packed_gemm")
+
+
+def dynamic_linear(x: torch.Tensor, weight: torch.Tensor, threshold: float, y: torch.Tensor,
+                   bias: torch.Tensor | None = None, activation: str | None = None,
+                   count: torch.Tensor | None = None, mask: torch.Tensor | None = None) -> int:
+    """Mask of x's columns and the sparse layer y = act(x[:, alive] @ weight[:, alive]^T + bias)
+    in one launch (gw_dynamic_linear). Returns the gw_status: GW_ERR_UNSUPPORTED for shapes
+    or layouts the single launch does not take (the caller then runs the separate kernels);
+    raises on any other error."""
+    M, K = x.shape
+    N = weight.shape[0]
+    with _on_device(x.device):
+        st = api().gw_dynamic_linear(
+            x.data_ptr(), DTYPE_CODES[x.dtype], M, K, x.stride(0), weight.data_ptr(), N,
+            weight.stride(0), float(threshold), _ptr(bias), epilogue_code(activation), y.data_ptr(),
+            y.stride(0), _ptr(count), _ptr(mask), _stream(x.device))
+    if st != GW_OK and st != GW_ERR_UNSUPPORTED:
+        _check(st, "gw_dynamic_linear")
+    return st
 
 
 def validate_indices(idx: torch.Tensor, K: int) -> int:

@@ -600,6 +600,33 @@ int gw_gather_gemm_peers(const void* x, int dtype, int64_t M, int64_t K, int64_t
   return e == cudaSuccess ? GW_OK : cuda_fail(e);
 }
 
+int gw_dynamic_linear(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
+                      const void* w, int64_t N, int64_t ldw, double threshold, const void* bias,
+                      int epilogue, void* y, int64_t ldy, int32_t* alive_count, int32_t* mask,
+                      void* stream) {
+  if (dtype != GW_DTYPE_F16 && dtype != GW_DTYPE_BF16) return GW_ERR_DTYPE;
+  if (!valid_epi(epilogue)) return GW_ERR_UNSUPPORTED;
+  if (!matrix_ok(M, K, ldx) || !matrix_ok(N, K, ldw) || !matrix_ok(M, N, ldy)) return GW_ERR_SHAPE;
+  if (!gw::dyn_linear_supported(M, K) || N > int64_t{65535} * 128) return GW_ERR_UNSUPPORTED;
+  if (!aligned16(x) || !aligned16(w) || (ldx % 8) != 0 || (ldw % 8) != 0) return GW_ERR_UNSUPPORTED;
+  const gw::DeviceInfo* d = nullptr;
+  int st = current_device(&d);
+  if (st != GW_OK) return st;
+  if (N == 0) {
+    if (alive_count) {
+      cudaError_t e = cudaMemsetAsync(alive_count, 0, sizeof(int32_t), static_cast<cudaStream_t>(stream));
+      if (e != cudaSuccess) return cuda_fail(e);
+    }
+    return GW_OK;
+  }
+  if (!x || !w || !y) return GW_ERR_NULL;
+  // The reference passes the threshold as an fp32 kernel scalar (mask.py:100).
+  cudaError_t e = gw::launch_dyn_linear(x, dtype, M, K, ldx, w, N, ldw, static_cast<float>(threshold),
+                                        bias, epilogue, y, ldy, alive_count, mask, d->err_word,
+                                        static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? GW_OK : cuda_fail(e);
+}
+
 int gw_packed_gemm(const void* a, int dtype, int64_t M, int64_t K, int64_t lda,
                    const void* w_packed, int64_t N, int64_t ldw, const void* bias, int epilogue,
                    void* y, int64_t ldy, void* stream) {

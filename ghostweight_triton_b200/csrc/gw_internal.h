@@ -161,6 +161,16 @@ cudaError_t launch_gemm_decode_gather(const DecodePlan& plan, const void* x, int
                                       int epilogue, void* y, int64_t ldy, unsigned int* err,
                                       cudaStream_t stream);
 
+// gw_gemm_dyn.cu: the per-forward activation mask, its compaction and the
+// gather-GEMM in one clustered launch, for at most 32 rows (fp16/bf16; x and
+// W rows 16-byte aligned, K a multiple of 8, K <= 8192). count (the alive
+// count) and mask (int32 [K]) are optional outputs.
+bool dyn_linear_supported(int64_t M, int64_t K);
+cudaError_t launch_dyn_linear(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
+                              const void* w, int64_t N, int64_t ldw, float thr, const void* bias,
+                              int epilogue, void* y, int64_t ldy, int32_t* count, int32_t* mask,
+                              unsigned int* err, cudaStream_t stream);
+
 // Driver entry point for cuTensorMapEncodeTiled (resolved once, no libcuda link).
 void* tensor_map_encoder();
 // 2-D tile map over a [rows, cols] 16-bit row-major matrix with row stride ld

@@ -140,6 +140,14 @@ static PyObject* fast_mask_compact(PyObject* self, PyObject* const* args, Py_ssi
                                          a[9].p, a[10].z, a[11].p));
 }
 
+static PyObject* fast_dynamic_linear(PyObject* self, PyObject* const* args, Py_ssize_t nargs) {
+  (void)self;
+  GW_PARSE("pilllplldpiplppp")
+  return PyLong_FromLong(gw_dynamic_linear(a[0].p, a[1].i, a[2].l, a[3].l, a[4].l, a[5].p, a[6].l,
+                                           a[7].l, a[8].d, a[9].p, a[10].i, a[11].p, a[12].l,
+                                           (int32_t*)a[13].p, (int32_t*)a[14].p, a[15].p));
+}
+
 static PyObject* fast_gather_gemm_workspace_bytes(PyObject* self, PyObject* const* args,
                                                   Py_ssize_t nargs) {
   (void)self;
@@ -169,6 +177,7 @@ static PyMethodDef gw_fast_methods[] = {
     GW_FAST(gather_columns_dev),
     GW_FAST(gather_rows_t_dev),
     GW_FAST(mask_compact),
+    GW_FAST(dynamic_linear),
     GW_FAST(gather_gemm_workspace_bytes),
     GW_FAST(library_anchor),
     {NULL, NULL, 0, NULL},

@@ -35,6 +35,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from ghostweight_triton_b200 import _native
 from ghostweight_triton_b200.kernels.gather import pack_weight, pack_weight_dev
 from ghostweight_triton_b200.kernels.mask import dead_neuron_mask_compact, alive_indices as _alive
 from ghostweight_triton_b200.kernels.matmul import ghost_linear, ghost_linear_dev, index_runs
@@ -268,12 +269,24 @@ class GhostLinear(nn.Module):
 
     def _forward_sync_free(self, x_2d: torch.Tensor) -> torch.Tensor:
         """Dynamic-mask forward whose alive count never leaves the device."""
-        _, buf, count = dead_neuron_mask_compact(x_2d, self.threshold, want_mask=False)
         bias = self.bias
         if bias is not None and bias.dtype != x_2d.dtype:
             bias = bias.to(x_2d.dtype)
         prev = self._readback.ready()           # the previous forward's count, if it has landed
         dense = prev is not None and 1.0 - prev / self.in_features < self.min_sparsity_to_activate
+        if not dense and x_2d.shape[0] <= 32 and x_2d.dtype in (torch.float16, torch.bfloat16):
+            # At most 32 rows: mask, compaction and the sparse product in one
+            # launch (gw_dynamic_linear), reading x and W once.
+            w = self.weight.detach()
+            if w.dtype is x_2d.dtype and w.stride(1) == 1 and x_2d.stride(1) == 1:
+                y = torch.empty((x_2d.shape[0], self.out_features), dtype=x_2d.dtype, device=x_2d.device)
+                count = torch.empty(1, dtype=torch.int32, device=x_2d.device)
+                if _native.dynamic_linear(x_2d, w, self.threshold, y, bias=bias, activation=self.activation,
+                                          count=count) == _native.GW_OK:
+                    self._readback.record(count)
+                    self._sparsity_pending = True
+                    return y
+        _, buf, count = dead_neuron_mask_compact(x_2d, self.threshold, want_mask=False)
         if dense:
             out = F.linear(x_2d, self.weight.to(x_2d.dtype), bias)
             if self.activation is not None:

@@ -302,6 +302,30 @@ GW_API int gw_gather_gemm_dev(const void* x, int dtype, int64_t M, int64_t K, in
                               size_t workspace_bytes, void* stream);
 
 /*
+ * The dynamic-mask layer in one launch, for at most 32 rows (decoding and
+ * small batches):
+ *   alive[k] = max(0, max_m fp32(|x[m, k]|)) > fp32(threshold)    (NaN ignored)
+ *   y[m, n]  = act( sum_{alive k} x[m, k] * w[n, k] + bias[n] )
+ * x [M, K] (ldx), w = nn.Linear.weight [N, K] (ldw), bias [N] or NULL, y [M, N]
+ * (ldy); fp16 or bf16 with fp32 accumulation and one rounding. alive_count
+ * (int32, device) and mask (int32 [K], 1 = alive) are optional outputs.
+ *
+ * Replaces the dynamic forward of ghostweight_triton/module.py:103-117
+ * (dead_neuron_mask, torch.nonzero, ghostweight_matmul and the bias add): one
+ * launch that reads x and w once, no index list in memory, no host
+ * synchronisation. The k range is split over the original columns across a
+ * cluster of CTAs, each of which masks, compacts and multiplies its own
+ * columns; partial sums are reduced in distributed shared memory.
+ * Requires 1 <= M <= 32, K a multiple of 8 and at most 8192, x and w 16-byte
+ * aligned, ldx and ldw multiples of 8; other requests return
+ * GW_ERR_UNSUPPORTED (gw_mask_compact with the *_dev entry points covers them).
+ */
+GW_API int gw_dynamic_linear(const void* x, int dtype, int64_t M, int64_t K, int64_t ldx,
+                             const void* w, int64_t N, int64_t ldw, double threshold,
+                             const void* bias, int epilogue, void* y, int64_t ldy,
+                             int32_t* alive_count, int32_t* mask, void* stream);
+
+/*
  * Dense GEMM over an already-compacted activation (the two-step path of
  * gather.py:1-14: gather_compact followed by a matmul):
  *   y[m, n] = act( sum_{j < K} a[m, j] * w_packed[n, j] + bias[n] )
