@@ -66,7 +66,11 @@ struct DyCfg {
   static constexpr int kPartStride = MP + 4;                // floats per feature row (16-byte rows)
   static constexpr int kPartBytes = kDyN * kPartStride * 4;
   static constexpr int kTmemCols = 32;
-  static constexpr int kSmemBytes = 1024 + kWBytes + kXBytes + 1024;
+  // Per warp, two rows of W's range staged densely (kStageRows x 1 KB).
+  static constexpr int kStageRows = 4;
+  static constexpr int kStageBytes = 8 * kStageRows * kDyKS * 2;   // 32 KB
+  static constexpr int kMiscBytes = 2048;                          // bits, positions, alive list, barriers
+  static constexpr int kSmemBytes = 1024 + kWBytes + kXBytes + kStageBytes + kMiscBytes;
   static_assert(kPartBytes <= kWBytes, "partials live in the W' tile after the MMAs");
   static_assert(kSmemBytes <= 232448, "shared memory budget per CTA");
 };
@@ -128,21 +132,6 @@ __device__ __forceinline__ uint32_t alive8(const uint4 q, float thr) {
   return b;
 }
 
-// Stores the alive elements of one vector (columns 8 v .. 8 v + 7 of the
-// range; `bits` alive, numbered from `pos`) into row r of a tile.
-__device__ __forceinline__ void put_alive(uint32_t tile, int r, const uint4 q, uint32_t bits, int pos,
-                                          int atom_bytes) {
-  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    if ((bits >> e) & 1u) {
-      const uint16_t v = static_cast<uint16_t>((w[e >> 1] >> ((e & 1) * 16)) & 0xFFFFu);
-      asm volatile("st.shared.u16 [%0], %1;" :: "r"(tile + tile_off(r, pos, atom_bytes)), "h"(v) : "memory");
-      ++pos;
-    }
-  }
-}
-
 // 16-byte load issued only when `pred` is set (zeros otherwise); inline PTX so
 // that a batch of such loads is issued back to back, none behind a branch.
 __device__ __forceinline__ uint4 ld_nc_v4_if(const void* p, bool pred) {
@@ -165,7 +154,8 @@ __global__ void __launch_bounds__(kDyThreads, 1) gemm_dyn_kernel(const DyParams 
   uint8_t* smem = smem_raw + ((1024u - (raw_s & 1023u)) & 1023u);
   const uint32_t w_s = smem_u32(smem);              // W' tile (later: the partial sums)
   const uint32_t x_s = w_s + C::kWBytes;            // x' tile
-  uint8_t* misc = smem + C::kWBytes + C::kXBytes;
+  uint8_t* stage = smem + C::kWBytes + C::kXBytes;  // per-warp dense rows of W's range
+  uint8_t* misc = stage + C::kStageBytes;
   uint8_t* vb = misc;                                // [4][kDyVec] alive bits per row group
   int32_t* vpos = reinterpret_cast<int32_t*>(misc + 256);    // [kDyVec] first local position
   uint8_t* vmask = misc + 512;                       // [kDyVec] alive bits of the vector
@@ -173,6 +163,7 @@ __global__ void __launch_bounds__(kDyThreads, 1) gemm_dyn_kernel(const DyParams 
   const uint32_t mma_bar = smem_u32(misc + 584);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 592);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 596);
+  int16_t* acol = reinterpret_cast<int16_t*>(misc + 1024);   // [kDyKS] range column of alive p
   float* part = reinterpret_cast<float*>(smem);
 
   const int tid = threadIdx.x;
@@ -252,7 +243,8 @@ __global__ void __launch_bounds__(kDyThreads, 1) gemm_dyn_kernel(const DyParams 
 
   // ---------------------------------------------------------------- C: x' and W' tiles
   // The last k atom is zero past K'_s (the MMA reads whole 16-column steps and
-  // 0 * stale data could be NaN); then the alive values go to their places.
+  // 0 * stale data could be NaN); the alive list acol[p] = range column of the
+  // p-th alive column is written at the same time.
   if (kp & 63) {
     const uint32_t wa = w_s + static_cast<uint32_t>((nkb - 1) * C::kWAtomBytes);
     const uint32_t xa = x_s + static_cast<uint32_t>((nkb - 1) * C::kXAtomBytes);
@@ -261,39 +253,86 @@ __global__ void __launch_bounds__(kDyThreads, 1) gemm_dyn_kernel(const DyParams 
     for (int o = tid * 16; o < C::kXAtomBytes; o += kDyThreads * 16)
       asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" :: "r"(xa + o), "r"(0u) : "memory");
   }
-  __syncthreads();
-  if (v < nvec) {
-    const uint32_t mv = vmask[v];
-    const int pv = vpos[v];
-#pragma unroll
-    for (int i = 0; i < RPT; ++i) {
-      const int r = g + 4 * i;
-      if (r < rows && mv) put_alive(x_s, r, xv[i], mv, pv, C::kXAtomBytes);
+  if (tid < nvec) {
+    uint32_t mv = vmask[tid];
+    int pv = vpos[tid];
+    while (mv) {
+      const int e = __ffs(mv) - 1;
+      acol[pv++] = static_cast<int16_t>(8 * tid + e);
+      mv &= mv - 1u;
     }
   }
-  {
-    // Warp w: rows 16 w .. 16 w + 15 of the feature block; lane: vectors lane
-    // and lane + 32. Eight rows (16 loads) in flight per lane; vectors with no
-    // alive column and rows past N are not read.
-    const uint32_t mA = vmask[lane], mB = vmask[lane + 32];
-    const int pA = vpos[lane], pB = vpos[lane + 32];
-#pragma unroll 1
-    for (int rb = 0; rb < 16; rb += 8) {
-      uint4 q[8][2];
+  __syncthreads();
+  // Lane l produces alive positions p = 32 i + l: its range columns, once.
+  constexpr int kMaxI = kDyKS / 32;
+  const int ni = (kp + 31) >> 5;
+  int cp[kMaxI];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int r = warp * 16 + rb + j;
+  for (int i = 0; i < kMaxI; ++i) {
+    const int pp = 32 * i + lane;
+    cp[i] = pp < kp ? acol[pp] : 0;
+  }
+  // x': rows warp, warp + 8, ... of x, 2-byte loads of the alive columns
+  // (x is small and was just read, so these come from L2).
+  for (int r = warp; r < rows; r += 8) {
+    const uint16_t* xr = p.x + static_cast<int64_t>(r) * p.ldx + col0;
+    uint16_t xv2[kMaxI];
+#pragma unroll
+    for (int i = 0; i < kMaxI; ++i) xv2[i] = i < ni && 32 * i + lane < kp ? __ldg(xr + cp[i]) : uint16_t(0);
+#pragma unroll
+    for (int i = 0; i < kMaxI; ++i)
+      if (i < ni && 32 * i + lane < kp)
+        asm volatile("st.shared.u16 [%0], %1;" :: "r"(x_s + tile_off(r, 32 * i + lane, C::kXAtomBytes)),
+                     "h"(xv2[i]) : "memory");
+  }
+  {
+    // W': warp w handles rows 16 w .. 16 w + 15 of the feature block in four
+    // batches of four rows. A batch is read densely (16-byte loads; vectors
+    // with no alive column and rows past N are not read) into the warp's
+    // staging rows, then lane l copies alive positions 32 i + l from there
+    // into the swizzled tile. The next batch's loads are issued before the
+    // current batch is staged, so they are in flight during the copies.
+    uint8_t* st_w = stage + warp * (C::kStageRows * kDyKS * 2);
+    const uint32_t st_s = smem_u32(st_w);
+    const bool liveA = vmask[lane] != 0, liveB = vmask[lane + 32] != 0;
+    auto load_batch = [&](int b, uint4 (&q)[C::kStageRows][2]) {
+#pragma unroll
+      for (int j = 0; j < C::kStageRows; ++j) {
+        const int r = warp * 16 + b * C::kStageRows + j;
         const bool live = n0 + r < p.N;
         const uint16_t* wr = p.w + (live ? (n0 + r) * p.ldw + col0 : 0);
-        q[j][0] = ld_nc_v4_if(wr + 8 * lane, live && mA != 0u);
-        q[j][1] = ld_nc_v4_if(wr + 8 * (lane + 32), live && mB != 0u);
+        q[j][0] = ld_nc_v4_if(wr + 8 * lane, live && liveA);
+        q[j][1] = ld_nc_v4_if(wr + 8 * (lane + 32), live && liveB);
       }
+    };
+    uint4 qa[C::kStageRows][2], qb[C::kStageRows][2];
+    load_batch(0, qa);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int r = warp * 16 + rb + j;
-        if (mA) put_alive(w_s, r, q[j][0], mA, pA, C::kWAtomBytes);
-        if (mB) put_alive(w_s, r, q[j][1], mB, pB, C::kWAtomBytes);
+    for (int b = 0; b < 16 / C::kStageRows; ++b) {
+      uint4 (&cur)[C::kStageRows][2] = (b & 1) ? qb : qa;
+      uint4 (&nxt)[C::kStageRows][2] = (b & 1) ? qa : qb;
+      if (b + 1 < 16 / C::kStageRows) load_batch(b + 1, nxt);
+#pragma unroll
+      for (int j = 0; j < C::kStageRows; ++j) {
+        reinterpret_cast<uint4*>(st_w + j * kDyKS * 2)[lane] = cur[j][0];
+        reinterpret_cast<uint4*>(st_w + j * kDyKS * 2)[lane + 32] = cur[j][1];
       }
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < C::kStageRows; ++j) {
+        const int r = warp * 16 + b * C::kStageRows + j;
+#pragma unroll
+        for (int i = 0; i < kMaxI; ++i) {
+          if (i < ni && 32 * i + lane < kp) {
+            uint16_t v;
+            asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v)
+                         : "r"(st_s + static_cast<uint32_t>(j * kDyKS * 2 + cp[i] * 2)) : "memory");
+            asm volatile("st.shared.u16 [%0], %1;" :: "r"(w_s + tile_off(r, 32 * i + lane, C::kWAtomBytes)),
+                         "h"(v) : "memory");
+          }
+        }
+      }
+      __syncwarp();                                  // the staging rows are free again
     }
   }
   fence_proxy_async_smem();                          // the tiles are read by the tensor core

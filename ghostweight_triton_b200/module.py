@@ -43,6 +43,19 @@ from ghostweight_triton_b200.kernels.matmul import ghost_linear, ghost_linear_de
 _ACTIVATIONS = (None, "gelu", "gelu_tanh")
 
 
+_SM_COUNT: dict[int, int] = {}
+
+
+def _one_wave(K: int, N: int, device: torch.device) -> bool:
+    """Whether gw_dynamic_linear's grid (ceil(N / 128) feature blocks x ceil(K / 512)
+    ranks, one CTA per SM) runs in a single wave on this device."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    sms = _SM_COUNT.get(idx)
+    if sms is None:
+        sms = _SM_COUNT[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return -(-N // 128) * -(-K // 512) <= sms
+
+
 class _CountReadback:
     """The last dynamic forward's alive count on its way to the host.
 
@@ -274,9 +287,13 @@ class GhostLinear(nn.Module):
             bias = bias.to(x_2d.dtype)
         prev = self._readback.ready()           # the previous forward's count, if it has landed
         dense = prev is not None and 1.0 - prev / self.in_features < self.min_sparsity_to_activate
-        if not dense and x_2d.shape[0] <= 32 and x_2d.dtype in (torch.float16, torch.bfloat16):
+        if (not dense and x_2d.shape[0] <= 32 and x_2d.dtype in (torch.float16, torch.bfloat16)
+                and _one_wave(self.in_features, self.out_features, x_2d.device)):
             # At most 32 rows: mask, compaction and the sparse product in one
-            # launch (gw_dynamic_linear), reading x and W once.
+            # launch (gw_dynamic_linear), reading x and W once. Taken where its
+            # clusters run in one wave (every projection of GPT-2 and
+            # DistilBERT); larger layers run the separate kernels, which were
+            # faster there.
             w = self.weight.detach()
             if w.dtype is x_2d.dtype and w.stride(1) == 1 and x_2d.stride(1) == 1:
                 y = torch.empty((x_2d.shape[0], self.out_features), dtype=x_2d.dtype, device=x_2d.device)
