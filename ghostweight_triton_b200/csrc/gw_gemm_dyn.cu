@@ -96,9 +96,12 @@ struct DyParams {
   unsigned int* err;
 };
 
+// Not volatile: used only after the cluster barrier that publishes the data
+// (an asm volatile with a memory clobber, which nothing moves across), so the
+// compiler may issue many of these loads before using any.
 __device__ __forceinline__ float ld_dsmem_f32(uint32_t cluster_addr) {
   float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
+  asm("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr));
   return v;
 }
 __device__ __forceinline__ int32_t ld_dsmem_s32(uint32_t cluster_addr) {
@@ -277,13 +280,14 @@ __global__ void __launch_bounds__(kDyThreads, 1) gemm_dyn_kernel(const DyParams 
   for (int r = warp; r < rows; r += 8) {
     const uint16_t* xr = p.x + static_cast<int64_t>(r) * p.ldx + col0;
     uint16_t xv2[kMaxI];
+    // Unconditional loads (an invalid position reads column 0 of the range and
+    // is not stored), so that all of a row's loads are in flight at once.
 #pragma unroll
-    for (int i = 0; i < kMaxI; ++i) xv2[i] = i < ni && 32 * i + lane < kp ? __ldg(xr + cp[i]) : uint16_t(0);
+    for (int i = 0; i < kMaxI; ++i) xv2[i] = __ldg(xr + cp[i]);
 #pragma unroll
     for (int i = 0; i < kMaxI; ++i)
       if (i < ni && 32 * i + lane < kp)
-        asm volatile("st.shared.u16 [%0], %1;" :: "r"(x_s + tile_off(r, 32 * i + lane, C::kXAtomBytes)),
-                     "h"(xv2[i]) : "memory");
+        *reinterpret_cast<uint16_t*>(smem + C::kWBytes + tile_off(r, 32 * i + lane, C::kXAtomBytes)) = xv2[i];
   }
   {
     // W': warp w handles rows 16 w .. 16 w + 15 of the feature block in four
@@ -318,19 +322,18 @@ __global__ void __launch_bounds__(kDyThreads, 1) gemm_dyn_kernel(const DyParams 
         reinterpret_cast<uint4*>(st_w + j * kDyKS * 2)[lane + 32] = cur[j][1];
       }
       __syncwarp();
+      // Plain loads and stores: the compiler issues a row's loads together.
+      const uint16_t* st16 = reinterpret_cast<const uint16_t*>(st_w);
 #pragma unroll
       for (int j = 0; j < C::kStageRows; ++j) {
         const int r = warp * 16 + b * C::kStageRows + j;
+        uint16_t vals[kMaxI];
 #pragma unroll
-        for (int i = 0; i < kMaxI; ++i) {
-          if (i < ni && 32 * i + lane < kp) {
-            uint16_t v;
-            asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v)
-                         : "r"(st_s + static_cast<uint32_t>(j * kDyKS * 2 + cp[i] * 2)) : "memory");
-            asm volatile("st.shared.u16 [%0], %1;" :: "r"(w_s + tile_off(r, 32 * i + lane, C::kWAtomBytes)),
-                         "h"(v) : "memory");
-          }
-        }
+        for (int i = 0; i < kMaxI; ++i) vals[i] = st16[j * kDyKS + cp[i]];
+#pragma unroll
+        for (int i = 0; i < kMaxI; ++i)
+          if (i < ni && 32 * i + lane < kp)
+            *reinterpret_cast<uint16_t*>(smem + tile_off(r, 32 * i + lane, C::kWAtomBytes)) = vals[i];
       }
       __syncwarp();                                  // the staging rows are free again
     }
@@ -387,17 +390,37 @@ __global__ void __launch_bounds__(kDyThreads, 1) gemm_dyn_kernel(const DyParams 
     const int f1 = (rank + 1) * kDyN / S;
     const int nf = f1 - f0;
     const uint32_t part_s = w_s;
-    for (int t = tid; t < rows * nf; t += kDyThreads) {
-      const int m = t / nf;
-      const int f = f0 + (t - m * nf);
-      const int64_t n = n0 + f;
-      if (n >= p.N) continue;
-      const uint32_t local = part_s + static_cast<uint32_t>((f * C::kPartStride + m) * 4);
-      float s = 0.0f;
-      for (int q = 0; q < S; ++q) s += ld_dsmem_f32(mapa_shared(local, static_cast<uint32_t>(q)));
-      if (p.bias) s += Elem<DT>::to_f(__ldg(p.bias + n));
-      s = apply_epilogue16(s, p.epi);
-      p.y[static_cast<int64_t>(m) * p.ldy + n] = Elem<DT>::from_f(s);
+    // Up to four outputs per thread and pass, all of their S partials loaded
+    // before any is added (sums in rank order: the result is reproducible).
+    constexpr int kT = 4;
+    const int tasks = rows * nf;
+    for (int t0 = tid; t0 < tasks; t0 += kT * kDyThreads) {
+      float part_q[kT][16];
+#pragma unroll
+      for (int u = 0; u < kT; ++u) {
+        const int t = t0 + u * kDyThreads;
+        const int m = t < tasks ? t / nf : 0;
+        const int f = t < tasks ? f0 + (t - m * nf) : f0;
+        const uint32_t local = part_s + static_cast<uint32_t>((f * C::kPartStride + m) * 4);
+#pragma unroll
+        for (int q = 0; q < 16; ++q)
+          part_q[u][q] = q < S ? ld_dsmem_f32(mapa_shared(local, static_cast<uint32_t>(q))) : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < kT; ++u) {
+        const int t = t0 + u * kDyThreads;
+        if (t >= tasks) continue;
+        const int m = t / nf;
+        const int64_t n = n0 + f0 + (t - m * nf);
+        if (n >= p.N) continue;
+        float s = 0.0f;
+#pragma unroll
+        for (int q = 0; q < 16; ++q)
+          if (q < S) s += part_q[u][q];
+        if (p.bias) s += Elem<DT>::to_f(__ldg(p.bias + n));
+        s = apply_epilogue16(s, p.epi);
+        p.y[static_cast<int64_t>(m) * p.ldy + n] = Elem<DT>::from_f(s);
+      }
     }
     if (p.count && n_blk == 0 && rank == 0 && tid == 0) {
       int32_t total = 0;
