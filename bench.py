@@ -579,6 +579,59 @@ def traffic_from_profiles() -> float | None:
     return None
 
 
+def dynamic_decode_record(steps: int) -> dict:
+    """The per-forward activation mask at decode size (16 rows, 50% of x's columns zero):
+    the single launch (gw_dynamic_linear: mask, compaction and GEMM) against the four
+    launches of the device-count path (mask, weight packing, gather, GEMM) and dense
+    cuBLAS, on GPT-2's MLP shapes and 4096 x 4096; 16 layers per CUDA graph, replayed."""
+    import torch.nn.functional as F
+
+    from ghostweight_triton_b200 import _native
+    from ghostweight_triton_b200.kernels.gather import pack_weight_dev
+    from ghostweight_triton_b200.kernels.mask import dead_neuron_mask_compact
+    from ghostweight_triton_b200.kernels.matmul import ghost_linear_dev
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    n_layers = 16
+    out = []
+    for M, N, K in ((16, 3072, 768), (16, 768, 3072), (16, 4096, 4096), (1, 4096, 4096)):
+        g = torch.Generator(device=dev).manual_seed(M + N + K)
+        ws = [(torch.randn(N, K, device=dev, generator=g) / K ** 0.5).half() for _ in range(n_layers)]
+        xs = []
+        for _ in range(n_layers):
+            x = torch.randn(M, K, device=dev, generator=g).half()
+            x[:, torch.randperm(K, device=dev, generator=g)[:K // 2]] = 0
+            xs.append(x)
+        ys = [torch.empty(M, N, device=dev, dtype=torch.float16) for _ in range(n_layers)]
+        cnt = torch.empty(1, dtype=torch.int32, device=dev)
+
+        def one(i):
+            assert _native.dynamic_linear(xs[i], ws[i], 0.0, ys[i], count=cnt) == _native.GW_OK
+
+        def four(i):
+            _, buf, c = dead_neuron_mask_compact(xs[i], 0.0, want_mask=False)
+            ghost_linear_dev(xs[i], pack_weight_dev(ws[i], buf, c), buf, c, out=ys[i])
+
+        def dense(i):
+            torch.mm(xs[i], ws[i].t(), out=ys[i])
+
+        row = {"M": M, "N": N, "K": K}
+        for name, f in (("single_launch_us", one), ("four_launches_us", four), ("cublas_dense_us", dense)):
+            row[name] = round(graph_time(lambda: [f(i) for i in range(n_layers)], max(5, min(steps, 20)), 1)
+                              / n_layers * 1e6, 2)
+        one(0)
+        ref = F.linear(xs[0].float(), ws[0].float())
+        row["max_abs_err_vs_fp32"] = float((ys[0].float() - ref).abs().max())
+        row["alive_count_ok"] = int(cnt.item()) == K - K // 2
+        out.append(row)
+        del ws, xs, ys
+    torch.cuda.empty_cache()
+    return {"what": "dynamic activation mask at decode size: one launch vs mask + pack + gather + GEMM "
+                    "vs dense cuBLAS; graph replay of 16 layer calls", "rows": out,
+            "note": "with a random dynamic mask every 16-byte vector of W holds alive columns, so any "
+                    "sparse path reads all of W; dense cuBLAS reads it once at full speed"}
+
+
 def run_ours(args, world, rank, local):
     from ghostweight_triton_b200 import GhostLinear
 
@@ -728,6 +781,7 @@ def run_ours(args, world, rank, local):
         if not args.no_models:
             extra["models"] = {w: model_record(w, args.steps, args.warmup, world, rank, full=False)
                                for w in ("gpt2", "distilbert")}
+            extra["dynamic_decode"] = dynamic_decode_record(args.steps)
         if not args.no_reference_triton:
             extra["reference_triton"] = reference_triton_record()
         if not args.no_cpu_baseline:
