@@ -657,7 +657,7 @@ def run_ours(args, world, rank, local):
 
     def step(i):
         L = layers[i % N_SETS]
-        _native.gather_gemm(L["x"], L["wp"], L["idx"], L["y"], strategy="pregather", workspace=ws)
+        _native.gather_gemm(L["x"], L["wp"], L["idx"], L["y"], strategy=args.strategy, workspace=ws)
 
     def step_overlap(i):
         L = layers[i % N_SETS]
@@ -818,7 +818,7 @@ def run_ours(args, world, rank, local):
             "cpu_baseline": cpu,
             "e2e": e2e,
             "clocks": clocks,
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": (2 if args.strategy == "pregather" else 1) * args.steps,
             "step_kernels": {"step_us": round(per_step * 1e6, 2),
                              "gemm_on_gathered_operand_us": round(t_gemm * 1e6, 2),
                              "gemm_on_gathered_operand_tflops": round(useful / t_gemm / 1e12, 2),
@@ -826,7 +826,9 @@ def run_ours(args, world, rank, local):
                              "gather_alone_GBps": round(gather_bytes / t_gather / 1e9, 1),
                              "gather_alone_frac_hbm": round(gather_bytes / t_gather / 1e9 / float(peaks["hbm_gbs"]), 3),
                              "single_launch_overlap_us": round(t_ovl * 1e6, 2)},
-            "strategy": "pregather (gather launch + PDL-chained TMA tcgen05 GEMM launch)",
+            "strategy": ("pregather (gather launch + PDL-chained TMA tcgen05 GEMM launch)"
+                         if args.strategy == "pregather" else
+                         "overlap (one launch: the pair GEMM's epilogue warps gather x' while its MMAs run)"),
         }
         line.update(extra)
         print(json.dumps(line), flush=True)
@@ -1514,7 +1516,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["gemm", "mlp-sharded", "ghostlinear-fp32", "gpt2", "distilbert",
-                                           "decode", "small-batch"],
+                                           "decode", "small-batch", "dynamic-decode"],
                     default="gemm")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--rows", type=int, nargs="+", default=None,
@@ -1528,6 +1530,8 @@ def main():
     ap.add_argument("--no-reference-triton", action="store_true",
                     help="skip timing the reference's Triton kernels")
     ap.add_argument("--reference-triton-child", metavar="DIR", default=None, help=argparse.SUPPRESS)
+    ap.add_argument("--strategy", choices=["pregather", "overlap"], default="pregather",
+                    help="gemm workload: the gather-GEMM strategy of the timed step")
     args = ap.parse_args()
     if args.reference_triton_child:
         reference_triton_child(args.reference_triton_child)
@@ -1547,6 +1551,17 @@ def main():
             run_decode(args, world, rank, local)
         elif args.workload == "small-batch":
             run_small_batch(args, world, rank, local)
+        elif args.workload == "dynamic-decode":
+            rec = dynamic_decode_record(args.steps)
+            if rank == 0:
+                r = rec["rows"][0]
+                print(json.dumps({
+                    "metric": "dynamic-mask layer call time (M=16, 768 -> 3072 fp16, 50% of x's columns zero)",
+                    "value": r["single_launch_us"], "unit": "us", "n_gpus": world, "steps": args.steps,
+                    "warmup": args.warmup, "ms_per_step": round(r["single_launch_us"] / 1e3, 5),
+                    "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+                    "data": "synthetic, seeded", "config": {"workload": "dynamic decode, 16 rows per call"},
+                    "dynamic_decode": rec, "gpu_launches": 16}), flush=True)
         else:
             run_model(args, world, rank, local, args.workload)
     finally:
