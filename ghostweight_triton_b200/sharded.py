@@ -171,6 +171,9 @@ class ColumnParallelGhostLinear(nn.Module):
         self._peer_out: PeerOutputs | None = None
         self._peer_step = 0
         self._flag: torch.Tensor | None = None
+        # Weak references to the tensor each shared buffer last returned (see
+        # _forward_peers): a buffer is not overwritten while it is referenced.
+        self._peer_returned: list = [None, None]
 
     @property
     def k_alive(self) -> int:
@@ -239,20 +242,25 @@ class ColumnParallelGhostLinear(nn.Module):
         # ranks take the same path and issue the same collectives.
         if (self.gather_output == "peers" and self.world > 1 and self.out_features % 8 == 0
                 and self.n_local % 8 == 0):
-            return self._forward_peers(x).reshape(*lead, self.out_features)
+            return self._forward_peers(x, lead)
         y = self.local_forward(x)
         if not self.gather_output:
             return y.reshape(*lead, self.n_local)
         full = gather_columns_from_ranks(y, self.out_features, self.group)
         return full.reshape(*lead, self.out_features)
 
-    def _forward_peers(self, x: torch.Tensor) -> torch.Tensor:
-        """Full [M, N] output with the all-gather fused into the GEMM (peer stores).
+    def _forward_peers(self, x: torch.Tensor, lead: tuple = ()) -> torch.Tensor:
+        """Full [..., N] output with the all-gather fused into the GEMM (peer stores).
 
-        The result is a view of one of two shared buffers used in turn: it stays
-        valid until the call after the next one. Every rank must call with the
+        The result is a view of one of two shared buffers used in turn, which
+        every rank's GEMM of the call after the next one writes again. That call
+        raises RuntimeError while the tensor returned from that buffer is still
+        referenced (keep a ``.clone()`` of outputs you need longer; views derived
+        from the returned tensor are not tracked). Every rank must call with the
         same M.
         """
+        import weakref
+
         from ghostweight_triton_b200 import _native
 
         assert self.alive is not None, "call freeze_weight_mask() first"
@@ -265,6 +273,13 @@ class ColumnParallelGhostLinear(nn.Module):
             po = self._peer_out = PeerOutputs(M, self.out_features, x2.dtype, self.group)
             self._flag = torch.zeros(1, dtype=torch.int32, device=x2.device)
         i = self._peer_step % 2
+        held = self._peer_returned[i]
+        if held is not None and held() is not None:
+            # Checked on every rank before any collective of this call, so a
+            # refusal leaves the ranks in step (each rank holds its own output).
+            raise RuntimeError(
+                "the output this layer returned two calls ago is still referenced and its "
+                "shared buffer would be overwritten now; clone() outputs kept across calls")
         self._peer_step += 1
         full = po.local(i)[:M]
         n_real = self.row_stop - self.row_start
@@ -278,7 +293,9 @@ class ColumnParallelGhostLinear(nn.Module):
         # Orders every rank's readers of `full` after every rank's GEMM (and its
         # peer stores): each rank joins only after its own GEMM on this stream.
         dist.all_reduce(self._flag, group=self.group)
-        return full
+        out = full.reshape(*lead, self.out_features) if lead else full
+        self._peer_returned[i] = weakref.ref(out)
+        return out
 
     def close(self) -> None:
         """Release the shared output buffers (collective when gather_output="peers")."""

@@ -72,6 +72,18 @@ def _rank_main(rank: int, world: int, port: int, q) -> None:
                 yp = layer(xs).clone()
                 refp = ref if step != 1 else F.linear(xs.float(), w.float(), b.float())
                 errs.append(excess(yp, refp))
+            # A result still referenced is not overwritten: the call that would
+            # reuse its buffer raises on every rank before any collective.
+            kept = layer(x)
+            layer(x)
+            try:
+                layer(x)
+                raise AssertionError("reusing a referenced peer buffer did not raise")
+            except RuntimeError as e:
+                assert "still referenced" in str(e)
+            kept_err = excess(kept, ref)
+            del kept
+            errs += [kept_err, excess(layer(x).clone(), ref)]
             layer.close()
             results[str(dtype)] = (max(err, *errs), layer.k_alive, tuple(y.shape))
         # Whole 128-column blocks dead: the alive list is 64-column runs, so both
