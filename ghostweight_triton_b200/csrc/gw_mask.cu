@@ -13,7 +13,8 @@
 //   * a warp covers 32 consecutive 16-byte vectors of one row (512 contiguous
 //     bytes, fully coalesced); 8 warps of a CTA walk different rows; each CTA
 //     owns a 32-vector column strip and a contiguous chunk of rows;
-//   * 4 rows are loaded per iteration per thread (streaming, no L1 allocation);
+//   * 4 rows are loaded per batch per thread (streaming, no L1 allocation),
+//     the last batch of a chunk included (clamped rows, masked results);
 //   * a warp whose columns are all alive stops reading (warp-uniform exit);
 //   * per-CTA alive bits are OR-ed into a 32-bit word array in the workspace;
 //   * the last CTA to finish (ticket counter) performs the compaction: a
@@ -65,7 +66,7 @@ __device__ __forceinline__ uint32_t vec_bits(const uint4 v, float thr) {
 // columns); requires 16-byte aligned base, ld and cols multiples of the vector.
 // VEC = false: each thread owns one column (scalar loads).
 template <int DT, bool VEC>
-__global__ void __launch_bounds__(kMaskThreads)
+__global__ void __launch_bounds__(kMaskThreads, 8)
 mask_compact_kernel(const void* __restrict__ x, int64_t rows, int64_t cols, int64_t ld,
                     float thr, int64_t rows_per_cta, uint32_t* __restrict__ ws,
                     int32_t* __restrict__ mask, int64_t* __restrict__ idx,
@@ -94,32 +95,28 @@ mask_compact_kernel(const void* __restrict__ x, int64_t rows, int64_t cols, int6
   const bool have = (v < nvec);
   if (!all_alive) {
     const raw* col = static_cast<const raw*>(x) + (have ? v * VPT : 0);
-    int64_t r = r0 + warp;
-    // Main loop: 4 independent rows in flight per thread.
-    for (; r + (kMaskUnroll - 1) * kMaskWarps < r1; r += kMaskUnroll * kMaskWarps) {
+    // 4 rows in flight per thread in every batch, the last one included: rows
+    // past the chunk load the chunk's last row again (a valid address) and are
+    // masked out, so no row is read on its own. A warp whose columns are all
+    // alive leaves the loop and reads nothing more.
+    for (int64_t r = r0 + warp; r < r1; r += kMaskUnroll * kMaskWarps) {
       if (__all_sync(0xFFFFFFFFu, !have || bits == kFull)) break;
       if (have) {
         if constexpr (VEC) {
           uint4 q[kMaskUnroll];
 #pragma unroll
-          for (int u = 0; u < kMaskUnroll; ++u) q[u] = ld_stream_v4(col + (r + u * kMaskWarps) * ld);
+          for (int u = 0; u < kMaskUnroll; ++u)
+            q[u] = ld_stream_v4(col + min(r + u * kMaskWarps, r1 - 1) * ld);
 #pragma unroll
-          for (int u = 0; u < kMaskUnroll; ++u) bits |= vec_bits<DT>(q[u], thr);
+          for (int u = 0; u < kMaskUnroll; ++u)
+            bits |= (r + u * kMaskWarps < r1) ? vec_bits<DT>(q[u], thr) : 0u;
         } else {
           raw q[kMaskUnroll];
 #pragma unroll
-          for (int u = 0; u < kMaskUnroll; ++u) q[u] = __ldg(col + (r + u * kMaskWarps) * ld);
+          for (int u = 0; u < kMaskUnroll; ++u) q[u] = __ldg(col + min(r + u * kMaskWarps, r1 - 1) * ld);
 #pragma unroll
-          for (int u = 0; u < kMaskUnroll; ++u) bits |= (fabsf(Elem<DT>::to_f(q[u])) > thr) ? 1u : 0u;
-        }
-      }
-    }
-    for (; r < r1; r += kMaskWarps) {
-      if (have) {
-        if constexpr (VEC) {
-          bits |= vec_bits<DT>(ld_stream_v4(col + r * ld), thr);
-        } else {
-          bits |= (fabsf(Elem<DT>::to_f(__ldg(col + r * ld))) > thr) ? 1u : 0u;
+          for (int u = 0; u < kMaskUnroll; ++u)
+            bits |= (r + u * kMaskWarps < r1 && fabsf(Elem<DT>::to_f(q[u])) > thr) ? 1u : 0u;
         }
       }
     }

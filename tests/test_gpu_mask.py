@@ -74,6 +74,22 @@ def test_oracle_sweep(dt, M, K, sp, pattern):
     check_mask_and_compaction(x, a, dt, 1e-6)
 
 
+@pytest.mark.parametrize("dt", ["f16", "bf16", "f32"])
+@pytest.mark.parametrize("M", [4096, 1000, 77, 9])
+def test_single_row_columns_beside_dense_ones(dt, M):
+    # Dense columns let their warps stop reading early; columns alive in one
+    # row only (the last row, a row in a chunk's ragged last batch, the first
+    # row) must still be found whatever batch that row falls in.
+    K = 1024
+    a = np.zeros((M, K), dtype=rand_matrix((1, 1), 0, dt).dtype)
+    dense = rand_matrix((M, K), M + 7, dt)
+    a[:, 0::4] = dense[:, 0::4]
+    a[M - 1, 1::4] = dense[M - 1, 1::4]
+    a[(M * 5) // 7, 2::8] = dense[(M * 5) // 7, 2::8]
+    a[0, 3::8] = dense[0, 3::8]
+    check_mask_and_compaction(to_dev(a, dt), a, dt, 1e-6)
+
+
 @pytest.mark.parametrize("thr", [0.0, 0.5, 1.7, -1.0, float("inf")])
 def test_thresholds_vs_oracle(thr):
     a = rand_matrix((64, 512), 3, "f16")
