@@ -75,6 +75,14 @@ mask_compact_kernel(const void* __restrict__ x, int64_t rows, int64_t cols, int6
   constexpr int VPT = VEC ? static_cast<int>(16 / sizeof(raw)) : 1;   // columns per thread
   constexpr uint32_t kFull = (VPT == 32) ? 0xFFFFFFFFu : ((1u << VPT) - 1u);
 
+  // Launched as a programmatic dependent: x may come from the previous kernel
+  // of the stream, which may let this grid start early, so wait for it before
+  // any access. Then let the next kernel begin its launch; whatever it reads
+  // of this grid's results (mask, indices, count) it reads after its own
+  // griddepcontrol.wait, which waits for this whole grid.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
   uint32_t* ticket = ws;
   uint32_t* flags = ws + kFlagsOffset / sizeof(uint32_t);
 
@@ -248,24 +256,19 @@ cudaError_t launch_mask_compact(const void* x, int dtype, int64_t rows, int64_t 
   dim3 grid(static_cast<unsigned>(col_tiles), static_cast<unsigned>(row_tiles));
   uint32_t* ws = static_cast<uint32_t*>(workspace);
 #define GW_MASK_LAUNCH(DT, V)                                                               \
-  mask_compact_kernel<DT, V><<<grid, kMaskThreads, 0, stream>>>(x, rows, cols, ld, thr,     \
-                                                                 rows_per_cta, ws, mask, idx, \
-                                                                 count)
+  launch_pdl(mask_compact_kernel<DT, V>, grid, dim3(kMaskThreads), stream, x, rows, cols, ld,  \
+             thr, rows_per_cta, ws, mask, idx, count)
   switch (dtype) {
     case GW_DTYPE_F16:
-      if (vec) GW_MASK_LAUNCH(GW_DTYPE_F16, true); else GW_MASK_LAUNCH(GW_DTYPE_F16, false);
-      break;
+      return vec ? GW_MASK_LAUNCH(GW_DTYPE_F16, true) : GW_MASK_LAUNCH(GW_DTYPE_F16, false);
     case GW_DTYPE_BF16:
-      if (vec) GW_MASK_LAUNCH(GW_DTYPE_BF16, true); else GW_MASK_LAUNCH(GW_DTYPE_BF16, false);
-      break;
+      return vec ? GW_MASK_LAUNCH(GW_DTYPE_BF16, true) : GW_MASK_LAUNCH(GW_DTYPE_BF16, false);
     case GW_DTYPE_F32:
-      if (vec) GW_MASK_LAUNCH(GW_DTYPE_F32, true); else GW_MASK_LAUNCH(GW_DTYPE_F32, false);
-      break;
+      return vec ? GW_MASK_LAUNCH(GW_DTYPE_F32, true) : GW_MASK_LAUNCH(GW_DTYPE_F32, false);
     default:
       return cudaErrorInvalidValue;
   }
 #undef GW_MASK_LAUNCH
-  return cudaGetLastError();
 }
 
 }  // namespace gw
