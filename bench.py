@@ -138,6 +138,51 @@ def physical_gpu_index(local: int) -> int:
     return local
 
 
+def gpu_local_cpus(device_index: int) -> set[int] | None:
+    """CPUs that NVML reports as nearest the GPU (its NUMA node), within this
+    process's allowed set; None when NVML or the affinity call is unavailable."""
+    try:
+        import pynvml
+
+        uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+        pynvml.nvmlInit()
+        try:
+            h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            words = pynvml.nvmlDeviceGetCpuAffinity(h, ((os.cpu_count() or 64) + 63) // 64)
+        finally:
+            pynvml.nvmlShutdown()
+        cpus = {64 * i + b for i, w in enumerate(words) for b in range(64) if (int(w) >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        return cpus or None
+    except Exception:
+        return None
+
+
+class NearGpu:
+    """Run a block on the CPUs nearest this rank's GPU, so that host buffers
+    first touched inside it live on the GPU's NUMA node; the previous affinity
+    comes back on exit."""
+
+    def __init__(self, device_index: int):
+        self.cpus = gpu_local_cpus(device_index)
+        self.prev = None
+
+    def __enter__(self):
+        if self.cpus:
+            self.prev = os.sched_getaffinity(0)
+            os.sched_setaffinity(0, self.cpus)
+        return self
+
+    def __exit__(self, *exc):
+        if self.prev:
+            os.sched_setaffinity(0, self.prev)
+
+    def describe(self) -> str:
+        if not self.cpus:
+            return "not bound (no NVML CPU affinity)"
+        return f"{len(self.cpus)} CPUs NVML reports nearest the GPU (of {len(self.prev or self.cpus)} allowed)"
+
+
 def dist_setup(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -715,6 +760,7 @@ def run_ours(args, world, rank, local):
     # e2e through the public API: GhostLinear (frozen weight mask), pinned host x in, y out.
     e2e = None
     if not args.no_e2e:
+        near = NearGpu(device.index).__enter__()
         gl = GhostLinear(K, N, bias=False, device=device, dtype=torch.float16)
         with torch.no_grad():
             gl.weight.copy_(layers[0]["w"])
@@ -780,7 +826,10 @@ def run_ours(args, world, rank, local):
                "pcie_h2d_GBps": round(M * K * 2 / t_h2d / 1e9, 1),
                "pcie_d2h_GBps": round(M * N * 2 / t_d2h / 1e9, 1),
                "path": "GhostLinear.forward (frozen weight mask) with pinned-host x -> device -> pinned-host y; "
-                       "upload, compute and download of consecutive steps overlap on three streams"}
+                       "upload, compute and download of consecutive steps overlap on three streams",
+               "host_cpus": near.describe()}
+        near.__exit__()
+        del hx, hy
 
     extra = {}
     cpu = None

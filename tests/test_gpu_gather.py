@@ -90,15 +90,23 @@ def test_out_of_range_index_reads_zero_and_flags():
     assert _native.validate_indices(idx, 16) == 1
 
 
-# ----------------------------------------------------------------- window gather (TMA, >= 256 rows)
+# ----------------------------------------------------------------- many-row gathers
+# Bit-exact against the oracle over row counts, widths and dead patterns,
+# including rows shorter than a 128-byte line, ragged widths and row counts
+# that are not a multiple of the CTA's warps.
 @pytest.mark.parametrize("dt", ["f16", "bf16"])
 @pytest.mark.parametrize("rows,cols,sp,pattern", [
-    (4096, 4096, 0.5, "random"),    # 128-column chunks, one 256-column box per window
-    (4096, 4096, 0.0, "random"),    # dense: 256-column chunks, windows straddle two boxes
-    (1000, 4096, 0.9, "random"),    # sparse: 32-column chunks; ragged last row block
-    (300, 4096, 0.75, "block"),     # 64-column dead blocks
-    (257, 1000, 0.33, "random"),    # columns not a multiple of the box: zero fill past K
-    (512, 8192, 0.6875, "block"),   # the sharded-MLP pattern (128-column blocks)
+    (4096, 4096, 0.5, "random"),
+    (4096, 4096, 0.0, "random"),
+    (1024, 4096, 0.9, "random"),
+    (2048, 4096, 0.75, "block"),    # 64-column dead blocks
+    (1024, 8192, 0.6875, "block"),  # the sharded-MLP pattern (128-column blocks)
+    (1500, 72, 0.5, "random"),
+    (1031, 1000, 0.33, "random"),
+    (1000, 4096, 0.9, "random"),
+    (300, 4096, 0.75, "block"),
+    (257, 1000, 0.33, "random"),
+    (512, 8192, 0.6875, "block"),
 ])
 def test_window_gather_bit_exact(dt, rows, cols, sp, pattern):
     x = rand_matrix((rows, cols), rows + cols, dt)
@@ -114,10 +122,11 @@ def test_window_gather_bit_exact(dt, rows, cols, sp, pattern):
     assert (got[:, len(idx):] == 0).all()          # padding columns written as zeros
 
 
+@pytest.mark.parametrize("rows", [512, 1024])
 @pytest.mark.parametrize("case", ["unsorted", "repeated", "bad_index", "wide_window"])
-def test_window_gather_fallbacks(case):
-    """Chunks whose window does not fit (or holds a bad index) are gathered directly."""
-    rows, cols = 512, 4096
+def test_irregular_index_lists(case, rows):
+    """Unsorted, repeated and out-of-range indices, and a dense run then every 8th column."""
+    cols = 4096
     x = rand_matrix((rows, cols), 11, "f16")
     rng = np.random.default_rng(5)
     if case == "unsorted":
@@ -169,3 +178,34 @@ class TestReferenceSuite:
         A_c, W_c = gather_compact(A, W, torch.arange(32, device=device))
         assert A_c.dtype == dtype and W_c.dtype == dtype
         assert A_c.is_cuda and W_c.is_cuda and A_c.is_contiguous() and W_c.is_contiguous()
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16"])
+def test_gather_unaligned_output_rows(dt):
+    # ld_dst = kp + 5 = 1026 (output rows not 16-byte aligned), kp % 8 != 0.
+    rows, cols = 1100, 2048
+    x = rand_matrix((rows, cols), 21, dt)
+    idx = np.sort(np.random.default_rng(6).permutation(cols)[:1021])
+    base = torch.full((rows, len(idx) + 5), 9, dtype=torch.float16 if dt == "f16" else torch.bfloat16,
+                      device="cuda")
+    out = base[:, :len(idx)]
+    _native.gather_columns(to_dev(x), torch.from_numpy(idx).cuda(), out)
+    assert np.array_equal(to_np(out.contiguous()), O.gather_columns(x, idx))
+    assert (base[:, len(idx):].float() == 9).all()        # nothing written past the width
+
+
+@pytest.mark.parametrize("n", [0, 1, 700, 2048])
+def test_gather_device_count(n):
+    # The count lives on the device: columns [n, round_up(max(n, 1), 64)) are
+    # zero, the ones past that untouched.
+    rows, cols = 1024, 4096
+    x = rand_matrix((rows, cols), 31, "f16")
+    idx = np.sort(np.random.default_rng(7).permutation(cols)[:2048])
+    out = torch.full((rows, 2048), 5, dtype=torch.float16, device="cuda")
+    n_dev = torch.tensor([n], dtype=torch.int32, device="cuda")
+    _native.gather_columns_dev(to_dev(x), torch.from_numpy(idx).cuda(), n_dev, out, pad_to=2048)
+    got = to_np(out)
+    assert np.array_equal(got[:, :n], O.gather_columns(x, idx[:n]))
+    edge = max(-(-max(n, 1) // 64) * 64, 64)
+    assert (got[:, n:edge] == 0).all()
+    assert (got[:, edge:] == 5).all()
