@@ -73,14 +73,17 @@ def _rank_main(rank: int, world: int, port: int, q) -> None:
                 refp = ref if step != 1 else F.linear(xs.float(), w.float(), b.float())
                 errs.append(excess(yp, refp))
             # A result still referenced is not overwritten: the call that would
-            # reuse its buffer raises on every rank before any collective.
+            # reuse its buffer raises on every rank before any collective. (The
+            # N = 1000 case splits into 500-wide shards, which take the NCCL
+            # path: its outputs are fresh tensors and nothing is refused.)
+            peer_path = layer.out_features % 8 == 0 and layer.n_local % 8 == 0
             kept = layer(x)
             layer(x)
             try:
                 layer(x)
-                raise AssertionError("reusing a referenced peer buffer did not raise")
+                assert not peer_path, "reusing a referenced peer buffer did not raise"
             except RuntimeError as e:
-                assert "still referenced" in str(e)
+                assert peer_path and "still referenced" in str(e)
             kept_err = excess(kept, ref)
             del kept
             errs += [kept_err, excess(layer(x).clone(), ref)]
