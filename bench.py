@@ -783,6 +783,12 @@ def run_ours(args, world, rank, local):
 
         def e2e_step(i):
             b = i % 2
+            # The host waits for slot b's previous download before queueing
+            # this step: at most two steps are in flight, so the outputs that
+            # wait for their downloads stay at two and the caching allocator
+            # reaches its steady pool during warm-up (left unbounded, the host
+            # runs many steps ahead and every step may need a new cudaMalloc).
+            ev_out[b].synchronize()
             s_in.wait_event(ev_comp[b])                  # slot b's x no longer read
             with torch.cuda.stream(s_in):
                 xd[b].copy_(hx[i % N_SETS], non_blocking=True)
@@ -812,7 +818,7 @@ def run_ours(args, world, rank, local):
             barrier(world)
             return max_over_ranks(st.elapsed_time(en) / 1e3, world)
 
-        for i in range(max(3, args.warmup)):
+        for i in range(max(8, args.warmup)):
             e2e_step(i)
         torch.cuda.synchronize()
         e_steps = max(1, min(args.steps, 200))
@@ -826,7 +832,8 @@ def run_ours(args, world, rank, local):
                "pcie_h2d_GBps": round(M * K * 2 / t_h2d / 1e9, 1),
                "pcie_d2h_GBps": round(M * N * 2 / t_d2h / 1e9, 1),
                "path": "GhostLinear.forward (frozen weight mask) with pinned-host x -> device -> pinned-host y; "
-                       "upload, compute and download of consecutive steps overlap on three streams",
+                       "upload, compute and download of consecutive steps overlap on three streams; "
+                       "the host waits for a slot's previous download before reusing it (two steps in flight)",
                "host_cpus": near.describe()}
         near.__exit__()
         del hx, hy
