@@ -766,26 +766,27 @@ def run_ours(args, world, rank, local):
             gl.weight.copy_(layers[0]["w"])
         gl.freeze_weight_mask()
         hx = [L["x"].cpu().pin_memory() for L in layers]
-        hy = [torch.empty(M, N, dtype=torch.float16).pin_memory() for _ in range(2)]
+        n_slots = 3
+        hy = [torch.empty(M, N, dtype=torch.float16).pin_memory() for _ in range(n_slots)]
         layers_y0 = layers[0]["y"]
-        # Three streams, two slots: the upload of step i+1 and the download of
+        # Three streams, three slots: the upload of step i+1 and the download of
         # step i-1 run while step i computes (PCIe carries both directions at
         # once). Events order each slot's reuse.
         comp = torch.cuda.current_stream()
         s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
-        xd = [torch.empty(M, K, dtype=torch.float16, device=device) for _ in range(2)]
-        ev_in = [torch.cuda.Event() for _ in range(2)]
-        ev_comp = [torch.cuda.Event() for _ in range(2)]
-        ev_out = [torch.cuda.Event() for _ in range(2)]
-        for b in range(2):
+        xd = [torch.empty(M, K, dtype=torch.float16, device=device) for _ in range(n_slots)]
+        ev_in = [torch.cuda.Event() for _ in range(n_slots)]
+        ev_comp = [torch.cuda.Event() for _ in range(n_slots)]
+        ev_out = [torch.cuda.Event() for _ in range(n_slots)]
+        for b in range(n_slots):
             ev_comp[b].record(comp)
             ev_out[b].record(comp)
 
         def e2e_step(i):
-            b = i % 2
+            b = i % n_slots
             # The host waits for slot b's previous download before queueing
-            # this step: at most two steps are in flight, so the outputs that
-            # wait for their downloads stay at two and the caching allocator
+            # this step: at most three steps are in flight, so the outputs that
+            # wait for their downloads stay at three and the caching allocator
             # reaches its steady pool during warm-up (left unbounded, the host
             # runs many steps ahead and every step may need a new cudaMalloc).
             ev_out[b].synchronize()
@@ -833,7 +834,7 @@ def run_ours(args, world, rank, local):
                "pcie_d2h_GBps": round(M * N * 2 / t_d2h / 1e9, 1),
                "path": "GhostLinear.forward (frozen weight mask) with pinned-host x -> device -> pinned-host y; "
                        "upload, compute and download of consecutive steps overlap on three streams; "
-                       "the host waits for a slot's previous download before reusing it (two steps in flight)",
+                       "the host waits for a slot's previous download before reusing it (three slots, at most three steps in flight)",
                "host_cpus": near.describe()}
         near.__exit__()
         del hx, hy
