@@ -105,6 +105,11 @@ struct Tc2Params {
   int m_tiles;
   int n_tiles;
   int num_tiles;
+  // Jobs: tiles [0, num_full) whole, then each tile of [num_full, num_tiles)
+  // as two jobs of 128 columns (the last, partial round of tiles split in
+  // half so that it spreads over the pairs); num_jobs counts both kinds.
+  int num_full;
+  int num_jobs;
   unsigned int* err;
   // Peer outputs: every finished tile is also stored, at the same place, into
   // these buffers of other GPUs (same ldy; device addresses valid here).
@@ -143,6 +148,20 @@ __device__ __forceinline__ void tile_coords(int tile, const Tc2Params& p, int& m
   } else {
     n_blk = tile / p.m_tiles;
     m_blk = tile - n_blk * p.m_tiles;
+  }
+}
+
+// Job -> (row block, column block, sub): sub = -1 for a whole tile, else
+// which 128-column half of the tile the job covers.
+__device__ __forceinline__ void job_coords(int job, const Tc2Params& p, int& m_blk, int& n_blk,
+                                           int& sub) {
+  if (job < p.num_full) {
+    tile_coords(job, p, m_blk, n_blk);
+    sub = -1;
+  } else {
+    const int j = job - p.num_full;
+    tile_coords(p.num_full + (j >> 1), p, m_blk, n_blk);
+    sub = j & 1;
   }
 }
 
@@ -341,6 +360,7 @@ __device__ __forceinline__ void gather_units(const Tc2Params& p, int e, int lane
 template <int BN, int DT, int EPI, bool GATHER>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
 gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
+                const __grid_constant__ CUtensorMap tmap_bh,
                 const __grid_constant__ CUtensorMap tmap_a,
                 const __grid_constant__ CUtensorMap tmap_y, const Tc2Params p) {
   using C = Tc2Cfg<BN>;
@@ -386,6 +406,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
+    if (p.num_jobs > p.num_full) tma_prefetch_desc(&tmap_bh);
     if (p.y_tma) tma_prefetch_desc(&tmap_y);
   }
   if (warp == 1) {
@@ -416,11 +437,16 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
         nxt0 = run_start_load(p.a_cols, 0);
         if (num_kb > 1) nxt1 = run_start_load(p.a_cols, 1);
       }
-      for (int tile = pair; ok && tile < p.num_tiles; tile += num_pairs) {
-        int m_blk, n_blk;
-        tile_coords(tile, p, m_blk, n_blk);
+      for (int job = pair; ok && job < p.num_jobs; job += num_pairs) {
+        int m_blk, n_blk, sub;
+        job_coords(job, p, m_blk, n_blk, sub);
         const int a_row = m_blk * kPairM + static_cast<int>(rank) * kHalfM;
-        const int b_row = n_blk * BN + static_cast<int>(rank) * kHalfN;
+        // A half job's W' rows: 64 per CTA through the 64-row box of tmap_bh,
+        // in the first half of each B atom slot.
+        const int b_row = sub < 0 ? n_blk * BN + static_cast<int>(rank) * kHalfN
+                                  : n_blk * BN + sub * 128 + static_cast<int>(rank) * 64;
+        const void* tb = sub < 0 ? static_cast<const void*>(&tmap_b) : static_cast<const void*>(&tmap_bh);
+        const uint32_t b_atom_bytes = sub < 0 ? C::kBAtomBytes : 64 * kBK2 * 2;
         for (int ks = 0; ks < num_ks; ++ks, ++it) {
           const int s = it % kStages2;
           const uint32_t ph = (it / kStages2) & 1u;
@@ -437,12 +463,12 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
           // The last stage of an odd number of atoms carries one atom.
           const int atoms = min(kAtoms2, num_kb - ks * kAtoms2);
           if (rank == 0)
-            mbar_arrive_expect_tx(full(s), 2u * atoms * (kAAtomBytes2 + C::kBAtomBytes));
+            mbar_arrive_expect_tx(full(s), 2u * atoms * (kAAtomBytes2 + b_atom_bytes));
           if constexpr (GATHER) {
             // W' first (it does not depend on the gather), then each unit of x'
             // once its flag says it is complete; count the flag down.
             for (int a = 0; a < atoms; ++a)
-              tma_load_2d_pair(b_s + a * C::kBAtomBytes, &tmap_b, (ks * kAtoms2 + a) * kBK2, b_row,
+              tma_load_2d_pair(b_s + a * C::kBAtomBytes, tb, (ks * kAtoms2 + a) * kBK2, b_row,
                                leader_full);
             // The flags of this half-panel are read 16 at a time (ready_bits
             // covers k atoms [snap_kb, snap_kb + 16)); only an atom that was not
@@ -474,7 +500,7 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
               const int kx = (ks * kAtoms2 + a) * kBK2;
               const int ax = p.a_cols ? run_start_check(a == 0 ? cur0 : cur1, p.a_width, p.err) : kx;
               tma_load_2d_pair(a_s + a * kAAtomBytes2, &tmap_a, ax, a_row, leader_full);
-              tma_load_2d_pair(b_s + a * C::kBAtomBytes, &tmap_b, kx, b_row, leader_full);
+              tma_load_2d_pair(b_s + a * C::kBAtomBytes, tb, kx, b_row, leader_full);
             }
           }
         }
@@ -488,7 +514,8 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader only)
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc = idesc_f16(DT == GW_DTYPE_BF16 ? 1u : 0u, kPairM, BN);
+      constexpr uint32_t idesc_full = idesc_f16(DT == GW_DTYPE_BF16 ? 1u : 0u, kPairM, BN);
+      constexpr uint32_t idesc_half = idesc_f16(DT == GW_DTYPE_BF16 ? 1u : 0u, kPairM, 128);
       int num_kb = p.num_kb;
       if (p.k_dev) {                   // K' written by an earlier kernel: read it after the wait
         asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -497,9 +524,12 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
       const int num_ks = (num_kb + kAtoms2 - 1) / kAtoms2;
       uint32_t it = 0, lt = 0;
       bool ok = true;
-      for (int tile = pair; ok && tile < p.num_tiles; tile += num_pairs, ++lt) {
+      for (int job = pair; ok && job < p.num_jobs; job += num_pairs, ++lt) {
         const uint32_t b = lt & 1u;
         const uint32_t aph = (lt >> 1) & 1u;
+        // A half job is a 256 x 128 MMA into the first 128 columns of the
+        // accumulator; B holds 64 rows per CTA at the same addresses.
+        const uint32_t idesc = job < p.num_full ? idesc_full : idesc_half;
         if (!mbar_wait_cluster(tempty(b), aph ^ 1u, abort_flag, p.err)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + b * BN;
@@ -553,9 +583,9 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
       gather_units<DT>(p, warp - 2, lane, claim_slot, call);
     }
     uint32_t lt = 0;
-    for (int tile = pair; tile < p.num_tiles; tile += num_pairs, ++lt) {
-      int m_blk, n_blk;
-      tile_coords(tile, p, m_blk, n_blk);
+    for (int job = pair; job < p.num_jobs; job += num_pairs, ++lt) {
+      int m_blk, n_blk, sub;
+      job_coords(job, p, m_blk, n_blk, sub);
       const uint32_t b = lt & 1u;
       const uint32_t aph = (lt >> 1) & 1u;
       if (!mbar_wait_cluster(tfull(b), aph, abort_flag, p.err)) break;
@@ -564,9 +594,12 @@ gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_b,
       const int64_t row = warp_row0 + lane;
       const bool row_ok = row < p.M;
       uint16_t* yrow = p.y + (row_ok ? row * p.ldy : 0);
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * BN + half * C::kCols0;
-      const int64_t n_warp = static_cast<int64_t>(n_blk) * BN + half * C::kCols0;
-      const int steps = (half ? C::kCols1 : C::kCols0) / 32;   // 32-column loads (even)
+      // Whole tile: columns [0, 128) (half 0) or [128, BN) (half 1). Half
+      // job: 64 columns each, [0, 64) and [64, 128) of its 128.
+      const int col0 = sub < 0 ? half * C::kCols0 : half * 64;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * BN + col0;
+      const int64_t n_warp = static_cast<int64_t>(n_blk) * BN + (sub < 0 ? 0 : sub * 128) + col0;
+      const int steps = sub < 0 ? (half ? C::kCols1 : C::kCols0) / 32 : 2;   // 32-column loads (even)
       uint32_t acc[32];
       tc_ld_32x32b_x32(t_row, acc);
 #pragma unroll 1
@@ -706,6 +739,17 @@ int pair_gemm_tile_width(int64_t M, int64_t N, int sm_count) {
   return (forced_bn == 256 || forced_bn == 192) ? forced_bn : pair_tile_width(M, N, sm_count);
 }
 
+namespace {
+// GW_GEMM_PAIR_TAIL=0 keeps the last round of tiles whole (tuning, tests).
+bool pair_tail_split_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("GW_GEMM_PAIR_TAIL");
+    return !(v && std::atoi(v) == 0);
+  }();
+  return on;
+}
+}  // namespace
+
 bool use_pair_gemm(int64_t M, int64_t N, int sm_count) {
   // GW_GEMM_PAIR=0 forces the single-CTA kernel, =1 the pair kernel (tuning, tests).
   static const int forced = [] {
@@ -735,19 +779,32 @@ cudaError_t launch_tc2_bn(int dtype, Tc2Params& p, const void* a, int64_t M, int
   p.m_tiles = static_cast<int>(m_tiles);
   p.n_tiles = static_cast<int>(n_tiles);
   p.num_tiles = static_cast<int>(num_tiles);
-  CUtensorMap ta, tb, ty;
+  CUtensorMap ta, tb, tbh, ty;
   // With a_cols, A is x [M, a_width] (K = the alive count, a multiple of 64).
   if (p.a_cols && (K % kBK2) != 0) return cudaErrorInvalidValue;
   if (!make_tmap_kmajor(&ta, a, M, p.a_cols ? p.a_width : K, lda, kBK2, kHalfM))
     return cudaErrorInvalidValue;
   if (!make_tmap_kmajor(&tb, w, N, K, ldw, kBK2, C::kHalfN)) return cudaErrorInvalidValue;
+  tbh = tb;                  // read only by half jobs (set below)
   // TMA-store epilogue when y's rows are 16-byte aligned (else direct stores).
   p.y_tma = p.y_vec_ok && make_tmap_kmajor(&ty, y, M, N, ldy, kEpiCols, 32) ? 1 : 0;
   if (!p.y_tma) ty = ta;     // not read by the kernel
   if (p.n_peers > 0 && !p.y_tma) return cudaErrorInvalidValue;   // peer stores ride the TMA path
 
   const int64_t pairs = std::max<int64_t>(1, (sm_count > 0 ? sm_count : 148) / 2);
-  const int grid = static_cast<int>(2 * std::min<int64_t>(num_tiles, pairs));
+  // The last, partial round of 256-wide tiles leaves pairs idle for a whole
+  // tile time. When at most half the pairs would be busy in it, its tiles run
+  // as two 128-column jobs each, so the round takes a half job (which loads
+  // three quarters of a tile's bytes) and spreads over twice as many pairs.
+  p.num_full = p.num_tiles;
+  p.num_jobs = p.num_tiles;
+  const int64_t rem = num_tiles % pairs;
+  if (BN == 256 && !p.ghdr && pair_tail_split_enabled() && rem > 0 && 2 * rem <= pairs) {
+    if (!make_tmap_kmajor(&tbh, w, N, K, ldw, kBK2, 64)) return cudaErrorInvalidValue;
+    p.num_full = static_cast<int>(num_tiles - rem);
+    p.num_jobs = static_cast<int>(num_tiles + rem);
+  }
+  const int grid = static_cast<int>(2 * std::min<int64_t>(p.num_jobs, pairs));
   if (p.ghdr) {
     // In-kernel gather: tiles row block by row block; claim groups of as many
     // half-panels as one wave of tiles spans.
@@ -781,7 +838,7 @@ cudaError_t launch_tc2_bn(int dtype, Tc2Params& p, const void* a, int64_t M, int
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, tb, ta, ty, p);
+  return cudaLaunchKernelEx(&cfg, kern, tb, tbh, ta, ty, p);
 }
 
 cudaError_t launch_gemm_tc2(const void* a, int dtype, int64_t M, int64_t K, int64_t lda,
