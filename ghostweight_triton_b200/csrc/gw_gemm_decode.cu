@@ -64,7 +64,9 @@ struct DcCfg {
   // of the block) has the same shape and lives in the ring.
   static constexpr int kRecvStride = MP + 4;                    // floats per row
   static constexpr int kRecvBytes = kDcN * kRecvStride * 4;
-  static constexpr int kTmemCols = MP < 32 ? 32 : MP;           // power of two >= 32
+  // Two accumulators of MP columns (even and odd k-blocks, issued by two
+  // threads), a power of two >= 32.
+  static constexpr int kTmemCols = 2 * MP < 32 ? 32 : 2 * MP;
   static constexpr int kSmemBytes = 1024 + kRingBytes + kRecvBytes + 256;
   // Two CTAs per SM (228 KB of shared memory, 1 KB reserved per CTA).
   static_assert(2 * (kSmemBytes + 1024) <= 233472, "two CTAs per SM");
@@ -182,6 +184,36 @@ __device__ __forceinline__ void dc_finish(const DcParams& p, const float* recv, 
   }
 }
 
+// Issues the MMAs of k-blocks first, first + step, ... of this CTA's range
+// (local indices; `used` counts ring slots in order) into accumulator d, with
+// one commit per k-block to its stage's empty barrier, then one to tfull (or
+// raises the abort flag) and one to drain_bar.
+template <int MP, int DT, typename FullF, typename EmptyF>
+__device__ __forceinline__ void dc_issue(const DcParams& p, uint32_t sbase, uint32_t d, int nk,
+                                         int first, int step, FullF full, EmptyF empty,
+                                         uint32_t tfull, uint32_t drain_bar,
+                                         volatile int* abort_flag) {
+  using C = DcCfg<MP>;
+  constexpr uint32_t idesc = idesc_f16(DT == GW_DTYPE_BF16 ? 1u : 0u, kDcN, MP);
+  bool ok = true;
+  for (int used = first; used < nk; used += step) {
+    const int s = used % C::kStages;
+    const uint32_t ph = (used / C::kStages) & 1u;
+    if (!mbar_wait(full(s), ph, abort_flag, p.err)) { ok = false; break; }
+    tc_fence_after();
+    const uint32_t w_s = sbase + s * C::kStageBytes;
+    const uint64_t w_desc = smem_desc_kmajor_sw128(w_s);
+    const uint64_t a_desc = smem_desc_kmajor_sw128(w_s + kDcWBytes);
+#pragma unroll
+    for (int k = 0; k < kDcK / 16; ++k)
+      tc_mma_f16(d, w_desc + 2u * k, a_desc + 2u * k, idesc, (used > first || k > 0) ? 1u : 0u);
+    tc_commit(empty(s));
+  }
+  if (ok) tc_commit(tfull);
+  else *abort_flag = 1;            // the drain warps stop waiting for tfull
+  tc_commit(drain_bar);
+}
+
 template <int MP, int DT>
 __global__ void __launch_bounds__(kDcThreads, 2)
 gemm_decode_kernel(const __grid_constant__ CUtensorMap tmap_w,
@@ -215,14 +247,20 @@ gemm_decode_kernel(const __grid_constant__ CUtensorMap tmap_w,
   const int S = p.split;
   const int F = kDcN / S;                                 // features per slice
   const uint32_t slice_bytes = static_cast<uint32_t>(F * C::kRecvStride * 4);
+  // One thread issuing waits about 200 cycles per stage and 70-80 per MMA,
+  // more than the tensor core needs for a 128 x MP x 64 k-block, so the main
+  // loop is issue-bound. With two k-blocks or more (and no gather, whose warps
+  // are busy), warp 1 issues the even k-blocks into accumulator 0 and the
+  // first drain warp the odd ones into accumulator 1; the drain adds the two.
+  const bool dual = !p.gx && kb1 - kb0 >= 2;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(full(s), p.gx ? 2 : 1);    // gather mode: the producer's and the gathering warp's arrivals
       mbar_init(empty(s), 1);
     }
-    mbar_init(tfull, 1);
-    mbar_init(drain_bar, 1);
+    mbar_init(tfull, dual ? 2 : 1);       // one commit per issuing thread
+    mbar_init(drain_bar, dual ? 2 : 1);
     mbar_init(recv_bar, 1);
     mbar_init(sent_bar, static_cast<uint32_t>(S));
     // Every CTA of the cluster (this one included) sends one slice here.
@@ -292,32 +330,22 @@ gemm_decode_kernel(const __grid_constant__ CUtensorMap tmap_w,
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+    // ------------------------------------------------------------ MMA issuer (even k-blocks)
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16(DT == GW_DTYPE_BF16 ? 1u : 0u, kDcN, MP);
-      bool ok = true;
-      int used = 0;
-      for (int kb = kb0; kb < kb1; ++kb, ++used) {
-        const int s = used % C::kStages;
-        const uint32_t ph = (used / C::kStages) & 1u;
-        if (!mbar_wait(full(s), ph, abort_flag, p.err)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t w_s = sbase + s * C::kStageBytes;
-        const uint64_t w_desc = smem_desc_kmajor_sw128(w_s);
-        const uint64_t a_desc = smem_desc_kmajor_sw128(w_s + kDcWBytes);
-#pragma unroll
-        for (int k = 0; k < kDcK / 16; ++k)
-          tc_mma_f16(tmem_base, w_desc + 2u * k, a_desc + 2u * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
-        tc_commit(empty(s));
-      }
-      if (ok) tc_commit(tfull);
-      else *abort_flag = 1;            // the drain warps stop waiting for tfull
-      // Every MMA has finished writing TMEM before TMEM is freed.
-      tc_commit(drain_bar);
+      dc_issue<MP, DT>(p, sbase, tmem_base, kb1 - kb0, 0, dual ? 2 : 1, full, empty, tfull,
+                       drain_bar, abort_flag);
+      // Every MMA (of both issuers) has finished writing TMEM before TMEM is freed.
       mbar_wait(drain_bar, 0u, nullptr, p.err, 100000000ull);
     }
     __syncwarp();
   } else {
+    if (dual && warp == 2) {
+      // ---------------------------------------------------------- MMA issuer (odd k-blocks)
+      if (lane == 0)
+        dc_issue<MP, DT>(p, sbase, tmem_base + MP, kb1 - kb0, 1, 2, full, empty, tfull, drain_bar,
+                         abort_flag);
+      __syncwarp();
+    }
     if (p.gx) {
       // ---------------------------------------------------------- gather a
       // Warp w fills the a tiles of stages w - 2, w + 2, ... (x and the alive
@@ -341,10 +369,20 @@ gemm_decode_kernel(const __grid_constant__ CUtensorMap tmap_w,
     // column m of the accumulator is row m of y.
     if (mbar_wait(tfull, 0u, abort_flag, p.err)) {
       tc_fence_after();
+      const uint32_t t_lane = tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16);
 #pragma unroll
-      for (int c = 0; c < MP; c += 16)
-        tc_ld_32x32b_x16(tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16) + c, acc + c);
-      tc_wait_ld();
+      for (int c = 0; c < MP; c += 16) tc_ld_32x32b_x16(t_lane + c, acc + c);
+      if (dual) {
+        uint32_t odd[MP];
+#pragma unroll
+        for (int c = 0; c < MP; c += 16) tc_ld_32x32b_x16(t_lane + MP + c, odd + c);
+        tc_wait_ld();
+#pragma unroll
+        for (int c = 0; c < MP; ++c)
+          acc[c] = __float_as_uint(__uint_as_float(acc[c]) + __uint_as_float(odd[c]));
+      } else {
+        tc_wait_ld();
+      }
     }
     tc_fence_before();
   }
