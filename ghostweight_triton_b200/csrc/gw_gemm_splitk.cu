@@ -58,7 +58,13 @@ struct SkCfg {
   static constexpr int kRedBytes = kSkBM * kRedStride * 4;
   static constexpr int kRingBytes =
       kStages * kStageBytes > kRedBytes ? kStages * kStageBytes : kRedBytes;
-  static constexpr int kTmemCols = BN < 32 ? 32 : BN;             // power of two >= 32
+  // Up to 128 columns a stage's four MMAs take fewer tensor cycles than one
+  // issuing thread needs (about 200 cycles per stage wait, 70-80 per MMA), so
+  // two threads issue: even k-blocks into accumulator 0, odd ones into
+  // accumulator 1 (BN columns further on), which the drain adds.
+  static constexpr bool kDual = BN <= 128;
+  static constexpr int kAccCols = kDual ? 2 * BN : BN;
+  static constexpr int kTmemCols = kAccCols < 32 ? 32 : kAccCols;  // power of two >= 32
   static constexpr int kSmemBytes = 1024 + kRingBytes + 256;
   static_assert(kSmemBytes <= 232448, "shared memory budget per CTA");
 };
@@ -170,6 +176,36 @@ __device__ __forceinline__ void reduce_slice(const SkParams& p, uint32_t red_loc
   asm volatile("" ::"f"(sink));
 }
 
+// Issues the MMAs of k-blocks first, first + step, ... of this CTA's range
+// (local indices) into accumulator d, one commit per k-block to its stage's
+// empty barrier, then one to tfull (or raises the abort flag) and one to
+// drain_bar.
+template <int BN, int DT, typename FullF, typename EmptyF>
+__device__ __forceinline__ void sk_issue(const SkParams& p, uint32_t sbase, uint32_t d, int nk,
+                                         int first, int step, FullF full, EmptyF empty,
+                                         uint32_t tfull, uint32_t drain_bar,
+                                         volatile int* abort_flag) {
+  using C = SkCfg<BN>;
+  constexpr uint32_t idesc = idesc_f16(DT == GW_DTYPE_BF16 ? 1u : 0u, kSkBM, BN);
+  bool ok = true;
+  for (int used = first; used < nk; used += step) {
+    const int s = used % C::kStages;
+    const uint32_t ph = (used / C::kStages) & 1u;
+    if (!mbar_wait(full(s), ph, abort_flag, p.err)) { ok = false; break; }
+    tc_fence_after();
+    const uint32_t a_s = sbase + s * C::kStageBytes;
+    const uint64_t a_desc = smem_desc_kmajor_sw128(a_s);
+    const uint64_t b_desc = smem_desc_kmajor_sw128(a_s + C::kABytes);
+#pragma unroll
+    for (int k = 0; k < kSkBK / 16; ++k)
+      tc_mma_f16(d, a_desc + 2u * k, b_desc + 2u * k, idesc, (used > first || k > 0) ? 1u : 0u);
+    tc_commit(empty(s));
+  }
+  if (ok) tc_commit(tfull);
+  else *abort_flag = 1;            // the drain warps stop waiting for tfull
+  tc_commit(drain_bar);
+}
+
 template <int BN, int DT, int EPI>
 __global__ void __launch_bounds__(kSkThreads, 1)
 gemm_splitk_kernel(const __grid_constant__ CUtensorMap tmap_b,
@@ -200,14 +236,15 @@ gemm_splitk_kernel(const __grid_constant__ CUtensorMap tmap_b,
   const int kb1 = static_cast<int>(static_cast<int64_t>(rank + 1) * p.num_kb / p.split);
   const int64_t rows_left = p.M - static_cast<int64_t>(m_blk) * kSkBM;
   const int rows_valid = rows_left >= kSkBM ? kSkBM : static_cast<int>(rows_left);
+  const bool dual = C::kDual && kb1 - kb0 >= 2;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(full(s), 1);
       mbar_init(empty(s), 1);
     }
-    mbar_init(tfull, 1);
-    mbar_init(drain_bar, 1);
+    mbar_init(tfull, dual ? 2 : 1);       // one commit per issuing thread
+    mbar_init(drain_bar, dual ? 2 : 1);
     *abort_flag = 0;
     *acc_ok = 0;
     mbar_init_fence();
@@ -254,33 +291,24 @@ gemm_splitk_kernel(const __grid_constant__ CUtensorMap tmap_b,
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+    // ------------------------------------------------------------ MMA issuer (even k-blocks)
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16(DT == GW_DTYPE_BF16 ? 1u : 0u, kSkBM, BN);
-      bool ok = true;
-      int used = 0;
-      for (int kb = kb0; kb < kb1; ++kb, ++used) {
-        const int s = used % C::kStages;
-        const uint32_t ph = (used / C::kStages) & 1u;
-        if (!mbar_wait(full(s), ph, abort_flag, p.err)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t a_s = sbase + s * C::kStageBytes;
-        const uint64_t a_desc = smem_desc_kmajor_sw128(a_s);
-        const uint64_t b_desc = smem_desc_kmajor_sw128(a_s + C::kABytes);
-#pragma unroll
-        for (int k = 0; k < kSkBK / 16; ++k)
-          tc_mma_f16(tmem_base, a_desc + 2u * k, b_desc + 2u * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
-        tc_commit(empty(s));
-      }
-      if (ok) tc_commit(tfull);
-      else *abort_flag = 1;            // the drain warps stop waiting for tfull
-      // Every MMA has finished reading shared memory and writing TMEM before
-      // the ring is reused as the reduction buffer and TMEM is freed.
-      tc_commit(drain_bar);
+      sk_issue<BN, DT>(p, sbase, tmem_base, kb1 - kb0, 0, dual ? 2 : 1, full, empty, tfull, drain_bar,
+                       abort_flag);
+      // Every MMA (of both issuers) has finished reading shared memory and
+      // writing TMEM before the ring is reused as the reduction buffer and
+      // TMEM is freed.
       mbar_wait(drain_bar, 0u, nullptr, p.err, 100000000ull);
     }
     __syncwarp();
   } else {
+    if (dual && warp == 2) {
+      // ---------------------------------------------------------- MMA issuer (odd k-blocks)
+      if (lane == 0)
+        sk_issue<BN, DT>(p, sbase, tmem_base + BN, kb1 - kb0, 1, 2, full, empty, tfull, drain_bar,
+                         abort_flag);
+      __syncwarp();
+    }
     // ------------------------------------------------------------ TMEM drain
     // Warp w reads TMEM lanes 32 (w % 4) .. +31 = rows of the tile.
     const int q = warp & 3;
@@ -292,8 +320,18 @@ gemm_splitk_kernel(const __grid_constant__ CUtensorMap tmap_b,
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t acc[32];
-          tc_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + c * 32, acc);
-          tc_wait_ld();
+          const uint32_t t_chunk = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + c * 32;
+          tc_ld_32x32b_x32(t_chunk, acc);
+          if (dual) {
+            uint32_t odd[32];
+            tc_ld_32x32b_x32(t_chunk + BN, odd);
+            tc_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              acc[j] = __float_as_uint(__uint_as_float(acc[j]) + __uint_as_float(odd[j]));
+          } else {
+            tc_wait_ld();
+          }
           if (row < rows_valid) {
             float4* dst = reinterpret_cast<float4*>(red_row + c * 32);
 #pragma unroll
