@@ -715,9 +715,25 @@ def run_ours(args, world, rank, local):
     ldp = (kp + 63) // 64 * 64
     xg = torch.empty(M, ldp, dtype=torch.float16, device=device)[:, :kp]   # x' for the kernels timed alone
 
+    from ghostweight_triton_b200.kernels.matmul import ghost_linear_pipelined
+
     def step(i):
+        # One step alone: the gather launch, then the PDL-chained GEMM launch
+        # (or the single-launch overlap strategy).
         L = layers[i % N_SETS]
-        _native.gather_gemm(L["x"], L["wp"], L["idx"], L["y"], strategy=args.strategy, workspace=ws)
+        _native.gather_gemm(L["x"], L["wp"], L["idx"], L["y"],
+                            strategy="overlap" if args.strategy == "overlap" else "pregather", workspace=ws)
+
+    def run_steps(n):
+        # n consecutive steps, each a whole gather-GEMM of its own batch. With
+        # the pipelined strategy they go through ghost_linear_pipelined: step
+        # i+1's gather runs on a low-priority stream under step i's GEMM.
+        if args.strategy == "pipelined":
+            ghost_linear_pipelined([(L["x"], L["wp"], L["idx"], L["y"])
+                                    for L in (layers[i % N_SETS] for i in range(n))])
+        else:
+            for i in range(n):
+                step(i)
 
     def step_overlap(i):
         L = layers[i % N_SETS]
@@ -733,19 +749,19 @@ def run_ours(args, world, rank, local):
 
     # Warm-up, then a clock-sampled soak of ~1 s so the sampler sees the load,
     # then exactly `steps` timed steps (the sampler keeps running through them).
-    for i in range(args.warmup):
-        step(i)
+    run_steps(args.warmup)
     torch.cuda.synchronize()
     sampler = ClockSampler(physical_gpu_index(local)).start() if rank == 0 else None
     t_soak = time.perf_counter()
     n_soak = 0
     while not args.no_soak and time.perf_counter() - t_soak < 1.0:
-        for i in range(200):
-            step(i)
+        run_steps(200)
         n_soak += 200
         torch.cuda.synchronize()
-    t = timed(step, args.steps, world)
+    t = timed(lambda _: run_steps(args.steps), 1, world)
     clocks = sampler.stop() if sampler else None
+    # The same K steps one call at a time (gather launch + GEMM launch each).
+    t_serial = timed(step, args.steps, world) / args.steps
 
     per_step = t / args.steps
     value = world * useful / per_step / 1e12
@@ -755,6 +771,7 @@ def run_ours(args, world, rank, local):
     t_gemm = timed(gemm_only, args.steps, world) / args.steps
     t_gather = timed(gather_only, args.steps, world) / args.steps
     t_ovl = timed(step_overlap, args.steps, world) / args.steps
+
     achieved = useful / t_gemm / 1e12
     gather_bytes = M * K * 2 + M * kp * 2 + kp * 8       # full rows read (50% random touches every sector) + x' written
     # e2e through the public API: GhostLinear (frozen weight mask), pinned host x in, y out.
@@ -873,6 +890,9 @@ def run_ours(args, world, rank, local):
             "config": {"workload": "gather-GEMM M=N=K=4096 fp16, 50% random dead input columns (K'=2048)",
                        "M": M, "N": N, "K": K, "K_alive": kp, "global_batch_rows": world * M,
                        "parallelism": f"independent batches per GPU x{world}",
+                       "step": ("one gather + one GEMM launch per batch; consecutive batches through "
+                                "ghost_linear_pipelined (batch i+1's gather under batch i's GEMM)"
+                                if args.strategy == "pipelined" else "one gather_gemm call per batch"),
                        "l2": f"{N_SETS} rotating layer sets (x, W', y) = {N_SETS * 80} MB > 126 MB L2",
                        "soak_steps_before_timing": n_soak},
             "dense_equiv_tflops": round(world * 2.0 * M * N * K / per_step / 1e12, 3),
@@ -897,10 +917,15 @@ def run_ours(args, world, rank, local):
                              "gather_alone_us": round(t_gather * 1e6, 2),
                              "gather_alone_GBps": round(gather_bytes / t_gather / 1e9, 1),
                              "gather_alone_frac_hbm": round(gather_bytes / t_gather / 1e9 / float(peaks["hbm_gbs"]), 3),
-                             "single_launch_overlap_us": round(t_ovl * 1e6, 2)},
-            "strategy": ("pregather (gather launch + PDL-chained TMA tcgen05 GEMM launch)"
-                         if args.strategy == "pregather" else
-                         "overlap (one launch: the pair GEMM's epilogue warps gather x' while its MMAs run)"),
+                             "single_launch_overlap_us": round(t_ovl * 1e6, 2),
+                             "one_call_at_a_time_step_us": round(t_serial * 1e6, 2),
+                             "one_call_at_a_time_tflops": round(world * useful / t_serial / 1e12, 2)},
+            "strategy": {"pipelined": "pipelined (ghost_linear_pipelined: each step's gather launch on a "
+                                      "low-priority stream under the previous step's GEMM launch, x' "
+                                      "double-buffered; every step gathers and multiplies its own batch)",
+                         "pregather": "pregather (gather launch + PDL-chained TMA tcgen05 GEMM launch)",
+                         "overlap": "overlap (one launch: the pair GEMM's epilogue warps gather x' while "
+                                    "its MMAs run)"}[args.strategy],
         }
         line.update(extra)
         print(json.dumps(line), flush=True)
@@ -1602,8 +1627,10 @@ def main():
     ap.add_argument("--no-reference-triton", action="store_true",
                     help="skip timing the reference's Triton kernels")
     ap.add_argument("--reference-triton-child", metavar="DIR", default=None, help=argparse.SUPPRESS)
-    ap.add_argument("--strategy", choices=["pregather", "overlap"], default="pregather",
-                    help="gemm workload: the gather-GEMM strategy of the timed step")
+    ap.add_argument("--strategy", choices=["pipelined", "pregather", "overlap"], default="pipelined",
+                    help="gemm workload: pipelined = consecutive steps through ghost_linear_pipelined "
+                         "(each step's gather under the previous step's GEMM); pregather / overlap = "
+                         "one gather_gemm call per step with that strategy")
     args = ap.parse_args()
     if args.reference_triton_child:
         reference_triton_child(args.reference_triton_child)

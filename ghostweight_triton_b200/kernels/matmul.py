@@ -214,3 +214,94 @@ def packed_linear(
     if y.numel():
         _native.packed_gemm(a, w_packed, y, bias=bias, activation=activation)
     return y
+
+
+class _PipeState:
+    """Per-device streams, events and x' buffers of ghost_linear_pipelined."""
+
+    def __init__(self, device: torch.device):
+        lo, hi = torch.cuda.Stream.priority_range()      # (least, greatest) priority
+        self.gemm = torch.cuda.Stream(device, priority=hi)
+        self.gather = torch.cuda.Stream(device, priority=lo)
+        self.ready = [torch.cuda.Event(), torch.cuda.Event()]
+        self.free = [torch.cuda.Event(), torch.cuda.Event()]
+        self.bufs: dict = {}
+
+    def xbuf(self, slot: int, dtype: torch.dtype, M: int, ldp: int, device) -> torch.Tensor:
+        key = (slot, dtype)
+        b = self.bufs.get(key)
+        if b is None or b.numel() < M * ldp:
+            b = self.bufs[key] = torch.empty(M * ldp, dtype=dtype, device=device)
+        return b[: M * ldp].view(M, ldp)
+
+
+_pipe_states: dict = {}
+
+
+def ghost_linear_pipelined(calls) -> list:
+    """Independent gather-GEMM calls with each gather overlapping the previous GEMM.
+
+    ``calls`` is a sequence of ``(x, w_packed, alive_indices, out[, bias[,
+    activation]])``, each meaning ``ghost_linear(x, w_packed, alive_indices,
+    bias, activation, out=out)``, and the outputs are returned in order. The
+    calls must not depend on one another (one call's output is not a later
+    call's input): call i+1's gather of x[:, alive] then runs on a
+    low-priority stream while call i's GEMM runs on a high-priority one. The
+    GEMM keeps the SMs it needs, and the gather fills the registers and issue
+    slots it leaves (the GEMM reads only a few percent of HBM bandwidth). x'
+    alternates between two buffers, ordered by events. The caller's current
+    stream waits for all of it before this returns. Calls with fewer than 256
+    rows, fp32 operands or index lists that are not int64 run as ``ghost_linear``
+    in order on the GEMM stream.
+    """
+    cur = torch.cuda.current_stream()
+    device = cur.device
+    st = _pipe_states.get(device.index)
+    if st is None:
+        st = _pipe_states[device.index] = _PipeState(device)
+    norm = []
+    for c in calls:
+        x, wp, idx, out = c[0], c[1], c[2], c[3]
+        bias = c[4] if len(c) > 4 else None
+        act = c[5] if len(c) > 5 else None
+        assert x.ndim == 2 and x.is_cuda and out is not None
+        norm.append((x, wp, idx, out, bias, act))
+    st.gemm.wait_stream(cur)
+    st.gather.wait_stream(cur)
+
+    def piped(c):
+        x, wp, idx, out, bias, act = c
+        return (x.shape[0] >= 256 and x.dtype is not torch.float32 and x.is_contiguous()
+                and idx.dtype is torch.int64 and idx.numel() > 0)
+
+    def gather(i):
+        x, wp, idx, _, _, _ = norm[i]
+        b = i % 2
+        kp = idx.numel()
+        ldp = (kp + 63) // 64 * 64
+        xg = st.xbuf(b, x.dtype, x.shape[0], ldp, device)[:, :kp]
+        st.gather.wait_event(st.free[b])
+        with torch.cuda.stream(st.gather):
+            _native.gather_columns(x, idx, xg)
+            st.ready[b].record(st.gather)
+        return xg
+
+    xgs = {}
+    if norm and piped(norm[0]):
+        xgs[0] = gather(0)
+    for i, c in enumerate(norm):
+        if i + 1 < len(norm) and piped(norm[i + 1]):
+            xgs[i + 1] = gather(i + 1)
+        x, wp, idx, out, bias, act = c
+        with torch.cuda.stream(st.gemm):
+            if i in xgs:
+                b = i % 2
+                st.gemm.wait_event(st.ready[b])
+                if out.numel():
+                    _native.packed_gemm(xgs.pop(i), wp, out, bias=bias, activation=act)
+                st.free[b].record(st.gemm)
+            else:
+                ghost_linear(x, wp, idx, bias=bias, activation=act, out=out)
+    cur.wait_stream(st.gemm)
+    cur.wait_stream(st.gather)
+    return [c[3] for c in norm]

@@ -1,0 +1,71 @@
+"""GPU: ghost_linear_pipelined (each call's gather overlapping the previous GEMM).
+
+Independent gather-GEMM calls run with the gather of call i+1 on a
+low-priority stream while call i's GEMM runs on a high-priority one, x'
+alternating between two buffers. Every output must equal the same call made
+alone through ghost_linear, bit for bit (the same kernels run on the same
+operands), for pipelined calls, for the calls that fall back to ghost_linear
+(few rows, fp32), with bias and GELU, and with shapes changing from call to
+call.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from ghostweight_triton_b200.kernels.gather import pack_weight
+from ghostweight_triton_b200.kernels.matmul import ghost_linear, ghost_linear_pipelined
+
+pytestmark = pytest.mark.gpu
+
+
+def _layer(M, K, N, kp, dtype, seed, bias=False):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x = torch.randn(M, K, device="cuda", generator=g).to(dtype)
+    w = (torch.randn(N, K, device="cuda", generator=g) / kp ** 0.5).to(dtype)
+    idx = torch.sort(torch.randperm(K, device="cuda", generator=g)[:kp]).values
+    b = torch.randn(N, device="cuda", generator=g).to(dtype) if bias else None
+    return x, pack_weight(w, idx), idx, b
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_pipelined_equals_one_call_at_a_time(dtype):
+    specs = [  # (M, K, N, K', bias, activation)
+        (4096, 4096, 4096, 2048, False, None),
+        (2048, 2048, 3072, 1000, True, "gelu_tanh"),
+        (4096, 4096, 4096, 2048, True, "gelu"),
+        (100, 1024, 512, 300, True, None),        # few rows: ghost_linear on the GEMM stream
+        (1024, 3072, 768, 1536, False, None),
+        (4096, 4096, 4096, 410, False, None),
+    ]
+    calls, refs = [], []
+    for s, (M, K, N, kp, bias, act) in enumerate(specs):
+        x, wp, idx, b = _layer(M, K, N, kp, dtype, 10 + s, bias)
+        refs.append(ghost_linear(x, wp, idx, bias=b, activation=act))
+        out = torch.full((M, N), float("nan"), device="cuda", dtype=dtype)
+        calls.append((x, wp, idx, out, b, act))
+    outs = ghost_linear_pipelined(calls)
+    torch.cuda.synchronize()
+    for o, r, c in zip(outs, refs, calls):
+        assert o is c[3]
+        assert torch.equal(o, r)
+
+
+def test_pipelined_repeated_and_fp32_fallback():
+    x, wp, idx, _ = _layer(4096, 2048, 2048, 1024, torch.float16, 3)
+    x32 = torch.randn(512, 256, device="cuda")
+    w32 = torch.randn(384, 256, device="cuda")
+    idx32 = torch.arange(0, 256, 2, device="cuda")
+    wp32 = pack_weight(w32, idx32)
+    ref = ghost_linear(x, wp, idx)
+    ref32 = ghost_linear(x32, wp32, idx32)
+    # Many calls through the same two x' slots, an fp32 call in between.
+    calls = [(x, wp, idx, torch.empty_like(ref)) for _ in range(7)]
+    calls.insert(3, (x32, wp32, idx32, torch.empty_like(ref32)))
+    outs = ghost_linear_pipelined(calls)
+    for i, o in enumerate(outs):
+        assert torch.equal(o, ref32 if i == 3 else ref)
+    # The caller's stream is ordered after every call: a kernel queued on it
+    # right away sees the results.
+    assert torch.equal(outs[-1].sum(), ref.sum())
