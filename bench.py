@@ -588,7 +588,7 @@ def sweep(device, peaks) -> list[dict]:
     """M in {4096, 1024, 128, 16} x sparsity x {random, block64}: ours vs dense cuBLAS."""
     import torch.nn.functional as F
 
-    from ghostweight_triton_b200.kernels.matmul import ghost_linear
+    from ghostweight_triton_b200.kernels.matmul import ghost_linear, ghost_linear_pipelined
 
     rows = []
     K = N = 4096
@@ -609,13 +609,21 @@ def sweep(device, peaks) -> list[dict]:
                 tdg = graph_time(lambda: [dense() for _ in range(20)], 20, 1) / 20
                 useful = 2.0 * M * N * kp
                 runs = {}
+                if M >= 1024:
+                    # The same 20 calls as independent batches through
+                    # ghost_linear_pipelined (each gather under the previous
+                    # GEMM), captured in one graph.
+                    tpg = graph_time(lambda: ghost_linear_pipelined(
+                        [(L["x"], L["wp"], L["idx"], L["y"])] * 20), 20, 1) / 20
+                    runs.update({"graph_pipelined_us": round(tpg * 1e6, 2),
+                                 "graph_pipelined_speedup_vs_dense": round(tdg / tpg, 3)})
                 if pattern.startswith("block"):
                     # 64-column runs: the GEMM reads x in place (no gather launch).
                     direct = lambda: ghost_linear(L["x"], L["wp"], L["idx"], out=L["y"], strategy="runs")
                     tr = event_time(lambda i: direct(), iters=20)
                     trg = graph_time(lambda: [direct() for _ in range(20)], 20, 1) / 20
-                    runs = {"runs_us": round(tr * 1e6, 2), "graph_runs_us": round(trg * 1e6, 2),
-                            "graph_runs_speedup_vs_dense": round(tdg / trg, 3)}
+                    runs.update({"runs_us": round(tr * 1e6, 2), "graph_runs_us": round(trg * 1e6, 2),
+                                 "graph_runs_speedup_vs_dense": round(tdg / trg, 3)})
                 rows.append({"M": M, "pattern": pattern, "sparsity": sp, "K_alive": kp,
                              "us": round(t * 1e6, 2), "useful_tflops": round(useful / t / 1e12, 1),
                              "dense_equiv_tflops": round(2.0 * M * N * K / t / 1e12, 1),

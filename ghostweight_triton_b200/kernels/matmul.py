@@ -250,9 +250,10 @@ def ghost_linear_pipelined(calls) -> list:
     GEMM keeps the SMs it needs, and the gather fills the registers and issue
     slots it leaves (the GEMM reads only a few percent of HBM bandwidth). x'
     alternates between two buffers, ordered by events. The caller's current
-    stream waits for all of it before this returns. Calls with fewer than 256
-    rows, fp32 operands or index lists that are not int64 run as ``ghost_linear``
-    in order on the GEMM stream.
+    stream waits for all of it before this returns, and the whole call can be
+    captured in a CUDA graph. Calls with fewer than 256 rows, fp32 operands or
+    index lists that are not int64 run as ``ghost_linear`` in order on the GEMM
+    stream.
     """
     cur = torch.cuda.current_stream()
     device = cur.device
@@ -268,6 +269,11 @@ def ghost_linear_pipelined(calls) -> list:
         norm.append((x, wp, idx, out, bias, act))
     st.gemm.wait_stream(cur)
     st.gather.wait_stream(cur)
+    # Both slots start free, ordered after the caller's work. Recording them
+    # here (not reusing an earlier call's events) also keeps every wait inside
+    # a CUDA graph capture that this call may be part of.
+    for e in st.free:
+        e.record(st.gemm)
 
     def piped(c):
         x, wp, idx, out, bias, act = c

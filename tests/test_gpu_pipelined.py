@@ -69,3 +69,26 @@ def test_pipelined_repeated_and_fp32_fallback():
     # The caller's stream is ordered after every call: a kernel queued on it
     # right away sees the results.
     assert torch.equal(outs[-1].sum(), ref.sum())
+
+
+def test_pipelined_captured_in_a_graph():
+    x, wp, idx, _ = _layer(4096, 2048, 2048, 1024, torch.float16, 5)
+    x2, wp2, idx2, b2 = _layer(2048, 1024, 3072, 700, torch.float16, 6, bias=True)
+    ref, ref2 = ghost_linear(x, wp, idx), ghost_linear(x2, wp2, idx2, bias=b2, activation="gelu")
+    outs = [torch.empty_like(ref), torch.empty_like(ref2), torch.empty_like(ref)]
+    ghost_linear_pipelined([(x, wp, idx, outs[0]), (x2, wp2, idx2, outs[1], b2, "gelu"),
+                            (x, wp, idx, outs[2])])          # eager first: events recorded outside
+    for o in outs:
+        o.zero_()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        ghost_linear_pipelined([(x, wp, idx, outs[0]), (x2, wp2, idx2, outs[1], b2, "gelu"),
+                                (x, wp, idx, outs[2])])
+    torch.cuda.current_stream().wait_stream(side)
+    for o in outs:
+        o.fill_(float("nan"))
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], ref) and torch.equal(outs[1], ref2) and torch.equal(outs[2], ref)
