@@ -231,6 +231,11 @@ class _PipeState:
         key = (slot, dtype)
         b = self.bufs.get(key)
         if b is None or b.numel() < M * ldp:
+            if b is not None:
+                # The gather and GEMM streams may still use the old buffer:
+                # the allocator reuses it only after their queued work.
+                b.record_stream(self.gather)
+                b.record_stream(self.gemm)
             b = self.bufs[key] = torch.empty(M * ldp, dtype=dtype, device=device)
         return b[: M * ldp].view(M, ldp)
 

@@ -92,3 +92,19 @@ def test_pipelined_captured_in_a_graph():
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(outs[0], ref) and torch.equal(outs[1], ref2) and torch.equal(outs[2], ref)
+
+
+def test_pipelined_growing_shapes_reuse_no_stale_buffer():
+    # Each call needs a larger x' than the one before, so both slots are
+    # replaced while earlier calls are still queued; a tensor allocated in
+    # between must not land on a buffer a queued GEMM still reads.
+    layers = [_layer(M, 2048, 1024, kp, torch.float16, 40 + i)
+              for i, (M, kp) in enumerate(((512, 256), (1024, 512), (2048, 1024), (4096, 2048)))]
+    refs = [ghost_linear(x, wp, idx) for x, wp, idx, _ in layers]
+    outs = ghost_linear_pipelined([(x, wp, idx, torch.empty_like(r))
+                                   for (x, wp, idx, _), r in zip(layers, refs)])
+    junk = [torch.full((4096, 4096), 7.0, dtype=torch.float16, device="cuda") for _ in range(4)]
+    torch.cuda.synchronize()
+    for o, r in zip(outs, refs):
+        assert torch.equal(o, r)
+    del junk
