@@ -32,7 +32,7 @@ __global__ void __launch_bounds__(kGThreads)
 gather_columns_kernel(const raw* __restrict__ src, int64_t rows, int64_t ld_src, int64_t cols_src,
                       const int64_t* __restrict__ idx, int64_t n_idx, raw* __restrict__ dst,
                       int64_t ld_dst, int64_t pad_to, unsigned int* err, int early_dependents,
-                      const int32_t* __restrict__ n_dev) {
+                      const int32_t* __restrict__ n_dev, int vec_rows) {
   // Launched as a programmatic dependent of the previous kernel of the stream
   // (which may have produced src or idx): wait for it to complete. When dst is
   // the x' of the GEMM launched next (early_dependents), let that GEMM start
@@ -71,6 +71,39 @@ gather_columns_kernel(const raw* __restrict__ src, int64_t rows, int64_t ld_src,
     scol[e] = c;
   }
   if (bad && blockIdx.y == 0 && warp == 0) raise_error(err, GW_DERR_BAD_INDEX);
+
+  // Runs: lanes 8k .. 8k+7 hold the 8 consecutive outputs c0 + 32 e + 8k ..
+  // + 7. When, in every such group, they come from 8 consecutive source
+  // columns starting at a multiple of 8 (a mask that kills whole column
+  // blocks), lane l instead moves outputs c0 + 8 l .. + 7 as one 16-byte
+  // vector per row. The test uses the indices already loaded (shuffles, no
+  // further loads), and every warp reaches the same answer from the same
+  // chunk, so the choice needs no barrier. Scattered, invalid or unaligned
+  // indices, a chunk past the alive count, unaligned rows and 4-byte elements
+  // keep the per-element loop below.
+  if (sizeof(raw) == 2 && vec_rows && c0 + kColChunk <= n_idx) {
+    // The first group decides most lists (a scattered list fails it at
+    // once); only a list that passes it has the other seven checked.
+    const int64_t base0 = __shfl_sync(0xFFFFFFFFu, scol[0], lane & ~7);
+    bool run = base0 >= 0 && (base0 & 7) == 0 && scol[0] == base0 + (lane & 7);
+    if (__all_sync(0xFFFFFFFFu, run)) {
+#pragma unroll
+      for (int e = 1; e < kColsPerLane; ++e) {
+        const int64_t base = __shfl_sync(0xFFFFFFFFu, scol[e], lane & ~7);
+        run = run && base >= 0 && (base & 7) == 0 && scol[e] == base + (lane & 7);
+      }
+    }
+    if (__all_sync(0xFFFFFFFFu, run)) {
+      const int64_t j0 = c0 + 8 * lane;
+      const int64_t v0 = __ldg(idx + j0);
+      for (int64_t r = static_cast<int64_t>(blockIdx.y) * kGWarps + warp; r < rows;
+           r += static_cast<int64_t>(gridDim.y) * kGWarps) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(src + r * ld_src + v0));
+        *reinterpret_cast<uint4*>(dst + r * ld_dst + j0) = v;
+      }
+      return;
+    }
+  }
 
   for (int64_t r = static_cast<int64_t>(blockIdx.y) * kGWarps + warp; r < rows;
        r += static_cast<int64_t>(gridDim.y) * kGWarps) {
@@ -219,16 +252,21 @@ cudaError_t launch_gather_columns(const void* src, int dtype, int64_t rows, int6
                                                    (target + col_blocks - 1) / col_blocks),
                                  65535);
   dim3 grid(static_cast<unsigned>(col_blocks), gy);
+  // Whole 16-byte vectors of 16-bit rows can move at once (source and
+  // destination rows 16-byte aligned).
+  const int vec_rows = (dtype != GW_DTYPE_F32 &&
+                        ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15u) == 0 &&
+                        ld_src % 8 == 0 && ld_dst % 8 == 0) ? 1 : 0;
   if (dtype == GW_DTYPE_F32) {
     return launch_pdl(gather_columns_kernel<uint32_t>, grid, dim3(kGThreads), stream,
                       static_cast<const uint32_t*>(src), rows, ld_src, cols_src, idx, n_idx,
                       static_cast<uint32_t*>(dst), ld_dst, pad_to, err, early_dependents ? 1 : 0,
-                      n_dev);
+                      n_dev, 0);
   }
   return launch_pdl(gather_columns_kernel<uint16_t>, grid, dim3(kGThreads), stream,
                     static_cast<const uint16_t*>(src), rows, ld_src, cols_src, idx, n_idx,
                     static_cast<uint16_t*>(dst), ld_dst, pad_to, err, early_dependents ? 1 : 0,
-                    n_dev);
+                    n_dev, vec_rows);
 }
 
 namespace {

@@ -209,3 +209,23 @@ def test_gather_device_count(n):
     edge = max(-(-max(n, 1) // 64) * 64, 64)
     assert (got[:, n:edge] == 0).all()
     assert (got[:, edge:] == 5).all()
+
+
+@pytest.mark.parametrize("case", ["offset_runs", "runs_then_scattered", "run_across_chunks", "all"])
+def test_gather_runs_and_mixed_chunks(case):
+    # Chunks whose lanes' 8 outputs are 8 aligned consecutive columns move
+    # 16-byte vectors; the others gather per element. Both must be exact.
+    rows, cols = 700, 4096
+    x = rand_matrix((rows, cols), 13, "bf16")
+    rng = np.random.default_rng(9)
+    if case == "offset_runs":                       # runs starting 4 columns past an 8-column boundary
+        idx = np.concatenate([np.arange(4 + 128 * b, 4 + 128 * b + 64) for b in range(16)])
+    elif case == "runs_then_scattered":
+        idx = np.concatenate([np.arange(512, 1024), np.sort(rng.choice(np.arange(1024, cols), 700, replace=False))])
+    elif case == "run_across_chunks":               # one run crossing several 256-column chunks, ragged end
+        idx = np.arange(1000, 1000 + 1000)
+    else:
+        idx = np.arange(cols)
+    out = torch.full((rows, len(idx)), 3, dtype=torch.bfloat16, device="cuda")
+    _native.gather_columns(to_dev(x), torch.from_numpy(idx).cuda(), out)
+    assert np.array_equal(to_np(out), O.gather_columns(x, idx))
