@@ -243,6 +243,31 @@ class GhostLinear(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         """x : [..., in_features] -> [..., out_features] (arbitrary batch dims)."""
+        # Frozen mask, repeated call: everything the gather-GEMM needs was kept
+        # by the last call (_fast), and is used again while the weight, bias
+        # and alive list are the same tensors (same in-place versions and
+        # storage), the mask is still frozen, and the input dtype, activation
+        # and dense-fallback threshold are unchanged. The checks read the
+        # module's dicts directly; a frozen small layer otherwise spends more
+        # host time in attribute lookups than its kernels take on the GPU.
+        d = self.__dict__
+        fast = d.get("_fast")
+        if fast is not None:
+            (dtype, w, wv, wp, b, bv, bp, alive, av, act, min_sp, in_f, out_f,
+             w_packed, bias_c, strategy, sparsity) = fast
+            params = d["_parameters"]
+            if (x.dtype is dtype and d["_mask_frozen"] and d["_buffers"]["_frozen_indices"] is alive
+                    and alive._version == av and params["weight"] is w and w._version == wv
+                    and w.data_ptr() == wp and params.get("bias") is b
+                    and (b is None or (b._version == bv and b.data_ptr() == bp))
+                    and d.get("activation") == act and d["min_sparsity_to_activate"] == min_sp
+                    and x.is_cuda):
+                shape = x.shape
+                out = ghost_linear(x.reshape(-1, in_f), w_packed, alive, bias=bias_c, activation=act,
+                                   strategy=strategy)
+                d["_last_sparsity"] = sparsity
+                return out.reshape(*shape[:-1], out_f)
+            d["_fast"] = None
         orig_shape = x.shape
         x_2d = x.reshape(-1, self.in_features)
         assert x_2d.is_cuda, "GhostLinear runs on CUDA (sm_100) only"
@@ -278,6 +303,13 @@ class GhostLinear(nn.Module):
                 w_packed = pack_weight(self.weight.detach(), alive, dtype=x_2d.dtype)
             out = ghost_linear(x_2d, w_packed, alive, bias=bias, activation=self.activation,
                                strategy=strategy)
+            if frozen and not torch.cuda.is_current_stream_capturing():
+                w, b = self.weight, self.bias
+                self.__dict__["_fast"] = (
+                    x_2d.dtype, w, w._version, w.data_ptr(), b,
+                    None if b is None else b._version, None if b is None else b.data_ptr(),
+                    alive, alive._version, self.activation, self.min_sparsity_to_activate,
+                    self.in_features, self.out_features, w_packed, bias, strategy, float(sparsity))
         return out.reshape(*orig_shape[:-1], self.out_features)
 
     def _forward_sync_free(self, x_2d: torch.Tensor) -> torch.Tensor:
