@@ -357,6 +357,43 @@ def gather_gemm(x: torch.Tensor, w_packed: torch.Tensor, idx: torch.Tensor, y: t
         _check(st, "gw_gather_gemm")
 
 
+def prepare_gather_gemm(w_packed: torch.Tensor, idx: torch.Tensor, bias: torch.Tensor | None,
+                        activation: str | None, strategy: str, dtype: torch.dtype) -> tuple:
+    """The arguments of gw_gather_gemm that stay fixed across calls with one packed
+    weight, alive list and bias (for :func:`gather_gemm_prepared`). The tensors
+    must stay alive and unchanged while the tuple is used."""
+    _rowmajor(w_packed)
+    assert idx.dtype == torch.int64 and idx.is_contiguous()
+    n = idx.numel()
+    return (DTYPE_CODES[dtype], w_packed.data_ptr(), w_packed.shape[0], max(w_packed.stride(0), n),
+            idx.data_ptr(), n, _ptr(bias), epilogue_code(activation), GEMM_STRATEGIES[strategy])
+
+
+def gather_gemm_prepared(prep: tuple, x: torch.Tensor, y: torch.Tensor) -> None:
+    """gather_gemm(x, ...) with the fixed arguments of :func:`prepare_gather_gemm`.
+
+    x [M, K] must be contiguous and on the current device, y [M, N] contiguous.
+    The "runs" strategy falls back to "auto" for x rows that TMA cannot load in
+    place (not 16-byte aligned), as gather_gemm does.
+    """
+    dtc, wptr, N, ldw, iptr, n, bptr, epi, strat = prep
+    M, K = x.shape
+    if strat == GEMM_STRATEGIES["runs"] and (x.data_ptr() % 16 or K % 8):
+        strat = GEMM_STRATEGIES["auto"]
+    ws_ptr, ws_bytes = None, 0
+    if strat != GEMM_STRATEGIES["runs"] and strat != GEMM_STRATEGIES["fused"] and dtc != 2:
+        ws_bytes = gather_gemm_workspace_bytes(M, n, x.dtype)
+        if ws_bytes:
+            ws = gemm_workspace(x.device, ws_bytes)
+            ws_ptr, ws_bytes = ws.data_ptr(), ws.numel()
+    dev = x.get_device()
+    st = api().gw_gather_gemm(
+        x.data_ptr(), dtc, M, K, K, wptr, N, ldw, iptr, n, bptr, epi, y.data_ptr(), N, strat,
+        ws_ptr, ws_bytes, _raw_stream(dev) if _raw_stream is not None else torch.cuda.current_stream().cuda_stream)
+    if st:
+        _check(st, "gw_gather_gemm")
+
+
 def gather_columns_dev(src: torch.Tensor, idx: torch.Tensor, n_dev: torch.Tensor, dst: torch.Tensor,
                        pad_to: int) -> None:
     """dst[r, j] = src[r, idx[j]] for j < n (n = n_dev[0] on the device, at most len(idx)); zero

@@ -254,17 +254,21 @@ class GhostLinear(nn.Module):
         fast = d.get("_fast")
         if fast is not None:
             (dtype, w, wv, wp, b, bv, bp, alive, av, act, min_sp, in_f, out_f,
-             w_packed, bias_c, strategy, sparsity) = fast
+             w_packed, bias_c, prep, sparsity) = fast
             params = d["_parameters"]
             if (x.dtype is dtype and d["_mask_frozen"] and d["_buffers"]["_frozen_indices"] is alive
                     and alive._version == av and params["weight"] is w and w._version == wv
                     and w.data_ptr() == wp and params.get("bias") is b
                     and (b is None or (b._version == bv and b.data_ptr() == bp))
                     and d.get("activation") == act and d["min_sparsity_to_activate"] == min_sp
-                    and x.is_cuda):
+                    and x.is_cuda and x.get_device() == torch.cuda.current_device()):
                 shape = x.shape
-                out = ghost_linear(x.reshape(-1, in_f), w_packed, alive, bias=bias_c, activation=act,
-                                   strategy=strategy)
+                x_2d = x.reshape(-1, in_f)
+                if not x_2d.is_contiguous():
+                    x_2d = x_2d.contiguous()
+                out = x_2d.new_empty((x_2d.shape[0], out_f))
+                if x_2d.shape[0]:
+                    _native.gather_gemm_prepared(prep, x_2d, out)
                 d["_last_sparsity"] = sparsity
                 return out.reshape(*shape[:-1], out_f)
             d["_fast"] = None
@@ -303,13 +307,16 @@ class GhostLinear(nn.Module):
                 w_packed = pack_weight(self.weight.detach(), alive, dtype=x_2d.dtype)
             out = ghost_linear(x_2d, w_packed, alive, bias=bias, activation=self.activation,
                                strategy=strategy)
-            if frozen and not torch.cuda.is_current_stream_capturing():
+            if (frozen and not torch.cuda.is_current_stream_capturing()
+                    and alive.dtype is torch.int64 and alive.is_contiguous()):
                 w, b = self.weight, self.bias
                 self.__dict__["_fast"] = (
                     x_2d.dtype, w, w._version, w.data_ptr(), b,
                     None if b is None else b._version, None if b is None else b.data_ptr(),
                     alive, alive._version, self.activation, self.min_sparsity_to_activate,
-                    self.in_features, self.out_features, w_packed, bias, strategy, float(sparsity))
+                    self.in_features, self.out_features, w_packed, bias,
+                    _native.prepare_gather_gemm(w_packed, alive, bias, self.activation, strategy, x_2d.dtype),
+                    float(sparsity))
         return out.reshape(*orig_shape[:-1], self.out_features)
 
     def _forward_sync_free(self, x_2d: torch.Tensor) -> torch.Tensor:
