@@ -67,6 +67,17 @@ def ghostweight_matmul(
         alive_indices = alive_indices.to(device=activations.device, dtype=torch.int64)
     if not alive_indices.is_contiguous():
         alive_indices = alive_indices.contiguous()
+    if (bias is None and activation is None and strategy == "auto" and M and N
+            and activations.get_device() == torch.cuda.current_device()):
+        # The reference call without the extensions: the cached packed weight
+        # comes with gw_gather_gemm's fixed arguments prepared.
+        w_packed, prep = _packed_cache.get_prepared(weights, alive_indices, activations.dtype)
+        C = activations.new_empty((M, N))
+        if prep is not None:
+            _native.gather_gemm_prepared(prep, activations, C)
+        else:
+            _gemm(activations, w_packed, alive_indices, C, None, None, "auto")
+        return C
     C = torch.empty((M, N), dtype=activations.dtype, device=activations.device)
     if M == 0 or N == 0:
         return C
@@ -101,28 +112,39 @@ class _PackedCache:
         self.bytes = 0
 
     def get(self, weights: torch.Tensor, idx: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+        return self.get_prepared(weights, idx, dtype, prepare=False)[0]
+
+    def get_prepared(self, weights: torch.Tensor, idx: torch.Tensor, dtype: torch.dtype,
+                     prepare: bool = True) -> tuple:
+        """(packed weight, the fixed gw_gather_gemm arguments for it without bias,
+        activation or strategy choice, or None when the entry is not kept)."""
         key = (id(weights), id(idx), dtype)
         e = self._entries.get(key)
         if e is not None:
-            w_ref, i_ref, w_ver, i_ver, packed = e
+            w_ref, i_ref, w_ver, i_ver, packed, prep = e
             if (w_ref() is weights and i_ref() is idx and w_ver == weights._version
                     and i_ver == idx._version and not torch.cuda.is_current_stream_capturing()):
                 self._entries.move_to_end(key)
-                return packed
+                if prep is None and prepare:
+                    prep = e[5] = _native.prepare_gather_gemm(packed, idx, None, None, "auto", dtype)
+                return packed, prep
             self._drop(key)
         packed = pack_weight(weights.t(), idx, dtype=dtype)
         if torch.cuda.is_current_stream_capturing():
-            return packed           # a graph's private pool: do not keep it
+            return packed, None     # a graph's private pool: do not keep it
         nbytes = packed.untyped_storage().nbytes()
         if nbytes > self.max_bytes:
-            return packed
+            return packed, None
         cb = lambda _ref, key=key: self._drop(key)
-        self._entries[key] = (self._weakref.ref(weights, cb), self._weakref.ref(idx, cb),
-                              weights._version, idx._version, packed)
+        prep = _native.prepare_gather_gemm(packed, idx, None, None, "auto", dtype) if prepare else None
+        self._entries[key] = [self._weakref.ref(weights, cb), self._weakref.ref(idx, cb),
+                              weights._version, idx._version, packed, prep]
         self.bytes += nbytes
         while len(self._entries) > self.max_entries or self.bytes > self.max_bytes:
             self._drop(next(iter(self._entries)))
-        return packed
+        if key not in self._entries:
+            return packed, None
+        return packed, prep
 
     def _drop(self, key) -> None:
         e = self._entries.pop(key, None)
