@@ -609,10 +609,11 @@ def sweep(device, peaks) -> list[dict]:
                 tdg = graph_time(lambda: [dense() for _ in range(20)], 20, 1) / 20
                 useful = 2.0 * M * N * kp
                 runs = {}
-                if M >= 1024:
+                if M > 4:
                     # The same 20 calls as independent batches through
                     # ghost_linear_pipelined (each gather under the previous
-                    # GEMM), captured in one graph.
+                    # GEMM), captured in one graph. At most 4 rows the decode
+                    # kernel gathers x' itself and nothing is pipelined.
                     tpg = graph_time(lambda: ghost_linear_pipelined(
                         [(L["x"], L["wp"], L["idx"], L["y"])] * 20), 20, 1) / 20
                     runs.update({"graph_pipelined_us": round(tpg * 1e6, 2),
@@ -1203,7 +1204,7 @@ def run_small_batch(args, world, rank, local):
     import torch.nn.functional as F
 
     from ghostweight_triton_b200 import GhostLinear, _native
-    from ghostweight_triton_b200.kernels.matmul import ghost_linear
+    from ghostweight_triton_b200.kernels.matmul import ghost_linear, ghost_linear_pipelined
 
     device = torch.device("cuda", torch.cuda.current_device())
     peaks, peak_src = load_peaks()
@@ -1243,13 +1244,18 @@ def run_small_batch(args, world, rank, local):
         xg = [torch.randn(M, kp, device=device, generator=g).half() for _ in range(n_layers)]
         tg = per_layer(lambda i, x, y: (lambda: _native.packed_gemm(x, packed[i], y)), xg, ys)
         td = per_layer(lambda i, x, y: (lambda: torch.mm(x, dense_w[i].t(), out=y)), xs, ys)
+        # The 8 layer calls as independent batches: each gather runs under the
+        # previous layer's GEMM (ghost_linear_pipelined), one graph.
+        pcalls = [(xs[i], packed[i], layers[i]._frozen_indices, ys[i]) for i in range(n_layers)]
+        tp = graph_time(lambda: ghost_linear_pipelined(pcalls), reps, world) / n_layers
         kernel, tile_n, split = _native.gemm_plan(M, N, kp)
         rows[M] = {"M": M, "us": round(t * 1e6, 3), "useful_tflops": round(2.0 * M * N * kp / t / 1e12, 2),
                    "gemm_us": round(tg * 1e6, 3), "cublas_dense_us": round(td * 1e6, 3),
                    "speedup_vs_dense": round(td / t, 3), "gemm_speedup_vs_dense": round(td / tg, 3),
+                   "pipelined_us": round(tp * 1e6, 3), "pipelined_speedup_vs_dense": round(td / tp, 3),
                    "plan": {"kernel": kernel, "tile_n": tile_n, "split": split},
                    "max_abs_err_vs_fp32": err}
-        del xs, ys, xg
+        del xs, ys, xg, pcalls
     M = 256 if 256 in rows else ms[0]
     hx = [torch.randn(M, K).half().pin_memory() for _ in range(n_layers)]
     hy = torch.empty(M, N, dtype=torch.float16).pin_memory()

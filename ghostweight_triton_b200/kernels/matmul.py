@@ -278,9 +278,9 @@ def ghost_linear_pipelined(calls) -> list:
     slots it leaves (the GEMM reads only a few percent of HBM bandwidth). x'
     alternates between two buffers, ordered by events. The caller's current
     stream waits for all of it before this returns, and the whole call can be
-    captured in a CUDA graph. Calls with fewer than 256 rows, fp32 operands or
-    index lists that are not int64 run as ``ghost_linear`` in order on the GEMM
-    stream.
+    captured in a CUDA graph. Calls with at most 4 rows (the decode kernel
+    gathers x' itself, one launch), fp32 operands or index lists that are not
+    int64 run as ``ghost_linear`` in order on the GEMM stream.
     """
     cur = torch.cuda.current_stream()
     device = cur.device
@@ -304,7 +304,7 @@ def ghost_linear_pipelined(calls) -> list:
 
     def piped(c):
         x, wp, idx, out, bias, act = c
-        return (x.shape[0] >= 256 and x.dtype is not torch.float32 and x.is_contiguous()
+        return (x.shape[0] > 4 and x.dtype is not torch.float32 and x.is_contiguous()
                 and idx.dtype is torch.int64 and idx.numel() > 0)
 
     def gather(i):

@@ -35,7 +35,8 @@ def test_pipelined_equals_one_call_at_a_time(dtype):
         (4096, 4096, 4096, 2048, False, None),
         (2048, 2048, 3072, 1000, True, "gelu_tanh"),
         (4096, 4096, 4096, 2048, True, "gelu"),
-        (100, 1024, 512, 300, True, None),        # few rows: ghost_linear on the GEMM stream
+        (100, 1024, 512, 300, True, None),        # split-K GEMM under the pipeline
+        (3, 1024, 512, 300, True, None),          # decode rows: ghost_linear on the GEMM stream
         (1024, 3072, 768, 1536, False, None),
         (4096, 4096, 4096, 410, False, None),
     ]
