@@ -16,11 +16,16 @@
 //   * 4 rows are loaded per batch per thread (streaming, no L1 allocation),
 //     the last batch of a chunk included (clamped rows, masked results);
 //   * a warp whose columns are all alive stops reading (warp-uniform exit);
-//   * per-CTA alive bits are OR-ed into a 32-bit word array in the workspace;
+//   * per-CTA alive bits are OR-ed into a 32-bit word array in the workspace,
+//     then the CTA takes a ticket with one acquire-release atomic;
 //   * the last CTA to finish (ticket counter) performs the compaction: a
-//     block-wide prefix sum of popcounts emits mask[], the ascending alive
-//     index list (the torch.nonzero of module.py:104) and the count, and resets
-//     the workspace to zero for the next call.
+//     block-wide prefix sum of popcounts places every alive column's index in
+//     shared memory, from where mask[], the ascending alive index list (the
+//     torch.nonzero of module.py:104) and the count are written with coalesced
+//     stores; it also resets the workspace to zero for the next call. (One
+//     thread per flag word writing its own indices scatters 8-byte stores over
+//     the index list, about one L2 transaction each, which took the last CTA
+//     about 1 us longer at 4096 columns.)
 #include "gw_common.cuh"
 #include "gw_internal.h"
 
@@ -41,6 +46,21 @@ __device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
   return v;
 }
+
+__device__ __forceinline__ uint32_t atom_add_acq_rel(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+__device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Columns the last CTA compacts per pass: one flag word per thread.
+constexpr int kPassCols = kMaskThreads * 32;
 
 // Alive bits (bit e for element e) of one 16-byte vector.
 template <int DT>
@@ -88,7 +108,9 @@ mask_compact_kernel(const void* __restrict__ x, int64_t rows, int64_t cols, int6
 
   __shared__ uint32_t s_bits[kMaskWarps][32];
   __shared__ int s_last;
-  __shared__ int64_t s_scan[kMaskWarps];
+  __shared__ int s_scan[kMaskWarps];
+  __shared__ uint32_t s_word[kMaskThreads];
+  __shared__ uint16_t s_pos[kPassCols];   // alive columns of one pass, relative to its start
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -145,11 +167,13 @@ mask_compact_kernel(const void* __restrict__ x, int64_t rows, int64_t cols, int6
       const int64_t w_idx = (static_cast<int64_t>(blockIdx.x) * 32 * VPT + lane * VPT) / 32;
       atomicOr(flags + w_idx, word);
     }
+    // __syncwarp orders the other lanes' flag updates before lane 0's
+    // release; the acquire half makes every CTA's flags visible to the last
+    // one, whose other threads read them after the barrier below.
     __syncwarp();
     if (lane == 0) {
-      __threadfence();
       const uint32_t total = gridDim.x * gridDim.y;
-      const uint32_t prev = atomicAdd(ticket, 1u);
+      const uint32_t prev = atom_add_acq_rel(ticket, 1u);
       s_last = (prev == total - 1u) ? 1 : 0;
     }
   }
@@ -157,20 +181,18 @@ mask_compact_kernel(const void* __restrict__ x, int64_t rows, int64_t cols, int6
   if (!s_last) return;
 
   // ---- Last CTA: stream compaction over the alive words --------------------
-  __threadfence();
   const int64_t nwords = (cols + 31) / 32;
-  int64_t base = 0;
   const bool mask_vec = (reinterpret_cast<uintptr_t>(mask) & 15u) == 0;
+  int64_t base = 0;
   for (int64_t w0 = 0; w0 < nwords; w0 += kMaskThreads) {
     const int64_t w = w0 + threadIdx.x;
     uint32_t word = 0;
-    int nvalid = 0;
     if (w < nwords) {
-      word = atomicExch(flags + w, 0u);
+      word = ld_relaxed_gpu(flags + w);
+      flags[w] = 0u;
       if (all_alive) word = 0xFFFFFFFFu;
       const int64_t rem = cols - w * 32;
-      nvalid = rem < 32 ? static_cast<int>(rem) : 32;
-      if (nvalid < 32) word &= (1u << nvalid) - 1u;
+      if (rem < 32) word &= (1u << rem) - 1u;
     }
     // Block-wide exclusive scan of popcounts.
     const int c = __popc(word);
@@ -181,41 +203,42 @@ mask_compact_kernel(const void* __restrict__ x, int64_t rows, int64_t cols, int6
       if (lane >= off) incl += t;
     }
     if (lane == 31) s_scan[warp] = incl;
+    s_word[threadIdx.x] = word;
     __syncthreads();
-    int64_t warp_base = 0, block_total = 0;
+    int warp_base = 0, pass_total = 0;
 #pragma unroll
     for (int i = 0; i < kMaskWarps; ++i) {
       if (i < warp) warp_base += s_scan[i];
-      block_total += s_scan[i];
+      pass_total += s_scan[i];
     }
-    int64_t pos = base + warp_base + (incl - c);
-    if (w < nwords) {
-      if (mask) {
-        int32_t* mrow = mask + w * 32;
-        if (mask_vec && nvalid == 32) {
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            int4 m4;
-            m4.x = (word >> (4 * q + 0)) & 1u;
-            m4.y = (word >> (4 * q + 1)) & 1u;
-            m4.z = (word >> (4 * q + 2)) & 1u;
-            m4.w = (word >> (4 * q + 3)) & 1u;
-            reinterpret_cast<int4*>(mrow)[q] = m4;
-          }
-        } else {
-          for (int e = 0; e < nvalid; ++e) mrow[e] = (word >> e) & 1u;
-        }
-      }
-      if (idx) {
-        uint32_t rest = word;
-        while (rest) {
-          const int e = __ffs(rest) - 1;
-          idx[pos++] = w * 32 + e;
-          rest &= rest - 1u;
-        }
+    if (idx) {
+      int p = warp_base + (incl - c);
+      uint32_t rest = word;
+      while (rest) {
+        const int e = __ffs(rest) - 1;
+        s_pos[p++] = static_cast<uint16_t>(threadIdx.x * 32 + e);
+        rest &= rest - 1u;
       }
     }
-    base += block_total;
+    __syncthreads();
+    const int64_t c0 = w0 * 32;
+    const int pcols = static_cast<int>(min(static_cast<int64_t>(kPassCols), cols - c0));
+    if (mask) {
+      int done = 0;
+      if (mask_vec) {
+        int4* m4 = reinterpret_cast<int4*>(mask + c0);
+        for (int q = threadIdx.x; q < pcols / 4; q += kMaskThreads) {
+          const uint32_t b = s_word[q >> 3] >> ((q & 7) * 4);
+          m4[q] = make_int4(b & 1u, (b >> 1) & 1u, (b >> 2) & 1u, (b >> 3) & 1u);
+        }
+        done = pcols & ~3;
+      }
+      for (int q = done + threadIdx.x; q < pcols; q += kMaskThreads)
+        mask[c0 + q] = (s_word[q >> 5] >> (q & 31)) & 1u;
+    }
+    if (idx)
+      for (int j = threadIdx.x; j < pass_total; j += kMaskThreads) idx[base + j] = c0 + s_pos[j];
+    base += pass_total;
     __syncthreads();
   }
   if (threadIdx.x == 0) {
