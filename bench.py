@@ -769,17 +769,48 @@ def run_ours(args, world, rank, local):
         torch.cuda.synchronize()
     t = timed(lambda _: run_steps(args.steps), 1, world)
     clocks = sampler.stop() if sampler else None
-    # The same K steps one call at a time (gather launch + GEMM launch each).
-    t_serial = timed(step, args.steps, world) / args.steps
-
-    per_step = t / args.steps
-    value = world * useful / per_step / 1e12
-    # The dominant kernel: the tcgen05 GEMM on the gathered operand, timed alone.
-    # For the breakdown also the gather alone and the single-launch "overlap"
-    # variant (gather inside the GEMM kernel).
+    # The dominant kernel: the tcgen05 GEMM on the gathered operand, timed alone
+    # (short windows, compared with the burst peak). For the breakdown also the
+    # gather alone and the single-launch "overlap" variant (gather inside the
+    # GEMM kernel).
     t_gemm = timed(gemm_only, args.steps, world) / args.steps
     t_gather = timed(gather_only, args.steps, world) / args.steps
     t_ovl = timed(step_overlap, args.steps, world) / args.steps
+    # The same K steps one call at a time (gather launch + GEMM launch each),
+    # against the pipelined steps under the same clocks: under the 1000 W cap
+    # the SM clock follows the load within milliseconds, so each window of an
+    # interleaved A/B follows a 0.3 s soak of its own kind, and the medians of
+    # three rounds are reported.
+    def soak_with(fn_n):
+        t0 = time.perf_counter()
+        while not args.no_soak and time.perf_counter() - t0 < 0.3:
+            fn_n(50)
+            torch.cuda.synchronize()
+
+    def serial_steps(n):
+        for i in range(n):
+            step(i)
+
+    ab = None
+    if args.strategy == "pipelined":
+        ab_p, ab_s = [], []
+        for _ in range(3):
+            soak_with(run_steps)
+            ab_p.append(timed(lambda _: run_steps(args.steps), 1, world) / args.steps)
+            soak_with(serial_steps)
+            ab_s.append(timed(step, args.steps, world) / args.steps)
+        t_serial = sorted(ab_s)[1]
+        ab = {"pipelined_us": round(sorted(ab_p)[1] * 1e6, 2), "one_call_at_a_time_us": round(t_serial * 1e6, 2),
+              "pipelined_speedup": round(t_serial / sorted(ab_p)[1], 3), "rounds": 3,
+              "soak_s_before_each_window": 0.0 if args.no_soak else 0.3,
+              "note": ("at the 1000 W cap both variants do the same work for the same energy, so "
+                       "they run at the same rate within a few percent; the pipelined one gains "
+                       "where the clocks are not capped (short bursts, graph-replayed sweeps)")}
+    else:
+        t_serial = timed(step, args.steps, world) / args.steps
+
+    per_step = t / args.steps
+    value = world * useful / per_step / 1e12
 
     achieved = useful / t_gemm / 1e12
     gather_bytes = M * K * 2 + M * kp * 2 + kp * 8       # full rows read (50% random touches every sector) + x' written
@@ -919,7 +950,7 @@ def run_ours(args, world, rank, local):
             "cpu_baseline": cpu,
             "e2e": e2e,
             "clocks": clocks,
-            "gpu_launches": (2 if args.strategy == "pregather" else 1) * args.steps,
+            "gpu_launches": (1 if args.strategy == "overlap" else 2) * args.steps,
             "step_kernels": {"step_us": round(per_step * 1e6, 2),
                              "gemm_on_gathered_operand_us": round(t_gemm * 1e6, 2),
                              "gemm_on_gathered_operand_tflops": round(useful / t_gemm / 1e12, 2),
@@ -928,7 +959,8 @@ def run_ours(args, world, rank, local):
                              "gather_alone_frac_hbm": round(gather_bytes / t_gather / 1e9 / float(peaks["hbm_gbs"]), 3),
                              "single_launch_overlap_us": round(t_ovl * 1e6, 2),
                              "one_call_at_a_time_step_us": round(t_serial * 1e6, 2),
-                             "one_call_at_a_time_tflops": round(world * useful / t_serial / 1e12, 2)},
+                             "one_call_at_a_time_tflops": round(world * useful / t_serial / 1e12, 2),
+                             "pipelined_vs_one_call_at_a_time_same_clocks": ab},
             "strategy": {"pipelined": "pipelined (ghost_linear_pipelined: each step's gather launch on a "
                                       "low-priority stream under the previous step's GEMM launch, x' "
                                       "double-buffered; every step gathers and multiplies its own batch)",
