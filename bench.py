@@ -571,12 +571,19 @@ def kernel_metrics(device, peaks) -> dict:
         assert int(cnt.item()) == kp
         mask_bytes = N * K * esz + K * 4 + kp * 8
         pack_bytes = 2 * N * kp * esz
+        # What the pack has to move at DRAM granularity: every 32-byte sector
+        # of a row that holds an alive column is read whole (50% random dead
+        # columns leave almost none untouched), and ld columns are written.
+        sectors = int(torch.unique(idx * esz // 32).numel())
+        pack_sector_bytes = N * sectors * 32 + N * ld * esz
         out[name] = {"mask_us": round(t_mask * 1e6, 2),
                      "mask_GBps": round(mask_bytes / t_mask / 1e9, 1),
                      "mask_frac_hbm": round(mask_bytes / t_mask / 1e9 / peaks["hbm_gbs"], 3),
                      "pack_us": round(t_pack * 1e6, 2),
                      "pack_GBps": round(pack_bytes / t_pack / 1e9, 1),
                      "pack_frac_hbm": round(pack_bytes / t_pack / 1e9 / peaks["hbm_gbs"], 3),
+                     "pack_touched_sector_bytes": pack_sector_bytes,
+                     "pack_frac_hbm_touched_sectors": round(pack_sector_bytes / t_pack / 1e9 / peaks["hbm_gbs"], 3),
                      "K_alive": kp, "copies_rotated": len(copies),
                      "timing": f"CUDA graph of {calls} calls over the rotated copies, per call"}
         del w, copies, wp
