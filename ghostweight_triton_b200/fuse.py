@@ -62,12 +62,18 @@ class GhostMLPChain(nn.Module):
         self.dropout = dropout
         self._plan: tuple | None = None
 
+    def refresh_packed(self) -> None:
+        """Rebuild the fused operands at the next forward: needed after in-place
+        writes through ``weight.data`` or ``bias.data``, which bypass the
+        version counters the plan is keyed on."""
+        self._plan = None
+
     def _operands(self, dtype: torch.dtype):
         fc, proj = self.fc, self.proj
         a_fc, a_proj = fc._frozen_indices, proj._frozen_indices
         key = (dtype, fc.weight.data_ptr(), fc.weight._version, proj.weight.data_ptr(),
                proj.weight._version, a_fc.data_ptr(), a_fc._version, a_proj.data_ptr(),
-               a_proj._version, None if fc.bias is None else fc.bias._version)
+               a_proj._version, None if fc.bias is None else (fc.bias.data_ptr(), fc.bias._version))
         if self._plan is not None and self._plan[0] == key:
             return self._plan[1:]
         with torch.no_grad():

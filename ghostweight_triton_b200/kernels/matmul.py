@@ -97,8 +97,10 @@ class _PackedCache:
     is used only for the very same tensor objects (held by weak reference, so
     an entry never outlives its weight) at the same in-place version counts
     (any in-place update of either tensor, or of a view sharing their storage,
-    changes them) and the same output dtype. Small LRU: at most `max_entries`
-    entries and `max_bytes` of packed data.
+    changes them), on the same storage (``w.data = ...`` keeps the object and
+    its version) and for the same output dtype. Writes through ``w.data``
+    change neither, so they need :func:`clear_packed_cache`. Small LRU: at
+    most `max_entries` entries and `max_bytes` of packed data.
     """
 
     def __init__(self, max_entries: int = 32, max_bytes: int = 2 << 30):
@@ -121,9 +123,10 @@ class _PackedCache:
         key = (id(weights), id(idx), dtype)
         e = self._entries.get(key)
         if e is not None:
-            w_ref, i_ref, w_ver, i_ver, packed, prep = e
+            w_ref, i_ref, w_ver, i_ver, packed, prep, ptrs = e
             if (w_ref() is weights and i_ref() is idx and w_ver == weights._version
-                    and i_ver == idx._version and not torch.cuda.is_current_stream_capturing()):
+                    and i_ver == idx._version and ptrs == (weights.data_ptr(), idx.data_ptr())
+                    and not torch.cuda.is_current_stream_capturing()):
                 self._entries.move_to_end(key)
                 if prep is None and prepare:
                     prep = e[5] = _native.prepare_gather_gemm(packed, idx, None, None, "auto", dtype)
@@ -138,7 +141,8 @@ class _PackedCache:
         cb = lambda _ref, key=key: self._drop(key)
         prep = _native.prepare_gather_gemm(packed, idx, None, None, "auto", dtype) if prepare else None
         self._entries[key] = [self._weakref.ref(weights, cb), self._weakref.ref(idx, cb),
-                              weights._version, idx._version, packed, prep]
+                              weights._version, idx._version, packed, prep,
+                              (weights.data_ptr(), idx.data_ptr())]
         self.bytes += nbytes
         while len(self._entries) > self.max_entries or self.bytes > self.max_bytes:
             self._drop(next(iter(self._entries)))
@@ -157,6 +161,18 @@ class _PackedCache:
 
 
 _packed_cache = _PackedCache()
+
+
+def clear_packed_cache() -> None:
+    """Forget every packed weight ghostweight_matmul keeps.
+
+    An entry is rebuilt by itself when the weight or the index list is
+    replaced, rebound to other storage (``w.data = ...``) or updated in place
+    through autograd-visible operations (optimizer steps, ``copy_`` under
+    ``no_grad``), which bump the tensor's version counter. In-place writes
+    through ``w.data`` bypass that counter; call this after them.
+    """
+    _packed_cache.clear()
 
 
 def _gemm(x, w_packed, idx, y, bias, activation, strategy):

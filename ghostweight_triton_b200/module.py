@@ -383,6 +383,18 @@ class GhostLinear(nn.Module):
         k_alive = int(self._frozen_indices.numel())
         self._last_sparsity = float(1.0 - k_alive / self.in_features)
 
+    def refresh_packed(self) -> None:
+        """Rebuild the packed weight W' at the next forward.
+
+        W' is kept between forwards and rebuilt by itself when the weight is
+        replaced, moved to other storage (``weight.data = ...``) or updated in
+        place through autograd-visible operations (optimizer steps, ``copy_``
+        under ``no_grad``), which bump its version counter. In-place writes
+        through ``weight.data`` bypass that counter; call this after them.
+        """
+        self._packed = None
+        self.__dict__["_fast"] = None
+
     def unfreeze_mask(self) -> None:
         """Switch back to dynamic per-forward masking."""
         self._mask_frozen = False

@@ -167,6 +167,7 @@ class ColumnParallelGhostLinear(nn.Module):
         self.bias = nn.Parameter(torch.zeros(self.n_local, **factory)) if bias else None
         self.alive: torch.Tensor | None = None
         self.w_packed: torch.Tensor | None = None
+        self._packed_key: tuple | None = None   # (weight, version, storage) w_packed was built from
         self.strategy = "auto"       # "runs" when the alive list is 64-column runs
         self._peer_out: PeerOutputs | None = None
         self._peer_step = 0
@@ -221,18 +222,38 @@ class ColumnParallelGhostLinear(nn.Module):
             mask, _, _ = dead_neuron_mask_compact(self.weight.detach(), self.threshold)
             union_mask(mask, self.group)
             self.alive = torch.nonzero(mask, as_tuple=False).squeeze(-1).to(torch.int64)
-            self.w_packed = pack_weight(self.weight.detach(), self.alive)
+            self._packed_key = None
+            self._packed_weight()
             # Same list on every rank, so every rank picks the same strategy.
             runs = (self.weight.dtype != torch.float32 and self.alive.numel() > 0
                     and index_runs(self.alive, self.in_features) == 0)
             self.strategy = "runs" if runs else "auto"
+
+    def _packed_weight(self) -> torch.Tensor:
+        """This shard's W' over the frozen alive list, packed again when the
+        weight was replaced, moved to other storage or updated in place through
+        autograd-visible operations (its version counter). The alive list stays
+        the frozen union, so repacking is local to the rank."""
+        w = self.weight
+        key = (w, w._version, w.data_ptr())
+        k = self._packed_key
+        if k is None or k[0] is not w or k[1:] != key[1:]:
+            with torch.no_grad():
+                self.w_packed = pack_weight(w.detach(), self.alive)
+            self._packed_key = key
+        return self.w_packed
+
+    def refresh_packed(self) -> None:
+        """Pack W' again at the next forward: needed after in-place writes
+        through ``weight.data``, which bypass the version counter."""
+        self._packed_key = None
 
     # ------------------------------------------------------------------ forward
     def local_forward(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """This rank's output columns y[:, start:start+n_local] (padded rows included)."""
         assert self.alive is not None, "call freeze_weight_mask() first"
         x2 = x.reshape(-1, self.in_features)
-        return ghost_linear(x2, self.w_packed, self.alive, bias=self.bias, out=out,
+        return ghost_linear(x2, self._packed_weight(), self.alive, bias=self.bias, out=out,
                             strategy=self.strategy)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
@@ -286,7 +307,7 @@ class ColumnParallelGhostLinear(nn.Module):
         esize = full.element_size()
         bias = self.bias[:n_real] if self.bias is not None else None
         runs = self.strategy == "runs" and x2.data_ptr() % 16 == 0 and x2.stride(0) % 8 == 0
-        _native.gather_gemm_peers(x2, self.w_packed[:n_real], self.alive,
+        _native.gather_gemm_peers(x2, self._packed_weight()[:n_real], self.alive,
                                   full[:, self.row_start:self.row_stop],
                                   po.peer_addresses(i, self.row_start * esize), bias=bias,
                                   strategy="runs" if runs else "pregather")

@@ -622,3 +622,29 @@ def test_sharded_mlp_size_bf16_rows():
     rows = torch.arange(0, M, 257, device="cuda")
     ref = (x[rows].float() @ w.float().t()).bfloat16()
     torch.testing.assert_close(y[rows], ref, **tols(torch.bfloat16))
+
+
+def test_matmul_packed_cache_follows_weight_storage():
+    """ghostweight_matmul's packed-weight cache is rebuilt when the weight is
+    rebound to other storage (same object and version), and after
+    clear_packed_cache() for in-place writes through .data."""
+    from ghostweight_triton_b200.kernels.matmul import clear_packed_cache
+
+    K, N, M = 512, 256, 64
+    g = torch.Generator(device="cuda").manual_seed(11)
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    w = (torch.randn(K, N, device="cuda", generator=g) * K ** -0.5).half()
+    idx = torch.sort(torch.randperm(K, device="cuda", generator=g)[: K // 2]).values
+
+    def check():
+        C = ghostweight_matmul(x, w, idx)
+        ref = x.float()[:, idx] @ w.float()[idx, :]
+        torch.testing.assert_close(C.float(), ref, atol=1e-2, rtol=1e-2)
+
+    check()
+    check()                                       # served from the cache
+    w.data = w.clone() * 2                        # new storage, same object and version
+    check()
+    w.data.mul_(0.5)                              # in place through .data: no version bump
+    clear_packed_cache()
+    check()

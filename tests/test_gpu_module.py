@@ -296,3 +296,35 @@ class TestEndToEnd:
         assert s["alive"] == 64 and s["dead"] == 64 and s["pct_dead"] == pytest.approx(0.5)
         log_sparsity(dead_neuron_mask(A))
         assert "64/128" in capsys.readouterr().out
+
+
+def test_packed_weight_follows_weight_updates():
+    """The frozen W' is rebuilt when the weight is rebound to other storage or
+    updated through a version-bumping in-place op, and after refresh_packed()
+    for in-place writes through .data (which bypass the version counter)."""
+    K, N, M = 512, 256, 64
+    g = torch.Generator(device="cuda").manual_seed(7)
+    gl = GhostLinear(K, N, bias=True, device="cuda", dtype=torch.float16)
+    dead = torch.randperm(K, device="cuda", generator=g)[: K // 2]
+    with torch.no_grad():
+        gl.weight.normal_(0.0, K ** -0.5, generator=g)
+        gl.weight[:, dead] = 0
+        gl.bias.normal_(0.0, 0.1, generator=g)
+    gl.freeze_weight_mask()
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+
+    def check():
+        with torch.no_grad():
+            y = gl(x)
+        ref = F.linear(x.float(), gl.weight.detach().float(), gl.bias.detach().float())
+        torch.testing.assert_close(y.float(), ref, atol=1e-2, rtol=1e-2)
+
+    check()
+    gl.weight.data = gl.weight.detach().clone() * 2          # new storage, same object and version
+    check()
+    with torch.no_grad():
+        gl.weight.mul_(0.5)                                  # version-bumping in-place update
+    check()
+    gl.weight.data.mul_(3)                                   # in place through .data: no version bump
+    gl.refresh_packed()
+    check()

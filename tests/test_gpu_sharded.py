@@ -27,3 +27,28 @@ def test_world1_matches_dense(dtype):
     x = torch.randn(M, K, device="cuda").to(dtype)
     torch.testing.assert_close(layer(x), F.linear(x.float(), w.float(), b.float()).to(dtype),
                                atol=1e-2, rtol=1e-2)
+
+
+def test_world1_repacks_after_weight_updates():
+    """W' follows the shard's weight: a version-bumping in-place update is
+    picked up by itself, a write through .data after refresh_packed()."""
+    torch.manual_seed(1)
+    N, K, M = 512, 1024, 128
+    w = (torch.randn(N, K, device="cuda") / K ** 0.5).half()
+    w[:, 256:768] = 0
+    b = torch.randn(N, device="cuda").half()
+    layer = ColumnParallelGhostLinear.from_full_weight(w, b)
+    x = torch.randn(M, K, device="cuda").half()
+
+    def check():
+        wn = layer.weight.detach()[:N].float()
+        ref = F.linear(x.float(), wn, layer.bias.detach()[:N].float())
+        torch.testing.assert_close(layer(x).float(), ref, atol=1e-2, rtol=1e-2)
+
+    check()
+    with torch.no_grad():
+        layer.weight.mul_(2)
+    check()
+    layer.weight.data.mul_(0.25)
+    layer.refresh_packed()
+    check()
